@@ -1,0 +1,161 @@
+"""Seeded synthetic DiT checkpoints in the reference's comfy_quant layout.
+
+The real Anima weights are not available here, so tests and benchmarks build a checkpoint with the
+2B MiniTrainDIT shapes (tools/reference.py:194-249): block linears N(0, 0.02) quantized with the
+ConvRot quantizers (quant.py), everything else bf16 N(0, 0.02), norm weights 1 + N(0, 0.02).
+The "mixed" precision follows the reference's asset builder: W4A8 for blocks 1..n-2, INT8 for the
+first and last block (tools/build_assets.py:118-120).
+
+Every tensor draws from its own generator seeded with (seed, crc32(name)), so any subset of a
+checkpoint can be rebuilt independently and identically on any machine (CPU generator) or on the
+same GPU model (CUDA generator).
+
+AdaLN-LoRA rank and the t_embedder widths are not fixed by the reference's source (they come from
+checkpoint shapes); these use rank 256 and 2048 -> 2048 -> 6144.
+"""
+
+from __future__ import annotations
+
+import zlib
+
+import torch
+
+from . import quant
+
+D = 2048
+HEADS = 16
+HEAD_DIM = 128
+MLP = 8192
+CTX_DIM = 1024
+ADALN_RANK = 256
+N_BLOCKS = 28
+
+QUANTIZED = ("self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj", "self_attn.output_proj",
+             "cross_attn.q_proj", "cross_attn.k_proj", "cross_attn.v_proj", "cross_attn.output_proj",
+             "mlp.layer1", "mlp.layer2")
+
+
+def block_linear_shapes() -> dict:
+    """[N, K] of every quantized linear of one block (module suffix -> shape)."""
+    return {
+        "self_attn.q_proj": (D, D), "self_attn.k_proj": (D, D), "self_attn.v_proj": (D, D),
+        "self_attn.output_proj": (D, D),
+        "cross_attn.q_proj": (D, D), "cross_attn.k_proj": (D, CTX_DIM), "cross_attn.v_proj": (D, CTX_DIM),
+        "cross_attn.output_proj": (D, D),
+        "mlp.layer1": (MLP, D), "mlp.layer2": (D, MLP),
+    }
+
+
+def _gen(seed: int, name: str, device) -> torch.Generator:
+    g = torch.Generator(device=device)
+    g.manual_seed((int(seed) * 1000003 + zlib.crc32(name.encode())) & 0x7FFFFFFFFFFF)
+    return g
+
+
+def randn(seed: int, name: str, shape, device="cpu", std: float = 1.0) -> torch.Tensor:
+    return torch.randn(shape, generator=_gen(seed, name, device), device=device, dtype=torch.float32) * std
+
+
+def block_format(fmt: str, block: int, n_blocks: int) -> str:
+    """'int8' or 'w4a8' for one block under fmt in {'int8', 'w4a8', 'mixed'}."""
+    if fmt == "int8":
+        return "int8"
+    if fmt in ("w4a8", "mixed"):
+        return "w4a8" if 0 < block < n_blocks - 1 else "int8"
+    raise ValueError(f"unknown weight format {fmt}")
+
+
+def quantized_linear(seed: int, name: str, shape, fmt: str, device="cpu", std: float = 0.02) -> dict:
+    """comfy_quant tensors for one linear, keyed by suffix ('weight', 'weight_scale', ...)."""
+    w = randn(seed, name, shape, device, std)
+    q = quant.quantize_int8_convrot(w) if fmt == "int8" else quant.quantize_w4a8(w)
+    return q
+
+
+def direct_linear(seed: int, name: str, shape, fmt: str, device="cpu", std: float = 0.02) -> dict:
+    """Quantized tensors drawn directly in the stored format, skipping the quantizer (cheap on a
+    CPU for whole 28-block checkpoints): int8 codes ~ round(N(0, 40)), per-row scales near
+    std/40; w4 codes uniform, fp8 group scales in [100, 130), FIXED_LUT codebook."""
+    n, k = shape
+    g = _gen(seed, name, device)
+    if fmt == "int8":
+        q = (torch.randn(shape, generator=g, device=device) * 40).round().clamp(-127, 127).to(torch.int8)
+        s = (std / 40) * (1 + 0.1 * torch.rand((n, 1), generator=g, device=device))
+        return {"weight": q, "weight_scale": s.float(),
+                "comfy_quant": quant.comfy_meta("int8_tensorwise", convrot=True, convrot_groupsize=quant.CONVROT_GROUP)}
+    codes = torch.randint(0, 16, (n, k), generator=g, device=device, dtype=torch.int32)
+    packed = ((codes[:, 0::2] & 0xF) | ((codes[:, 1::2] & 0xF) << 4)).to(torch.uint8).view(torch.int8)
+    s_rel = (100 + 30 * torch.rand((n, k // quant.W4_GROUP), generator=g, device=device)).to(torch.float8_e4m3fn)
+    s_ch = (std * 2.5 / 127) * (1 + 0.1 * torch.rand((n,), generator=g, device=device))
+    return {"weight": packed.contiguous(), "weight_s_rel": s_rel.contiguous(), "weight_s_channel": s_ch.float(),
+            "weight_codebook": torch.tensor(quant.FIXED_LUT, dtype=torch.float32, device=device),
+            "comfy_quant": quant.comfy_meta("asym_w4a8_int8", group_size=quant.W4_GROUP, convrot=True,
+                                            convrot_groupsize=quant.CONVROT_GROUP)}
+
+
+def block_tensors(seed: int, i: int, fmt: str = "int8", n_blocks: int = N_BLOCKS, device="cpu",
+                  direct: bool = False) -> dict:
+    """All tensors of block i, keyed by checkpoint name (without the model.diffusion_model. prefix).
+
+    direct=True draws the quantized linears in their stored format (direct_linear) instead of
+    quantizing Gaussian weights."""
+    p = f"blocks.{i}."
+    out = {}
+    bfmt = block_format(fmt, i, n_blocks)
+    make = direct_linear if direct else quantized_linear
+    for mod, shape in block_linear_shapes().items():
+        for suffix, t in make(seed, p + mod, shape, bfmt, device).items():
+            out[p + mod + "." + suffix] = t
+    for a in ("self_attn", "cross_attn"):
+        for nrm in ("q_norm", "k_norm"):
+            n = p + f"{a}.{nrm}.weight"
+            out[n] = (1 + randn(seed, n, (HEAD_DIM,), device, 0.02)).to(torch.bfloat16)
+    for m in ("adaln_modulation_self_attn", "adaln_modulation_cross_attn", "adaln_modulation_mlp"):
+        n1, n2 = p + m + ".1.weight", p + m + ".2.weight"
+        out[n1] = randn(seed, n1, (ADALN_RANK, D), device, 0.02).to(torch.bfloat16)
+        out[n2] = randn(seed, n2, (3 * D, ADALN_RANK), device, 0.02).to(torch.bfloat16)
+    return out
+
+
+def global_tensors(seed: int, device="cpu") -> dict:
+    """Non-block tensors: embedders, time conditioning, final layer."""
+    out = {}
+
+    def bf(name, shape, std=0.02):
+        out[name] = randn(seed, name, shape, device, std).to(torch.bfloat16)
+
+    bf("x_embedder.proj.1.weight", (D, 68))
+    bf("t_embedder.1.linear_1.weight", (D, D))
+    bf("t_embedder.1.linear_2.weight", (3 * D, D))
+    out["t_embedding_norm.weight"] = (1 + randn(seed, "t_embedding_norm.weight", (D,), device, 0.02)).to(torch.bfloat16)
+    bf("final_layer.adaln_modulation.1.weight", (ADALN_RANK, D))
+    bf("final_layer.adaln_modulation.2.weight", (2 * D, ADALN_RANK))
+    bf("final_layer.linear.weight", (64, D))
+    return out
+
+
+def dit_tensors(seed: int, fmt: str = "int8", n_blocks: int = N_BLOCKS, device="cpu", direct: bool = False) -> dict:
+    """A full synthetic checkpoint (n_blocks blocks) as a flat name -> tensor dict."""
+    out = global_tensors(seed, device)
+    for i in range(n_blocks):
+        out.update(block_tensors(seed, i, fmt, n_blocks, device, direct))
+    return out
+
+
+def lora_tensors(seed: int, targets, rank: int = 32, std: float = 0.01, n_blocks: int = N_BLOCKS,
+                 alpha: float | None = None) -> dict:
+    """PEFT-named LoRA (diffusion_model.<module>.lora_A/B.weight), fp32 N(0, std) A and B.
+
+    targets: module suffixes inside each block, e.g. ("self_attn.q_proj", "mlp.layer1").
+    """
+    shapes = block_linear_shapes()
+    out = {}
+    for i in range(n_blocks):
+        for t in targets:
+            N, K = shapes[t]
+            mod = f"diffusion_model.blocks.{i}.{t}"
+            out[mod + ".lora_A.weight"] = randn(seed, mod + ".A", (rank, K), "cpu", std)
+            out[mod + ".lora_B.weight"] = randn(seed, mod + ".B", (N, rank), "cpu", std)
+            if alpha is not None:
+                out[mod + ".alpha"] = torch.tensor(float(alpha))
+    return out
