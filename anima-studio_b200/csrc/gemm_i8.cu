@@ -1,0 +1,528 @@
+// tcgen05 kind::i8 GEMM with fused epilogues: the ConvRot-quantized block linears of the DiT
+// (the reference runs them as fp32 WGSL tiles that decode int8 in the loader, app/gpu/gemm.js:129-140).
+//
+//   C[m, n] = epi( a_scale[m] * w_scale[n] * (acc_hi[m, n] + acc_lo[m, n] / 254) )
+//   acc_hi = sum_k hi[m, k] * W[n, k]     acc_lo = sum_k lo[m, k] * W[n, k]     (s32 in TMEM)
+//
+// Activations are per-token int8 planes of the rotated input (x ~= s * (hi + lo / 254)); with one
+// plane (lo == NULL) this is plain W8A8. Weights are int8 [N, K] K-major, i.e. the comfy_quant
+// `weight` tensor as stored.
+//
+// Structure: persistent CTAs (one per SM), 192 threads, warp-specialised:
+//   warp 0      TMA producer: A tile(s) 128 x 128 B and W tile BN x 128 B per stage (SWIZZLE_128B)
+//   warp 1      TMEM allocator + single-thread UMMA issuer (M = 128, N = BN, K = 32 per instruction)
+//   warps 2..5  epilogue: tcgen05.ld of the accumulator rows (thread = row), fused epilogue, stores
+// Accumulators are double-buffered in TMEM when they fit (NPLANES * BN <= 256 columns) so the
+// epilogue of tile i overlaps the MMAs of tile i+1.
+
+#include "internal.h"
+#include "sm100.cuh"
+
+namespace anima {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BK = 128;      // bytes of K per stage (one SWIZZLE_128B row)
+constexpr int UMMA_K = 32;   // K per kind::i8 instruction
+constexpr int THREADS = 192;
+
+struct Params {
+  int M, N, K;
+  const float* a_scale;
+  const float* w_scale;
+  const float* bias;
+  const float* add;
+  int ld_add;
+  int act;
+  int out_mode;
+  int out_dtype;
+  void* out;
+  int ldo;
+  const float* gate;
+  int gate_off;
+  const float* norm_q;
+  const float* norm_k;
+  const float* rope;
+  int rope_rows;
+  int n_q;
+  float eps;
+  int num_m_blocks, num_k_blocks, num_tiles;
+};
+
+template <int BN, int NPLANES>
+struct Cfg {
+  static constexpr int A_BYTES = BM * BK;
+  static constexpr int B_BYTES = BN * BK;
+  static constexpr int STAGE_BYTES = NPLANES * A_BYTES + B_BYTES;
+  static constexpr int STAGES = (200 * 1024) / STAGE_BYTES;
+  static constexpr int ACC_COLS = NPLANES * BN;
+  static constexpr int ACC_BUFS = (2 * ACC_COLS <= 512) ? 2 : 1;
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
+  static_assert(STAGES >= 2, "need at least two pipeline stages");
+};
+
+// ------------------------------------------------------------------ epilogue helpers
+
+__device__ __forceinline__ float act_fn(float v, int act) {
+  if (act == ANIMA_ACT_GELU) return gelu_erf(v);
+  if (act == ANIMA_ACT_SILU) return silu_f(v);
+  return v;
+}
+
+// Load 32 accumulator columns of this thread's row and apply scale, bias, add and activation.
+template <int BN, int NPLANES>
+__device__ __forceinline__ void load_cols(const Params& p, uint32_t taddr, int col, int m, int n, bool row_ok,
+                                          float (&v)[32], bool apply_act) {
+  uint32_t rh[32];
+  tmem_ld32(taddr + col, rh);
+  if constexpr (NPLANES == 2) {
+    uint32_t rl[32];
+    tmem_ld32(taddr + BN + col, rl);
+    tmem_ld_wait();
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      v[j] = static_cast<float>(static_cast<int>(rh[j])) + static_cast<float>(static_cast<int>(rl[j])) * (1.0f / 254.0f);
+  } else {
+    tmem_ld_wait();
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = static_cast<float>(static_cast<int>(rh[j]));
+  }
+  const float as = row_ok ? __ldg(p.a_scale + m) : 0.0f;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] *= as * __ldg(p.w_scale + n + j);
+  if (p.bias) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] += __ldg(p.bias + n + j);
+  }
+  if (p.add && row_ok) {
+    const float4* a4 = reinterpret_cast<const float4*>(p.add + static_cast<size_t>(m) * p.ld_add + n);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float4 t = __ldg(a4 + j);
+      v[4 * j] += t.x;
+      v[4 * j + 1] += t.y;
+      v[4 * j + 2] += t.z;
+      v[4 * j + 3] += t.w;
+    }
+  }
+  if (apply_act && p.act != ANIMA_ACT_NONE) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = act_fn(v[j], p.act);
+  }
+}
+
+__device__ __forceinline__ void store32(void* out, int dtype, int ldo, int m, int n, const float (&v)[32]) {
+  if (dtype == ANIMA_F32) {
+    float4* o = reinterpret_cast<float4*>(static_cast<float*>(out) + static_cast<size_t>(m) * ldo + n);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+  } else if (dtype == ANIMA_BF16) {
+    uint4* o = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(out) + static_cast<size_t>(m) * ldo + n);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint4 u;
+      __nv_bfloat162 h0 = __floats2bfloat162_rn(v[8 * j], v[8 * j + 1]);
+      __nv_bfloat162 h1 = __floats2bfloat162_rn(v[8 * j + 2], v[8 * j + 3]);
+      __nv_bfloat162 h2 = __floats2bfloat162_rn(v[8 * j + 4], v[8 * j + 5]);
+      __nv_bfloat162 h3 = __floats2bfloat162_rn(v[8 * j + 6], v[8 * j + 7]);
+      u.x = *reinterpret_cast<uint32_t*>(&h0);
+      u.y = *reinterpret_cast<uint32_t*>(&h1);
+      u.z = *reinterpret_cast<uint32_t*>(&h2);
+      u.w = *reinterpret_cast<uint32_t*>(&h3);
+      o[j] = u;
+    }
+  } else {
+    uint4* o = reinterpret_cast<uint4*>(static_cast<__half*>(out) + static_cast<size_t>(m) * ldo + n);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint4 u;
+      __half2 h0 = __floats2half2_rn(v[8 * j], v[8 * j + 1]);
+      __half2 h1 = __floats2half2_rn(v[8 * j + 2], v[8 * j + 3]);
+      __half2 h2 = __floats2half2_rn(v[8 * j + 4], v[8 * j + 5]);
+      __half2 h3 = __floats2half2_rn(v[8 * j + 6], v[8 * j + 7]);
+      u.x = *reinterpret_cast<uint32_t*>(&h0);
+      u.y = *reinterpret_cast<uint32_t*>(&h1);
+      u.z = *reinterpret_cast<uint32_t*>(&h2);
+      u.w = *reinterpret_cast<uint32_t*>(&h3);
+      o[j] = u;
+    }
+  }
+}
+
+__device__ __forceinline__ void resid32(const Params& p, int m, int n, const float (&v)[32]) {
+  float4* o = reinterpret_cast<float4*>(static_cast<float*>(p.out) + static_cast<size_t>(m) * p.ldo + n);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    float4 c = o[j];
+    float g0 = 1.f, g1 = 1.f, g2 = 1.f, g3 = 1.f;
+    if (p.gate) {
+      const float* g = p.gate + p.gate_off + n + 4 * j;
+      g0 = __ldg(g);
+      g1 = __ldg(g + 1);
+      g2 = __ldg(g + 2);
+      g3 = __ldg(g + 3);
+    }
+    c.x += g0 * v[4 * j];
+    c.y += g1 * v[4 * j + 1];
+    c.z += g2 * v[4 * j + 2];
+    c.w += g3 * v[4 * j + 3];
+    o[j] = c;
+  }
+}
+
+// One tile's epilogue for this thread's row (m) over BN columns starting at n0.
+template <int BN, int NPLANES>
+__device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t taddr, int m, int n0) {
+  const bool row_ok = m < p.M;
+  if (p.out_mode == ANIMA_OUT_STORE || p.out_mode == ANIMA_OUT_RESID) {
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      float v[32];
+      load_cols<BN, NPLANES>(p, taddr, c, m, n0 + c, row_ok, v, true);
+      if (row_ok) {
+        if (p.out_mode == ANIMA_OUT_STORE)
+          store32(p.out, p.out_dtype, p.ldo, m, n0 + c, v);
+        else
+          resid32(p, m, n0 + c, v);
+      }
+    }
+    return;
+  }
+  // Per-head RMSNorm (+ split-half RoPE for q/k heads of a fused qkv projection): a head is 128
+  // consecutive columns and never straddles a tile (BN is a multiple of 128).
+#pragma unroll 1
+  for (int h0 = 0; h0 < BN; h0 += 128) {
+    const int nh = n0 + h0;
+    const bool qkv = p.out_mode == ANIMA_OUT_QKV_NORM_ROPE;
+    const bool is_q = !qkv || nh < p.n_q;
+    const bool is_k = qkv && !is_q && nh < 2 * p.n_q;
+    if (qkv && !is_q && !is_k) {  // v heads: plain store
+#pragma unroll 1
+      for (int c = 0; c < 128; c += 32) {
+        float v[32];
+        load_cols<BN, NPLANES>(p, taddr, h0 + c, m, nh + c, row_ok, v, true);
+        if (row_ok) store32(p.out, p.out_dtype, p.ldo, m, nh + c, v);
+      }
+      continue;
+    }
+    float ss = 0.f;
+#pragma unroll 1
+    for (int c = 0; c < 128; c += 32) {
+      float v[32];
+      load_cols<BN, NPLANES>(p, taddr, h0 + c, m, nh + c, row_ok, v, true);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) ss += v[j] * v[j];
+    }
+    const float rs = 1.0f / sqrtf(ss * (1.0f / 128.0f) + p.eps);
+    const float* w = is_k ? p.norm_k : p.norm_q;
+    if (qkv) {
+      const int tok = row_ok ? (m % p.rope_rows) : 0;
+      const float* cs = p.rope + static_cast<size_t>(tok) * 64;
+      const float* sn = p.rope + static_cast<size_t>(p.rope_rows) * 64 + static_cast<size_t>(tok) * 64;
+#pragma unroll 1
+      for (int c = 0; c < 64; c += 32) {
+        float v1[32], v2[32];
+        load_cols<BN, NPLANES>(p, taddr, h0 + c, m, nh + c, row_ok, v1, true);
+        load_cols<BN, NPLANES>(p, taddr, h0 + 64 + c, m, nh + 64 + c, row_ok, v2, true);
+        if (row_ok) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float y1 = v1[j] * rs * __ldg(w + c + j);
+            const float y2 = v2[j] * rs * __ldg(w + 64 + c + j);
+            const float co = __ldg(cs + c + j), si = __ldg(sn + c + j);
+            v1[j] = y1 * co - y2 * si;
+            v2[j] = y2 * co + y1 * si;
+          }
+          store32(p.out, p.out_dtype, p.ldo, m, nh + c, v1);
+          store32(p.out, p.out_dtype, p.ldo, m, nh + 64 + c, v2);
+        }
+      }
+    } else {
+#pragma unroll 1
+      for (int c = 0; c < 128; c += 32) {
+        float v[32];
+        load_cols<BN, NPLANES>(p, taddr, h0 + c, m, nh + c, row_ok, v, true);
+        if (row_ok) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = v[j] * rs * __ldg(w + c + j);
+          store32(p.out, p.out_dtype, p.ldo, m, nh + c, v);
+        }
+      }
+    }
+  }
+}
+
+// Warp-uniform bounded wait: lane 0 polls, the result is broadcast.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, unsigned err) {
+  int ok = 1;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort_flag, err) ? 1 : 0;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  return ok != 0;
+}
+
+template <int BN, int NPLANES>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_i8_kernel(const __grid_constant__ CUtensorMap tm_hi, const __grid_constant__ CUtensorMap tm_lo,
+                   const __grid_constant__ CUtensorMap tm_w, const Params p) {
+  using C = Cfg<BN, NPLANES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* acc_full = empty + C::STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);  // one arrival per epilogue warp
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_hi);
+    if (NPLANES == 2) tma_prefetch_desc(&tm_lo);
+    tma_prefetch_desc(&tm_w);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int armed_parity[C::STAGES];
+      for (int s = 0; s < C::STAGES; ++s) armed_parity[s] = -1;
+      for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+        const int mb = tile % p.num_m_blocks;
+        const int nb = tile / p.num_m_blocks;
+        for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, kErrTimeoutEmpty)) goto producer_done;
+          uint8_t* sa = smem + stage * C::STAGE_BYTES;
+          mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+          tma_load_2d(sa, &tm_hi, &full[stage], kb * BK, mb * BM);
+          if (NPLANES == 2) tma_load_2d(sa + C::A_BYTES, &tm_lo, &full[stage], kb * BK, mb * BM);
+          tma_load_2d(sa + NPLANES * C::A_BYTES, &tm_w, &full[stage], kb * BK, nb * BN);
+          armed_parity[stage] = static_cast<int>(phase);
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    producer_done:
+      if (*abort_flag) {
+        // Loads still in flight write shared memory: wait (bounded) until every armed stage landed.
+        for (int s = 0; s < C::STAGES; ++s) {
+          if (armed_parity[s] < 0) continue;
+          const unsigned long long t0 = globaltimer();
+          while (!mbar_test(smem_u32(&full[s]), static_cast<uint32_t>(armed_parity[s]))) {
+            if (globaltimer() - t0 > kWaitTimeoutNs) {
+              flag_error(kErrTimeoutDrain);
+              break;
+            }
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_i8(BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int t = 0;
+      for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++t) {
+        const int buf = t % C::ACC_BUFS;
+        const uint32_t acc_phase = (t / C::ACC_BUFS) & 1;
+        if (!mbar_wait(&acc_empty[buf], acc_phase ^ 1, abort_flag, kErrTimeoutAcc)) break;
+        tc_fence_after();
+        const uint32_t d_hi = tmem_base + buf * C::ACC_COLS;
+        const uint32_t d_lo = d_hi + BN;
+        bool aborted = false;
+        for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, kErrTimeoutFull)) {
+            aborted = true;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * C::STAGE_BYTES);
+          const uint32_t sb = sa + NPLANES * C::A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / UMMA_K; ++k) {
+            const uint64_t bdesc = sdesc_sw128(sb + k * UMMA_K, 16, 1024);
+            const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
+            umma_i8(d_hi, sdesc_sw128(sa + k * UMMA_K, 16, 1024), bdesc, idesc, acc);
+            if (NPLANES == 2) umma_i8(d_lo, sdesc_sw128(sa + C::A_BYTES + k * UMMA_K, 16, 1024), bdesc, idesc, acc);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (aborted) break;
+        umma_commit(&acc_full[buf]);
+      }
+      if (*abort_flag) {
+        // MMAs already issued complete before TMEM is released.
+        umma_commit(drain);
+        const unsigned long long t0 = globaltimer();
+        while (!mbar_test(smem_u32(drain), 0)) {
+          if (globaltimer() - t0 > kWaitTimeoutNs) {
+            flag_error(kErrTimeoutDrain);
+            break;
+          }
+        }
+      }
+    }
+  } else {
+    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row = quad * 32 + lane;
+    int t = 0;
+    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++t) {
+      const int buf = t % C::ACC_BUFS;
+      const uint32_t acc_phase = (t / C::ACC_BUFS) & 1;
+      if (!warp_wait(&acc_full[buf], acc_phase, abort_flag, kErrTimeoutAcc)) break;
+      tc_fence_after();
+      const int mb = tile % p.num_m_blocks;
+      const int nb = tile / p.num_m_blocks;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + buf * C::ACC_COLS;
+      epilogue_tile<BN, NPLANES>(p, taddr, mb * BM + row, nb * BN);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+template <int BN, int NPLANES>
+int launch(anima_ctx* ctx, const anima_qact* x, const anima_weight* W, const anima_linear_opts* o) {
+  using C = Cfg<BN, NPLANES>;
+  const int M = x->rows, N = W->N, K = W->K;
+  CUtensorMap tm_hi, tm_lo, tm_w;
+  uint64_t adims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M)};
+  uint64_t astr[1] = {static_cast<uint64_t>(x->ld)};
+  uint32_t abox[2] = {BK, BM};
+  int st = make_tmap(&tm_hi, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, x->hi, adims, astr, abox, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st) return st;
+  if (NPLANES == 2) {
+    st = make_tmap(&tm_lo, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, x->lo, adims, astr, abox, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+  } else {
+    tm_lo = tm_hi;
+  }
+  uint64_t wdims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(N)};
+  uint64_t wstr[1] = {static_cast<uint64_t>(K)};
+  uint32_t wbox[2] = {BK, BN};
+  st = make_tmap(&tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, W->data, wdims, wstr, wbox, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (st) return st;
+
+  Params p{};
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.a_scale = x->scale;
+  p.w_scale = W->scale;
+  p.bias = W->bias;
+  p.add = o->add;
+  p.ld_add = o->ld_add;
+  p.act = o->act;
+  p.out_mode = o->out_mode;
+  p.out_dtype = o->out_dtype;
+  p.out = o->out;
+  p.ldo = o->ldo;
+  p.gate = o->gate;
+  p.gate_off = o->gate_off;
+  p.norm_q = o->norm_q;
+  p.norm_k = o->norm_k;
+  p.rope = o->rope;
+  p.rope_rows = o->rope_rows;
+  p.n_q = o->n_q;
+  p.eps = o->eps > 0 ? o->eps : 1e-6f;
+  p.num_m_blocks = (M + BM - 1) / BM;
+  p.num_k_blocks = K / BK;
+  p.num_tiles = p.num_m_blocks * (N / BN);
+
+  static bool attr_set = false;
+  if (!attr_set) {
+    ANIMA_CUDA(cudaFuncSetAttribute(gemm_i8_kernel<BN, NPLANES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    C::SMEM_BYTES));
+    attr_set = true;
+  }
+  const int grid = p.num_tiles < ctx->num_sms ? p.num_tiles : ctx->num_sms;
+  ProfScope prof(ctx, NPLANES == 2 ? "linear.i8x2" : "linear.i8", 2.0 * M * N * K,
+                 static_cast<double>(M) * K * NPLANES + static_cast<double>(N) * K);
+  gemm_i8_kernel<BN, NPLANES><<<grid, THREADS, C::SMEM_BYTES, ctx->stream>>>(tm_hi, tm_lo, tm_w, p);
+  return check_launch("gemm_i8_kernel");
+}
+
+}  // namespace gemm
+}  // namespace anima
+
+using namespace anima;
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+extern "C" int anima_linear(anima_ctx* ctx, const anima_qact* x, const anima_weight* W, const anima_linear_opts* o) {
+  ANIMA_REQUIRE(ctx && x && W && o, "anima_linear: NULL argument");
+  if (W->kind == ANIMA_W_W4)
+    return set_error(ANIMA_ERR_UNSUPPORTED,
+                     "anima_linear: W4 weights are decoded once with anima_unpack_w4 and passed as kind I8");
+  ANIMA_REQUIRE(W->kind == ANIMA_W_I8, "anima_linear: weight kind %d is not a ConvRot int8 weight", W->kind);
+  ANIMA_REQUIRE(x->cols == W->K, "anima_linear: activation has %d columns, weight K is %d", x->cols, W->K);
+  ANIMA_REQUIRE(x->rows > 0 && W->N > 0, "anima_linear: empty problem (M=%d, N=%d)", x->rows, W->N);
+  ANIMA_REQUIRE(W->K % gemm::BK == 0, "anima_linear: K=%d must be a multiple of %d", W->K, gemm::BK);
+  ANIMA_REQUIRE(W->N % 128 == 0, "anima_linear: N=%d must be a multiple of 128", W->N);
+  ANIMA_REQUIRE(x->ld % 16 == 0 && x->ld >= x->cols, "anima_linear: activation ld %d must be >= K and a multiple of 16",
+                x->ld);
+  ANIMA_REQUIRE(x->hi && x->scale && W->data && W->scale && o->out, "anima_linear: missing data pointer");
+  ANIMA_REQUIRE(aligned16(x->hi) && (!x->lo || aligned16(x->lo)) && aligned16(W->data) && aligned16(o->out),
+                "anima_linear: data pointers must be 16-byte aligned");
+  const int esz = o->out_dtype == ANIMA_F32 ? 4 : 2;
+  ANIMA_REQUIRE(o->out_dtype == ANIMA_F32 || o->out_dtype == ANIMA_BF16 || o->out_dtype == ANIMA_F16,
+                "anima_linear: out_dtype %d unsupported", o->out_dtype);
+  ANIMA_REQUIRE((static_cast<long long>(o->ldo) * esz) % 16 == 0 && o->ldo >= W->N,
+                "anima_linear: ldo %d must be >= N and 16-byte aligned", o->ldo);
+  ANIMA_REQUIRE(o->out_mode >= ANIMA_OUT_STORE && o->out_mode <= ANIMA_OUT_HEAD_NORM, "anima_linear: bad out_mode %d",
+                o->out_mode);
+  ANIMA_REQUIRE(o->out_mode != ANIMA_OUT_RESID || o->out_dtype == ANIMA_F32,
+                "anima_linear: the residual output is fp32 (the reference's residual stream)");
+  ANIMA_REQUIRE(!o->add || (aligned16(o->add) && o->ld_add % 4 == 0 && o->ld_add >= W->N),
+                "anima_linear: add must be 16-byte aligned with ld_add >= N, multiple of 4");
+  if (o->out_mode == ANIMA_OUT_QKV_NORM_ROPE) {
+    ANIMA_REQUIRE(o->norm_q && o->norm_k && o->rope && o->rope_rows > 0, "anima_linear: qkv epilogue needs norms and rope");
+    ANIMA_REQUIRE(o->n_q % 128 == 0 && 2 * o->n_q <= W->N, "anima_linear: bad n_q %d", o->n_q);
+  }
+  if (o->out_mode == ANIMA_OUT_HEAD_NORM) ANIMA_REQUIRE(o->norm_q, "anima_linear: head-norm epilogue needs norm_q");
+  const bool two = x->lo != nullptr;
+  if (W->N % 256 == 0) {
+    return two ? gemm::launch<256, 2>(ctx, x, W, o) : gemm::launch<256, 1>(ctx, x, W, o);
+  }
+  return two ? gemm::launch<128, 2>(ctx, x, W, o) : gemm::launch<128, 1>(ctx, x, W, o);
+}

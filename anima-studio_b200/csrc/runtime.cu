@@ -1,0 +1,251 @@
+// Context, errors, memory, tensor maps and the per-op profiler of libanima_b200
+// (the role of the reference's GPU class, app/gpu/device.js:59-232).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "internal.h"
+#include "sm100.cuh"
+
+namespace anima {
+
+static thread_local std::string t_last_error;
+
+int set_error(int status, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_last_error = buf;
+  return status;
+}
+
+int check_cuda(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return ANIMA_OK;
+  return set_error(ANIMA_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) return ANIMA_OK;
+  return set_error(ANIMA_ERR_CUDA, "launch of %s failed: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+int make_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base, const uint64_t* dims,
+              const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swizzle) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return set_error(ANIMA_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0)
+    return set_error(ANIMA_ERR_ARG, "TMA base address %p is not 16-byte aligned", base);
+  for (int i = 1; i < rank; ++i)
+    if (strides_bytes[i - 1] % 16 != 0)
+      return set_error(ANIMA_ERR_ARG, "TMA stride %llu bytes is not a multiple of 16",
+                       (unsigned long long)strides_bytes[i - 1]);
+  cuuint64_t d[5];
+  cuuint64_t s[4];
+  cuuint32_t b[5], e[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    e[i] = 1;
+  }
+  for (int i = 0; i < rank - 1; ++i) s[i] = strides_bytes[i];
+  CUresult r = fn(map, dtype, rank, const_cast<void*>(base), d, s, b, e, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(ANIMA_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", (int)r);
+  return ANIMA_OK;
+}
+
+// ------------------------------------------------------------------ profiler
+
+struct ProfEntry {
+  double ms = 0, flops = 0, bytes = 0;
+  long calls = 0;
+};
+struct PendingEvent {
+  std::string name;
+  double flops, bytes;
+  cudaEvent_t e0, e1;
+};
+struct ProfileState {
+  std::map<std::string, ProfEntry> table;
+  std::vector<PendingEvent> pending;
+};
+
+static void prof_collect(anima_ctx* ctx) {
+  auto* st = static_cast<ProfileState*>(ctx->prof);
+  if (!st) return;
+  for (auto& p : st->pending) {
+    float ms = 0;
+    cudaEventSynchronize(p.e1);
+    cudaEventElapsedTime(&ms, p.e0, p.e1);
+    auto& e = st->table[p.name];
+    e.ms += ms;
+    e.flops += p.flops;
+    e.bytes += p.bytes;
+    e.calls += 1;
+    cudaEventDestroy(p.e0);
+    cudaEventDestroy(p.e1);
+  }
+  st->pending.clear();
+}
+
+ProfScope::ProfScope(anima_ctx* c, const char* n, double f, double b) : ctx(c), name(n), flops(f), bytes(b) {
+  if (!ctx || !ctx->profile) return;
+  cudaEventCreate(&e0);
+  cudaEventCreate(&e1);
+  cudaEventRecord(e0, ctx->stream);
+}
+
+ProfScope::~ProfScope() {
+  if (!e0) return;
+  cudaEventRecord(e1, ctx->stream);
+  static_cast<ProfileState*>(ctx->prof)->pending.push_back({name, flops, bytes, e0, e1});
+}
+
+}  // namespace anima
+
+using namespace anima;
+
+extern "C" {
+
+int anima_version(void) { return 1; }
+
+const char* anima_last_error(void) { return t_last_error.c_str(); }
+
+int anima_ctx_create(int device, anima_ctx** out) {
+  ANIMA_REQUIRE(out != nullptr, "anima_ctx_create: out is NULL");
+  int n = 0;
+  ANIMA_CUDA(cudaGetDeviceCount(&n));
+  ANIMA_REQUIRE(device >= 0 && device < n, "anima_ctx_create: device %d out of range (%d devices)", device, n);
+  ANIMA_CUDA(cudaSetDevice(device));
+  cudaDeviceProp prop;
+  ANIMA_CUDA(cudaGetDeviceProperties(&prop, device));
+  if (prop.major != 10)
+    return set_error(ANIMA_ERR_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a (B200)", device,
+                     prop.major, prop.minor);
+  auto* c = new anima_ctx();
+  c->device = device;
+  c->num_sms = prop.multiProcessorCount;
+  const char* p = getenv("ANIMA_PROFILE");
+  c->profile = p && p[0] == '1';
+  if (c->profile) c->prof = new ProfileState();
+  *out = c;
+  return ANIMA_OK;
+}
+
+int anima_ctx_destroy(anima_ctx* ctx) {
+  if (!ctx) return ANIMA_OK;
+  if (ctx->prof) {
+    prof_collect(ctx);
+    delete static_cast<ProfileState*>(ctx->prof);
+  }
+  delete ctx;
+  return ANIMA_OK;
+}
+
+int anima_ctx_set_stream(anima_ctx* ctx, void* stream) {
+  ANIMA_REQUIRE(ctx, "anima_ctx_set_stream: ctx is NULL");
+  ctx->stream = static_cast<cudaStream_t>(stream);
+  return ANIMA_OK;
+}
+
+int anima_sync(anima_ctx* ctx) {
+  ANIMA_REQUIRE(ctx, "anima_sync: ctx is NULL");
+  ANIMA_CUDA(cudaStreamSynchronize(ctx->stream));
+  unsigned err = 0, zero = 0;
+  ANIMA_CUDA(cudaMemcpyFromSymbol(&err, g_device_error, sizeof(err)));
+  if (err) {
+    ANIMA_CUDA(cudaMemcpyToSymbol(g_device_error, &zero, sizeof(zero)));
+    return set_error(ANIMA_ERR_DEVICE, "device error flags 0x%x (%s%s%s%s%s)", err,
+                     (err & kErrTimeoutFull) ? "data wait timed out; " : "",
+                     (err & kErrTimeoutEmpty) ? "stage wait timed out; " : "",
+                     (err & kErrTimeoutAcc) ? "accumulator wait timed out; " : "",
+                     (err & kErrTimeoutDrain) ? "drain after abort timed out; " : "",
+                     (err & kErrBadArgs) ? "kernel rejected its arguments; " : "");
+  }
+  if (ctx->profile) prof_collect(ctx);
+  return ANIMA_OK;
+}
+
+int anima_alloc(anima_ctx* ctx, size_t bytes, void** out) {
+  ANIMA_REQUIRE(ctx && out, "anima_alloc: NULL argument");
+  ANIMA_CUDA(cudaMallocAsync(out, bytes ? bytes : 16, ctx->stream));
+  return ANIMA_OK;
+}
+
+int anima_free(anima_ctx* ctx, void* ptr) {
+  ANIMA_REQUIRE(ctx, "anima_free: ctx is NULL");
+  if (ptr) ANIMA_CUDA(cudaFreeAsync(ptr, ctx->stream));
+  return ANIMA_OK;
+}
+
+int anima_upload(anima_ctx* ctx, void* dst, const void* src, size_t bytes) {
+  ANIMA_REQUIRE(ctx && dst && src, "anima_upload: NULL argument");
+  ANIMA_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, ctx->stream));
+  return ANIMA_OK;
+}
+
+int anima_download(anima_ctx* ctx, void* dst, const void* src, size_t bytes) {
+  ANIMA_REQUIRE(ctx && dst && src, "anima_download: NULL argument");
+  ANIMA_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, ctx->stream));
+  return ANIMA_OK;
+}
+
+int anima_zero(anima_ctx* ctx, void* p, size_t bytes) {
+  ANIMA_REQUIRE(ctx && p, "anima_zero: NULL argument");
+  ANIMA_CUDA(cudaMemsetAsync(p, 0, bytes, ctx->stream));
+  return ANIMA_OK;
+}
+
+int anima_profile_report(anima_ctx* ctx, char* buf, size_t cap) {
+  ANIMA_REQUIRE(ctx && buf && cap > 0, "anima_profile_report: NULL argument");
+  std::string s;
+  if (!ctx->profile) {
+    s = "profiling disabled (set ANIMA_PROFILE=1 before creating the context)\n";
+  } else {
+    ANIMA_CUDA(cudaStreamSynchronize(ctx->stream));
+    prof_collect(ctx);
+    auto* st = static_cast<ProfileState*>(ctx->prof);
+    char line[256];
+    snprintf(line, sizeof(line), "%-28s %8s %12s %12s %10s\n", "op", "calls", "total ms", "TFLOP/s", "GB/s");
+    s += line;
+    for (auto& kv : st->table) {
+      const ProfEntry& e = kv.second;
+      double sec = e.ms * 1e-3;
+      snprintf(line, sizeof(line), "%-28s %8ld %12.3f %12.1f %10.1f\n", kv.first.c_str(), e.calls, e.ms,
+               sec > 0 ? e.flops / sec * 1e-12 : 0.0, sec > 0 ? e.bytes / sec * 1e-9 : 0.0);
+      s += line;
+    }
+  }
+  size_t n = s.size() < cap - 1 ? s.size() : cap - 1;
+  memcpy(buf, s.data(), n);
+  buf[n] = 0;
+  return ANIMA_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,196 @@
+"""LoRA side paths on (possibly quantized) linears, without touching the base weights (app/lora.js).
+
+y = W x + sum_e scale_e * B_e (A_e x), evaluated next to the int8 GEMM and added in its epilogue
+before the activation (ops.js:55-57, 70-87). ConvRot layers receive rotated inputs x_r = x H and
+x A^T = x_r (A H)^T, so A is rotated once at load (lora.js:67-84, 103-134). scale = strength *
+alpha / r, or strength without an alpha (lora.js:141-149; tools/reference.py:78).
+
+File naming: PEFT ("<prefix><module>.lora_A/B.weight") or kohya ("lora_unet_<module_with_
+underscores>.lora_down/up.weight" + ".alpha"); LoKr/LoHa/DoRA tensors are counted as unsupported.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import re
+from dataclasses import dataclass
+
+import torch
+
+from . import device as dev
+from . import quant
+from .device import ctx_for, ptr
+
+SUFFIXES = [(".lora_A.weight", "A"), (".lora_B.weight", "B"), (".lora_down.weight", "A"),
+            (".lora_up.weight", "B"), (".alpha", "alpha")]
+TE_PREFIXES = ["lora_te_", "lora_te1_", "text_encoder.", "text_encoders.qwen3_06b.transformer.", "te."]
+DIT_PREFIXES = ["lora_unet_", "model.diffusion_model.", "diffusion_model.", "base_model.model.", "transformer.",
+                "unet."]
+UNSUPPORTED = re.compile(r"(lokr_|hada_|\.dora_scale|\.diff$|\.diff_b$|\.w_norm|\.b_norm)")
+
+
+def norm_name(name: str) -> str:
+    return name.replace(".", "_")
+
+
+def hadamard_rows(a: torch.Tensor) -> torch.Tensor:
+    """A H per 256-feature group of every row (lora.js:67-84): the rotation ConvRot inputs get."""
+    return quant.rotate(a.float())
+
+
+def linear_registry(model) -> dict:
+    """normalized module name -> (Linear, off, n) for every linear of a model (lora.js:48-65)."""
+    from .weights import Linear
+
+    reg = {}
+    seen = set()
+
+    def walk(o):
+        if id(o) in seen or o is None or isinstance(o, (torch.Tensor, str, int, float)):
+            return
+        seen.add(id(o))
+        if isinstance(o, Linear):
+            if o.parts:
+                for name, off, n in o.parts:
+                    reg[norm_name(name)] = (o, off, n)
+            elif o.name:
+                reg[norm_name(o.name)] = (o, 0, o.N)
+            return
+        if isinstance(o, dict):
+            for v in o.values():
+                walk(v)
+        elif isinstance(o, (list, tuple)):
+            for v in o:
+                walk(v)
+        elif hasattr(o, "__dict__"):
+            for v in vars(o).values():
+                walk(v)
+
+    walk(model)
+    return reg
+
+
+def find_target(module: str, dit_reg: dict, te_reg: dict | None = None):
+    """Strip a known prefix and look the module up (lora.js:89-102)."""
+    te = False
+    name = module
+    for p in TE_PREFIXES:
+        if name.startswith(p):
+            name, te = name[len(p):], True
+            break
+    if not te:
+        for p in DIT_PREFIXES:
+            if name.startswith(p):
+                name = name[len(p):]
+                break
+    key = norm_name(name)
+    for reg in ([te_reg] if te else [dit_reg, te_reg]):
+        if not reg:
+            continue
+        if key in reg:
+            return reg[key]
+        if "model_" + key in reg:
+            return reg["model_" + key]
+    return None
+
+
+@dataclass
+class LoraModule:
+    target: tuple       # (Linear, off, n)
+    A: torch.Tensor     # [r, K] fp32 on the device, rotated for ConvRot targets
+    B: torch.Tensor     # [n, r] fp32 on the device
+    r: int
+    alpha_scale: float
+
+
+@dataclass
+class Lora:
+    modules: list
+    matched: int
+    total: int
+    unsupported: int
+    skipped: int
+
+
+def load_lora(tensors: dict, dit_reg: dict, te_reg: dict | None = None, device="cuda") -> Lora:
+    """Group a LoRA file's tensors by module, match them to linears and upload them (lora.js:103-134)."""
+    groups: dict = {}
+    unsupported = 0
+    for key in tensors:
+        if UNSUPPORTED.search(key):
+            unsupported += 1
+            continue
+        for suf, role in SUFFIXES:
+            if key.endswith(suf):
+                groups.setdefault(key[: -len(suf)], {})[role] = key
+                break
+    modules = []
+    skipped = 0
+    for module, keys in groups.items():
+        if "A" not in keys or "B" not in keys:
+            skipped += 1
+            continue
+        target = find_target(module, dit_reg, te_reg)
+        A = tensors[keys["A"]].float()
+        B = tensors[keys["B"]].float()
+        r = A.shape[0]
+        if target is None or A.shape[1] != target[0].K or B.shape[0] != target[2] or B.shape[1] != r:
+            skipped += 1
+            continue
+        if target[0].quantized:
+            A = hadamard_rows(A)
+        alpha = float(tensors[keys["alpha"]].float().reshape(-1)[0]) if "alpha" in keys else None
+        modules.append(LoraModule(target, A.to(device).contiguous(), B.to(device).contiguous(), r,
+                                  alpha / r if alpha else 1.0))
+    return Lora(modules, len(modules), len(groups), unsupported, skipped)
+
+
+def attach_loras(registries, active):
+    """Replace every side path with [(lora, strength)] (lora.js:141-149)."""
+    for reg in registries:
+        if reg:
+            for (W, _, _) in reg.values():
+                W.lora = []
+    for lora, strength in active:
+        if not strength:
+            continue
+        for m in lora.modules:
+            W, off, n = m.target
+            W.lora.append({"A": m.A, "B": m.B, "r": m.r, "scale": strength * m.alpha_scale, "off": off, "n": n})
+    for reg in registries:
+        if reg:
+            for (W, _, _) in reg.values():
+                W._lora_cat = None
+
+
+def _cat_A(W):
+    """All entries' A stacked [sum r, K] (cached per attach)."""
+    cat = getattr(W, "_lora_cat", None)
+    if cat is None:
+        cat = torch.cat([e["A"] for e in W.lora], 0).contiguous()
+        W._lora_cat = cat
+    return cat
+
+
+def lora_delta(x, W) -> torch.Tensor:
+    """[M, N] fp32 low-rank update for quantized rows x (ops.js:70-87): T = x_r A^T for all entries
+    at once, then each entry's B into its column slice, scaled."""
+    M = x.rows
+    A = _cat_A(W)
+    R = A.shape[0]
+    ctx = ctx_for(x.hi)
+    T = torch.empty(M, R, dtype=torch.float32, device=x.hi.device)
+    qa = x.c()
+    ctx.call("anima_lora_down", C.byref(qa), ptr(A), R, ptr(T), R)
+    D = torch.empty(M, W.N, dtype=torch.float32, device=x.hi.device)
+    ctx.call("anima_zero", ptr(D), D.numel() * 4)
+    r0 = 0
+    for e in W.lora:
+        wb = dev.Weight()
+        wb.kind, wb.N, wb.K, wb.data = dev.W_F32, e["n"], e["r"], e["B"].data_ptr()
+        Cp = C.c_void_p(D.data_ptr() + 4 * e["off"])
+        Tp = C.c_void_p(T.data_ptr() + 4 * r0)
+        ctx.call("anima_matmul", M, e["n"], e["r"], C.c_float(e["scale"]), Tp, R, C.byref(wb), 0, Cp, W.N, 1,
+                 C.c_void_p(0), 0)
+        r0 += e["r"]
+    return D

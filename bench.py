@@ -1,0 +1,373 @@
+"""Benchmark: DiT denoise steps/s at 1024^2 (4096 tokens) on 1..8 B200.
+
+A step is one denoising step of the Turbo configuration: one 28-block INT8-ConvRot DiT forward at
+1024x1024 (latent 16x128x128, L = 4096 tokens) plus the Euler update, batch 1, no CFG, the text
+context a seeded 256x1024 N(0,1) block zero-padded to 512 rows as the reference does. Weights are
+synthetic (N(0, 0.02) quantized with the reference's ConvRot int8 quantizer); inputs seeded.
+
+  python bench.py [--gpus N --steps K --warmup W]           this implementation
+  python bench.py --impl reference [...]                    the reference's algorithm on the CPU
+
+Multi-GPU: one process per GPU (torchrun), each rank denoises its own image (data parallel, no
+collective on the data path); the reported value is the whole job's steps/s, timed on the device
+as the max over ranks.
+"""
+
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "DiT denoise steps/sec at 1024^2 (4096 tokens), 28-block INT8 ConvRot DiT"
+WORKLOAD = ("BASELINE configs[2]: Turbo DiT, 28 blocks, INT8 ConvRot weights, 1024x1024 (latent 16x128x128, "
+            "4096 tokens), batch 1 per GPU, Euler steps, no CFG, context 256x1024 zero-padded to 512 rows")
+
+
+def pkg(sub):
+    return importlib.import_module("anima-studio_b200." + sub)
+
+
+def load_peaks():
+    try:
+        return json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except (OSError, ValueError):
+        return {}
+
+
+def traffic_from_profile():
+    """Per-launch DRAM bytes of the mlp1 GEMM from the committed ncu summary, if present."""
+    p = os.path.join(ROOT, "profiles", "gemm_i8_mlp1_L4096.md")
+    try:
+        m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", open(p).read())
+        return float(m.group(1)) if m else None
+    except OSError:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples while the timed region runs."""
+
+    def __init__(self, index: int):
+        self.path = os.path.join("/tmp", f"anima_clocks_{os.getpid()}.csv")
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.f = open(self.path, "w")
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(index), f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                       "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.p.kill()
+        self.f.close()
+        rows = [r.split(", ") for r in open(self.path).read().strip().splitlines() if r.count(",") >= 8]
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows]
+        reasons = set()
+        for r in rows:
+            for name, v in zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"), r[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(rows[0][2]), "samples": len(rows),
+                "power_w_max": max(float(r[3]) for r in rows), "reasons": sorted(reasons)}
+
+
+def setup_dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+# ----------------------------------------------------------------------------- reference arm (CPU)
+
+def run_reference(args, world, rank):
+    """The reference's algorithm (tools/reference.py, restated in numpy as oracle/) on the host
+    cores: each step is a bounded sample — one of the 28 blocks at L = 4096 — scaled to a full
+    denoising step (28 blocks)."""
+    if rank != 0:
+        return
+    import torch
+
+    import oracle
+    from oracle import to_numpy as to_np
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    syn = pkg("synthetic")
+    seed, Hp = 1234, 64
+    L = Hp * Hp
+    t = to_np(syn.global_tensors(seed))
+    t.update(to_np(syn.block_tensors(seed, 0, "int8", 28, direct=True)))
+    W = oracle.DequantWeights(t)
+    ctx = np.concatenate([syn.randn(seed, "ctx", (256, 1024)).numpy(), np.zeros((256, 1024), np.float32)])
+    x = syn.randn(seed, "x", (L, 2048)).numpy()
+    _, adaln_lora, emb = oracle.time_cond(W, 0.9)
+    cos, sin = oracle.dit_rope(Hp, Hp)
+    cos, sin = np.concatenate([cos, cos], -1), np.concatenate([sin, sin], -1)
+    times = []
+    for i in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        oracle.dit_block(W, 0, x, ctx, emb, adaln_lora, cos, sin)
+        times.append(time.perf_counter() - t0)
+    block_s = statistics.mean(times[args.warmup:])
+    step_s = block_s * 28
+    v = 1.0 / step_s
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "steps/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "tokens": L, "blocks": 28},
+            "cpu_baseline": {"value": v, "unit": "steps/s", "cores": cores, "kind": "port",
+                             "sample": f"one DiT block at L=4096 per step ({block_s:.2f} s), x28 blocks; numpy "
+                                       "restatement of tools/reference.py (fp32, BLAS threads = cores)"},
+            "e2e": {"value": v, "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- this implementation
+
+def cpu_baseline_sample(seconds_budget=25.0):
+    """The oracle port timed on the host cores on a bounded sample (one block at L=4096)."""
+    import torch
+
+    import oracle
+    from oracle import to_numpy as to_np
+
+    cores = os.cpu_count() or 1
+    syn = pkg("synthetic")
+    seed, Hp = 1234, 64
+    t = to_np(syn.global_tensors(seed))
+    t.update(to_np(syn.block_tensors(seed, 0, "int8", 28, direct=True)))
+    W = oracle.DequantWeights(t)
+    ctx = np.concatenate([syn.randn(seed, "ctx", (256, 1024)).numpy(), np.zeros((256, 1024), np.float32)])
+    x = syn.randn(seed, "x", (Hp * Hp, 2048)).numpy()
+    _, adaln_lora, emb = oracle.time_cond(W, 0.9)
+    cos, sin = oracle.dit_rope(Hp, Hp)
+    cos, sin = np.concatenate([cos, cos], -1), np.concatenate([sin, sin], -1)
+    oracle.dit_block(W, 0, x, ctx, emb, adaln_lora, cos, sin)  # warm (dequantized weights cached)
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        oracle.dit_block(W, 0, x, ctx, emb, adaln_lora, cos, sin)
+        n += 1
+        if time.perf_counter() - t0 > seconds_budget / 2 or n >= 3:
+            break
+    block_s = (time.perf_counter() - t0) / n
+    return {"value": 1.0 / (28 * block_s), "unit": "steps/s", "cores": cores, "kind": "port",
+            "sample": f"{n} x one DiT block at L=4096 ({block_s:.2f} s each), x28 blocks per step; numpy restatement "
+                      "of tools/reference.py, fp32, BLAS on all host cores"}
+
+
+def measure_int8_peak(torch):
+    """Dense int8 tensor-core throughput of cuBLASLt (torch._int_mm, 8192^3), as the int8
+    roofline denominator (MEASURED_PEAKS.json has only bf16)."""
+    n = 8192
+    a = torch.randint(-127, 127, (n, n), dtype=torch.int8, device="cuda")
+    b = torch.randint(-127, 127, (n, n), dtype=torch.int8, device="cuda")
+    for _ in range(3):
+        torch._int_mm(a, b)
+    torch.cuda.synchronize()
+    best = 1e9
+    for _ in range(10):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        torch._int_mm(a, b)
+        e1.record()
+        e1.synchronize()
+        best = min(best, e0.elapsed_time(e1))
+    del a, b
+    return 2.0 * n ** 3 / (best * 1e-3) / 1e12
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=16)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="anima", choices=["anima", "reference"])
+    ap.add_argument("--precision", default="a16", choices=["a16", "a8"])
+    ap.add_argument("--attn", default="f16", choices=["bf16", "f16"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    world, rank, local = setup_dist()
+    if args.impl == "reference":
+        return run_reference(args, world, rank)
+
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    dev = pkg("device")
+    syn, ditm, ops, pl = pkg("synthetic"), pkg("dit"), pkg("ops"), pkg("pipeline")
+
+    cpu_base = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu_base = cpu_baseline_sample()  # before any CUDA work (keeps BLAS threads off the GPU feeder)
+
+    seed = 1234
+    tensors = syn.dit_tensors(seed, "int8", 28, device="cuda")
+    dit = ditm.AnimaDiT(tensors, "cuda", precision=args.precision,
+                        attn_dtype=torch.bfloat16 if args.attn == "bf16" else torch.float16)
+    del tensors
+    torch.cuda.empty_cache()
+    ctx = torch.cat([syn.randn(seed, "ctx", (256, 1024)), torch.zeros(256, 1024)]).cuda()
+    cond = dit.prepare_context(ctx)
+    sig = pl.sigmas_simple(8, 3.0)
+    tcs = dit.time_cond_batch(sig[:-1])
+    noise = syn.randn(seed + rank, "noise", (1, 16, 128, 128)).cuda()
+    x = noise * sig[0]
+
+    def step(i):
+        j = i % 8
+        v = dit.forward(x, cond, tcs[j])
+        ops.euler_step(x, v, sig[j], sig[j + 1])
+        if j == 7:  # next image: restart from the noise
+            x.copy_(noise * sig[0])
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    barrier()
+    clocks = ClockSampler(local)
+    launches0 = dev.Context.launches
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        step(args.warmup + i)
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    launches = dev.Context.launches - launches0
+    ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms], device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    value = world * args.steps / (ms_max * 1e-3)
+
+    # Per-kernel durations: an instrumented replay of the same steps (CUDA events around each
+    # launch on the launching stream), for the roofline of the dominant kernel.
+    with dev.KernelTimer({"anima_linear", "anima_attention"}) as kt:
+        for i in range(min(args.steps, 8)):
+            step(args.warmup + args.steps + i)
+    summ = kt.summary()
+    replay_steps = min(args.steps, 8)
+
+    # e2e through the public step API with host buffers: each step uploads the latent from pinned
+    # host memory, runs the DiT and the Euler update, and reads the new latent back.
+    e2e = None
+    if not args.no_e2e:
+        xh = torch.empty(1, 16, 128, 128, pin_memory=True)
+        xh.copy_(x.cpu())
+        xd = torch.empty_like(x)
+        for i in range(2):
+            xd.copy_(xh, non_blocking=True)
+            v = dit.forward(xd, cond, tcs[i])
+            ops.euler_step(xd, v, sig[i], sig[i + 1])
+            xh.copy_(xd, non_blocking=True)
+        torch.cuda.synchronize()
+        barrier()
+        t0 = time.perf_counter()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record()
+        for i in range(args.steps):
+            j = i % 8
+            xd.copy_(xh, non_blocking=True)
+            tc = dit.time_cond(sig[j])
+            v = dit.forward(xd, cond, tc)
+            ops.euler_step(xd, v, sig[j], sig[j + 1])
+            xh.copy_(xd, non_blocking=True)
+        f1.record()
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t0
+        barrier()
+        et = torch.tensor([max(f0.elapsed_time(f1), wall * 1e3)], device="cuda")
+        if world > 1:
+            dist.all_reduce(et, op=dist.ReduceOp.MAX)
+        nbytes = xh.numel() * 4
+        e2e = {"value": world * args.steps / (float(et.item()) * 1e-3), "unit": "steps/s",
+               "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes,
+               "api": "per step: pinned host latent -> device, time_cond(sigma), AnimaDiT.forward, "
+                      "euler_step, latent -> pinned host (the reference's per-pass host round trip, dit.js:256,322)"}
+
+    peaks = load_peaks()
+    int8_peak = measure_int8_peak(torch) if rank == 0 else None
+    dist.destroy_process_group() if world > 1 else None
+    if rank != 0:
+        return
+
+    # roofline of the dominant kernel: the int8 GEMM over all its launches in a step, and the
+    # north star's 2048->8192 linear (mlp1) alone
+    lin = {k: v for k, v in summ.items() if k[0] == "anima_linear"}
+    lin_n = sum(v[0] for v in lin.values())
+    lin_ms = sum(v[1] for v in lin.values())
+    lin_work = sum(v[2] for v in lin.values())
+    att = {k: v for k, v in summ.items() if k[0] == "anima_attention"}
+    att_ms = sum(v[1] for v in att.values())
+    att_work = sum(v[2] for v in att.values())
+    mlp1 = summ.get(("anima_linear", "dit.mlp1"), (1, 0.0, 0.0))
+    step_ms_replay = None
+    planes = 2 if args.precision == "a16" else 1
+    achieved = lin_work / (lin_ms * 1e-3) / 1e12 if lin_ms else 0.0
+    traffic = traffic_from_profile()
+    roof = {"kernel": "gemm_i8_kernel (all block linears)", "bound": "tensor", "achieved": achieved,
+            "peak": int8_peak, "unit": "TOPS", "frac": achieved / int8_peak if int8_peak else None,
+            "peak_source": "measured: cuBLASLt int8 GEMM 8192^3 (torch._int_mm) on this GPU",
+            "traffic": traffic,
+            "hw_ops_frac": planes * achieved / int8_peak if int8_peak else None,
+            "launches_per_step": lin_n / replay_steps, "ms_per_step": lin_ms / replay_steps,
+            "mlp1": {"shape": "4096x8192x2048 (+GELU)", "ms": mlp1[1] / max(mlp1[0], 1),
+                     "achieved_tops": mlp1[2] / max(mlp1[0], 1) / (mlp1[1] / max(mlp1[0], 1) * 1e-3) / 1e12
+                     if mlp1[1] else None},
+            "attention": {"ms_per_step": att_ms / replay_steps,
+                          "achieved_tflops": att_work / (att_ms * 1e-3) / 1e12 if att_ms else None,
+                          "peak_bf16_tflops": peaks.get("bf16_tflops"),
+                          "frac": (att_work / (att_ms * 1e-3) / 1e12) / peaks["bf16_tflops"]
+                          if att_ms and peaks.get("bf16_tflops") else None},
+            "note": "achieved = algorithmic 2MNK ops / CUDA-event time per launch (instrumented replay); "
+                    "a16 runs two int8 MMAs per product, so hw_ops_frac = planes x frac"}
+    line = {"metric": METRIC, "value": value, "unit": "steps/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "tokens": 4096, "blocks": 28, "batch_per_gpu": 1,
+                       "precision": args.precision, "attention": args.attn, "ctx_rows": 512,
+                       "parallelism": f"dp{world}", "images_per_s": value / 8,
+                       "l2": "inputs larger than L2: 1.5 GB of int8 weights stream through every step"},
+            "roofline": roof, "cpu_baseline": cpu_base, "e2e": e2e,
+            "gpu_launches": launches, "gpu_launches_per_step": launches / args.steps, "clocks": clk}
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

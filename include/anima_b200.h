@@ -1,0 +1,195 @@
+/*
+ * anima_b200.h — C ABI of the B200 (sm_100a) backend for the Anima DiT denoising path.
+ *
+ * It replaces the WebGPU operator surface of the reference (app/gpu/ops.js + app/gpu/device.js)
+ * for the DiT forward (app/models/dit.js:196-325). Each entry point below names the reference
+ * interface it stands in for. Conventions:
+ *   - Every call returns an anima_status; 0 is success. anima_last_error() gives the message of
+ *     the calling thread's last failure. No exceptions cross the ABI.
+ *   - All pointers are device pointers unless stated; sizes and strides are in elements.
+ *   - Calls are asynchronous on the context's stream (like the reference's recorded dispatches,
+ *     app/gpu/device.js:170-216); device-side faults and timeouts surface at anima_sync(), as the
+ *     reference surfaces WebGPU validation errors at read/sync (device.js:224-231).
+ *   - A context is owned by one host thread at a time (the reference's single worker thread).
+ */
+#ifndef ANIMA_B200_H
+#define ANIMA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct anima_ctx anima_ctx;
+
+typedef enum {
+  ANIMA_OK = 0,
+  ANIMA_ERR_ARG = 1,          /* bad shape, stride, alignment or enum value */
+  ANIMA_ERR_CUDA = 2,         /* a CUDA runtime/driver call failed */
+  ANIMA_ERR_DEVICE = 3,       /* a kernel reported a fault or a timed-out wait */
+  ANIMA_ERR_UNSUPPORTED = 4,  /* valid request this build does not implement */
+} anima_status;
+
+typedef enum { ANIMA_F32 = 0, ANIMA_BF16 = 1, ANIMA_F16 = 2, ANIMA_I8 = 3, ANIMA_U8 = 4 } anima_dtype;
+typedef enum { ANIMA_ACT_NONE = 0, ANIMA_ACT_GELU = 1, ANIMA_ACT_SILU = 2 } anima_act;
+
+/* Weight kinds of app/weights.js:118-146 ({kind: "i8" | "w4" | "bf16"}) plus fp32 (LoRA A/B). */
+typedef enum { ANIMA_W_I8 = 0, ANIMA_W_W4 = 1, ANIMA_W_BF16 = 2, ANIMA_W_F32 = 3 } anima_weight_kind;
+
+/* Rotated, per-token quantized activation rows (the "xr" input of ops.linear, ops.js:48-54):
+ *   x[m, k] ~= scale[m] * (hi[m, k] + lo[m, k] / 254)
+ * lo == NULL is the one-plane W8A8 form (x ~= scale * hi). hi/lo are row-major int8 [rows, ld]. */
+typedef struct {
+  int rows, cols, ld;
+  int8_t* hi;
+  int8_t* lo;
+  float* scale;
+} anima_qact;
+
+/* A linear layer's weights in the comfy_quant layout (app/weights.js:118-146).
+ *   I8  : data = int8 codes [N, K], scale = weight_scale [N]
+ *   W4  : data = packed nibbles [N, K/2] (low nibble = even k), s_rel = fp8-e4m3 [N, K/16],
+ *         codebook = [16], scale = weight_s_channel [N]
+ *   BF16: data = bf16 [N, K];  F32: data = fp32 [N, K]
+ * ConvRot layers (I8, W4) take rotated inputs, as in the reference (ops.js:35). */
+typedef struct {
+  int kind, N, K;
+  const void* data;
+  const float* scale;
+  const uint8_t* s_rel;
+  const float* codebook;
+  const float* bias;
+} anima_weight;
+
+typedef enum {
+  ANIMA_OUT_STORE = 0,          /* out[m, n] = y                                               */
+  ANIMA_OUT_RESID = 1,          /* out[m, n] += (gate ? gate[gate_off + n] : 1) * y, fp32 out  */
+  ANIMA_OUT_QKV_NORM_ROPE = 2,  /* per-head RMSNorm + split-half RoPE on q/k columns           */
+  ANIMA_OUT_HEAD_NORM = 3,      /* per-head RMSNorm with norm_q on every head, no RoPE         */
+} anima_out_mode;
+
+/* Epilogue of anima_linear, in the reference's order (app/gpu/gemm.js:186-192):
+ * y = acc * a_scale[m] * w_scale[n] (+ bias[n]) (+ add[m, n]) -> act -> output mode. */
+typedef struct {
+  int act;
+  const float* add;
+  int ld_add;
+  int out_mode;
+  int out_dtype;
+  void* out;
+  int ldo;
+  const float* gate;
+  int gate_off;
+  const float* norm_q; /* [128] */
+  const float* norm_k; /* [128] */
+  const float* rope;   /* cos [rope_rows, 64] followed by sin [rope_rows, 64]; row = m % rope_rows */
+  int rope_rows;
+  int n_q;             /* QKV: columns [0, n_q) q heads, [n_q, 2 n_q) k heads, the rest v */
+  float eps;
+} anima_linear_opts;
+
+typedef struct {
+  int batch, heads, head_dim, Lq, Lk;
+  int dtype;               /* ANIMA_BF16 or ANIMA_F16 for q/k/v */
+  const void* q; long long ldq, q_bstride; int q_off;
+  const void* k; long long ldk, k_bstride; int k_off;
+  const void* v; long long ldv, v_bstride; int v_off;
+  void* out; long long ldo, o_bstride; int out_dtype; /* F32, BF16 or F16 */
+  const int* key_len;      /* [batch] keys >= key_len[b] are masked; NULL = all Lk keys.
+                              k_bstride == v_bstride == 0 with batch > 1 shares one K/V and key_len[0]. */
+  float scale;             /* softmax scale, 1/sqrt(head_dim) in the reference */
+} anima_attention_args;
+
+/* ---------------------------------------------------------------- runtime (device.js GPU) */
+/* GPU.create (device.js:61-87). */
+int anima_ctx_create(int device, anima_ctx** out);
+int anima_ctx_destroy(anima_ctx* ctx);
+/* Run subsequent calls on this CUDA stream (cudaStream_t; NULL = legacy default stream). */
+int anima_ctx_set_stream(anima_ctx* ctx, void* stream);
+/* gpu.sync (device.js:218-232): wait for the stream, then report device-side errors. */
+int anima_sync(anima_ctx* ctx);
+const char* anima_last_error(void);
+/* gpu.empty / Tensor.release (device.js:20-23,124-128), plain device allocations. */
+int anima_alloc(anima_ctx* ctx, size_t bytes, void** out);
+int anima_free(anima_ctx* ctx, void* ptr);
+/* gpu.fromArray/upload and gpu.read (device.js:130-156,218-224): host <-> device copies. */
+int anima_upload(anima_ctx* ctx, void* dst, const void* src, size_t bytes);
+int anima_download(anima_ctx* ctx, void* dst, const void* src, size_t bytes);
+/* Profiler (device.js:235-288): per-op CUDA-event timing, enabled by ANIMA_PROFILE=1. Writes a
+ * text table into buf (NUL-terminated, truncated to cap). */
+int anima_profile_report(anima_ctx* ctx, char* buf, size_t cap);
+int anima_version(void);
+
+/* ---------------------------------------------------------------- weights (weights.js, gemm.js) */
+/* Decode 4-bit codes to their int8-grid values, bit-exact with tools/quant.py:179-180 and the
+ * tile loader of app/gpu/gemm.js:141-158: grid = clamp(rne(cb[code] * fp8(s_rel)), -127, 127).
+ * out: int8 [N, K]. */
+int anima_unpack_w4(anima_ctx* ctx, const uint8_t* packed, const uint8_t* s_rel, const float* codebook, int N, int K,
+                    int8_t* out);
+
+/* ---------------------------------------------------------------- operators (ops.js) */
+/* ops.linear (ops.js:48-66) for ConvRot weights: tcgen05 kind::i8 GEMM of the quantized rows x
+ * with W (kind I8; W4 must be unpacked with anima_unpack_w4 first), fused epilogue. */
+int anima_linear(anima_ctx* ctx, const anima_qact* x, const anima_weight* W, const anima_linear_opts* o);
+
+/* runMatmul for "bf16"/"f32" weights (ops.js:14-33, gemm.js:81-127): C = epi(alpha A B^T),
+ * A fp32 [M, lda], B bf16/f32 [N, ldb]; epilogue (+bias[n]) act, then store or C += gate*y.
+ * Used for x_embedder, final layer, time conditioning and the LoRA down/up products. */
+int anima_matmul(anima_ctx* ctx, int M, int N, int K, float alpha, const float* A, int lda, const anima_weight* B,
+                 int act, float* C, int ldc, int accumulate, const float* gate, int gate_off);
+
+/* LoRA down-projection for every side path of a linear at once (ops.js:78-79, the first GEMM of
+ * loraDelta): T[m, j] = sum_k x[m, k] * A[j, k] with x the quantized rows the base GEMM consumes
+ * and A the entries' (rotated) down matrices stacked [r, K] fp32; T fp32 [rows, ldt]. */
+int anima_lora_down(anima_ctx* ctx, const anima_qact* x, const float* A, int r, float* T, int ldt);
+
+/* ops.layernormMod (ops.js:129-137, kernels.js:95-145): y = LN(x)*(1+mod[scale_off+c]) +
+ * mod[shift_off+c], optionally followed by the 256-point ConvRot Hadamard. out_dtype F32/BF16/F16. */
+int anima_layernorm_mod(anima_ctx* ctx, const float* x, int rows, int cols, const float* mod, int shift_off,
+                        int scale_off, float eps, int rotate, void* out, int out_dtype);
+/* Same, fused with ConvRot and the per-token quantization a quantized linear consumes. */
+int anima_layernorm_mod_quant(anima_ctx* ctx, const float* x, int rows, int cols, const float* mod, int shift_off,
+                              int scale_off, float eps, const anima_qact* out);
+/* ops.rotate (ops.js:38-44, kernels.js:359-388): y = x H per 256 group. in/out dtype F32/BF16/F16. */
+int anima_rotate(anima_ctx* ctx, const void* x, int in_dtype, int rows, int cols, int ldx, void* y, int out_dtype);
+/* ops.rotate fused with per-token quantization into anima_qact (input F32/BF16/F16). */
+int anima_rotate_quant(anima_ctx* ctx, const void* x, int in_dtype, int rows, int cols, int ldx, const anima_qact* out);
+/* Per-token quantization without rotation (input already rotated). */
+int anima_quant_rows(anima_ctx* ctx, const void* x, int in_dtype, int rows, int cols, int ldx, const anima_qact* out);
+/* ops.rmsnorm (ops.js:111-117): y = x * rsqrt(mean(x^2) + eps) * w over rows of `cols`. */
+int anima_rmsnorm(anima_ctx* ctx, const void* x, int in_dtype, int rows, int cols, const float* w, float eps, void* y,
+                  int out_dtype);
+/* ops.qkNormRope (ops.js:140-145, kernels.js:301-334), in place on qkv [L, ld] (dtype F32/BF16/F16). */
+int anima_qk_norm_rope(anima_ctx* ctx, void* qkv, int dtype, int L, int H, int D, int ld, const float* qn,
+                       const float* kn, const float* rope, int rope_rows, float eps);
+/* ops.rope (ops.js:148-152, kernels.js:336-357), in place on x viewed as [L, H, D] at colOff. */
+int anima_rope(anima_ctx* ctx, void* x, int dtype, int L, int H, int D, int row_stride, int col_off,
+               const float* rope, int rope_rows);
+/* ops.attention (ops.js:166-208, kernels.js:147-299): non-causal multi-head attention, tcgen05
+ * flash kernel, fp32 softmax. head_dim must be 128. */
+int anima_attention(anima_ctx* ctx, const anima_attention_args* a);
+/* ops.elementwise (ops.js:154-160): op 0 copy, 1 add, 2 silu, 3 silu_mul; n fp32 elements. */
+int anima_elementwise(anima_ctx* ctx, int op, const float* a, const float* b, float* y, long long n);
+/* ops.zero (ops.js:89-93). */
+int anima_zero(anima_ctx* ctx, void* p, size_t bytes);
+
+/* ---------------------------------------------------------------- model glue (dit.js, pipeline.js) */
+/* patchify (dit.js:55-65): latent [B, 16, h, w] -> patches [B, (h/2)(w/2), 68] with the zero mask channel. */
+int anima_patchify(anima_ctx* ctx, const float* latent, int B, int h, int w, float* patches);
+/* unpatchify (dit.js:68-78): [B, (h/2)(w/2), 64] -> [B, 16, h, w]. */
+int anima_unpatchify(anima_ctx* ctx, const float* o, int B, int h, int w, float* latent);
+/* timestepEmbedding (dit.js:41-51) for B sigmas (device array): temb [B, 2048]. */
+int anima_timestep_embedding(anima_ctx* ctx, const float* sigmas, int B, float* temb);
+/* CFG combine + x0 prediction + Euler step (pipeline.js:260-269, samplers.js:109-117):
+ *   v = v_uncond ? v_uncond + cfg (v - v_uncond) : v;  den = x - sigma v;
+ *   x = (sigma_next == 0) ? den : (sigma_next/sigma) x + (1 - sigma_next/sigma) den.
+ * den_out may be NULL. */
+int anima_euler_step(anima_ctx* ctx, float* x, const float* v, const float* v_uncond, float cfg, float sigma,
+                     float sigma_next, long long n, float* den_out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ANIMA_B200_H */

@@ -11,3 +11,20 @@ tests/test_oracle.py checks this restatement against every one of them.
 """
 
 from .ref_np import *  # noqa: F401,F403
+
+
+def to_numpy(d: dict) -> dict:
+    """torch tensors of a checkpoint dict -> numpy for the oracle (bf16 -> fp32, fp8 -> raw bytes)."""
+    import torch
+
+    out = {}
+    for k, v in d.items():
+        if isinstance(v, torch.Tensor):
+            v = v.detach().cpu()
+            if v.dtype == torch.float8_e4m3fn:
+                v = v.view(torch.uint8)
+            elif v.dtype == torch.bfloat16:
+                v = v.float()
+            v = v.numpy()
+        out[k] = v
+    return out

@@ -164,15 +164,15 @@ def attention(q, k, v, key_len=None):
     """
     H, Lq, D = q.shape
     out = np.empty((H, Lq, v.shape[-1]), dtype=f32)
-    scale = 1.0 / math.sqrt(D)
-    for h in range(H):
-        s = (q[h].astype(np.float64) @ k[h].astype(np.float64).T) * scale
+    scale = f32(1.0 / math.sqrt(D))
+    for h in range(H):  # fp32 with max subtraction, like the reference's fp32 SDPA on the CPU
+        s = (q[h].astype(f32) @ k[h].astype(f32).T) * scale
         if key_len is not None:
             s[:, key_len:] = -np.inf
         s -= s.max(axis=-1, keepdims=True)
         p = np.exp(s)
-        p /= p.sum(axis=-1, keepdims=True)
-        out[h] = (p @ v[h].astype(np.float64)).astype(f32)
+        p /= p.sum(axis=-1, keepdims=True, dtype=f32)
+        out[h] = p @ v[h].astype(f32)
     return out
 
 

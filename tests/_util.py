@@ -6,17 +6,9 @@ import torch
 
 def to_np(d):
     """torch tensors -> numpy for the oracle: bf16 -> fp32, fp8 -> raw uint8 bytes."""
-    out = {}
-    for k, v in d.items():
-        if isinstance(v, torch.Tensor):
-            v = v.detach().cpu()
-            if v.dtype == torch.float8_e4m3fn:
-                v = v.view(torch.uint8)
-            elif v.dtype == torch.bfloat16:
-                v = v.float()
-            v = v.numpy()
-        out[k] = v
-    return out
+    import oracle
+
+    return oracle.to_numpy(d)
 
 
 def rel_l2(got, ref):

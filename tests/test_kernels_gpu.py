@@ -1,0 +1,318 @@
+"""Kernel parity on a B200: every operator of libanima_b200 against the numpy oracle.
+
+Integer work (W4 decode, the int8 GEMM accumulation) is checked bit-exact / to fp32 rounding;
+floating-point ops against the oracle's fp32 math with the tolerance stated in each test.
+"""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from tests._util import rel_l2, to_np
+from tests.conftest import GOLDEN, pkg
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module")
+def ops():
+    return pkg("ops")
+
+
+def gen(seed):
+    return torch.Generator(device="cpu").manual_seed(seed)
+
+
+def randn(shape, seed, scale=1.0):
+    return torch.randn(shape, generator=gen(seed)) * scale
+
+
+# ----------------------------------------------------------------------------- weights
+
+@pytest.mark.parametrize("case", ["w4_gauss", "w4_fit"])
+def test_unpack_w4_bit_exact(ops, case):
+    g = dict(np.load(os.path.join(GOLDEN, f"quant_{case}.npz")))
+    N, half = g["weight"].shape
+    out = ops.unpack_w4(torch.from_numpy(g["weight"].view(np.uint8)).to(DEV),
+                        torch.from_numpy(g["weight_s_rel"]).to(DEV),
+                        torch.from_numpy(g["weight_codebook"]).to(DEV), N, 2 * half)
+    np.testing.assert_array_equal(out.cpu().numpy().astype(np.float32), g["grid"])
+
+
+def test_unpack_w4_all_codes_and_scales(ops):
+    """Every (code, fp8 scale byte) pair except NaN bytes, against the oracle's decode."""
+    s_bytes = np.array([b for b in range(256) if (b & 0x7F) != 0x7F], dtype=np.uint8)
+    N = len(s_bytes)
+    K = 16 * 16
+    codes = np.tile(np.arange(16, dtype=np.uint8), (N, K // 16))
+    packed = (codes[:, 0::2] | (codes[:, 1::2] << 4)).astype(np.uint8)
+    s_rel = np.repeat(s_bytes[:, None], K // 16, 1)
+    cb = (oracle.FIXED_LUT * 3.7).astype(np.float32)
+    out = ops.unpack_w4(torch.from_numpy(packed).to(DEV), torch.from_numpy(s_rel).to(DEV),
+                        torch.from_numpy(cb).to(DEV), N, K)
+    ref = oracle.decode_w4_grid(packed, s_rel, cb)
+    np.testing.assert_array_equal(out.cpu().numpy().astype(np.float32), ref)
+
+
+# ----------------------------------------------------------------------------- row ops
+
+@pytest.mark.parametrize("rotate", [False, True])
+def test_layernorm_mod(ops, rotate):
+    x = randn((300, 2048), 1) * 3 + 0.5
+    mod = randn((6144,), 2, 0.5)
+    y = ops.layernorm_mod(x.to(DEV), mod.to(DEV), 0, 2048, 2048, rotate=rotate).cpu().numpy()
+    ref = oracle.layer_norm(x.numpy()) * (1 + mod[2048:4096].numpy()) + mod[:2048].numpy()
+    if rotate:
+        ref = oracle.rotate(ref)
+    assert rel_l2(y, ref) < 2e-6
+
+
+# two planes: |error| <= s / 508 per element, ~3.6e-5 relative for Gaussian rows
+@pytest.mark.parametrize("planes,tol", [(2, 6e-5), (1, 1e-2)])
+def test_layernorm_mod_quant(ops, planes, tol):
+    x = randn((257, 2048), 3) * 2
+    mod = randn((6144,), 4, 0.5)
+    q = ops.layernorm_mod_quant(x.to(DEV), mod.to(DEV), 0, 2048, 2048, planes=planes)
+    ref = oracle.rotate(oracle.layer_norm(x.numpy()) * (1 + mod[2048:4096].numpy()) + mod[:2048].numpy())
+    assert rel_l2(q.dequant().cpu().numpy(), ref) < tol
+    assert q.hi.abs().max().item() <= 127
+    s = q.scale.cpu().numpy()
+    np.testing.assert_allclose(s, np.abs(ref).max(1) / 127, rtol=1e-5)
+
+
+@pytest.mark.parametrize("cols", [1024, 2048, 8192])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_rotate_quant(ops, cols, dtype):
+    x = (randn((130, cols), 5) * 1.5).to(dtype)
+    q = ops.rotate_quant(x.to(DEV))
+    ref = oracle.rotate(x.float().numpy())
+    assert rel_l2(q.dequant().cpu().numpy(), ref) < 6e-5
+
+
+def test_rotate_plain(ops):
+    x = randn((64, 2048), 6)
+    y = ops.rotate(x.to(DEV)).cpu().numpy()
+    assert rel_l2(y, oracle.rotate(x.numpy())) < 1e-6
+
+
+def test_rmsnorm_and_qk_norm_rope(ops):
+    L, H = 96, 16
+    x = randn((L * H, 128), 7) * 2
+    w = 1 + randn((128,), 8, 0.1)
+    y = ops.rmsnorm(x.to(DEV), w.to(DEV), 128).cpu().numpy()
+    assert rel_l2(y, oracle.rms_norm(x.numpy(), w.numpy())) < 2e-6
+    qkv = randn((L, 3 * 2048), 9)
+    qn, kn = 1 + randn((128,), 10, 0.1), 1 + randn((128,), 11, 0.1)
+    cs = torch.from_numpy(pkg("dit").rope_table(8, 12))
+    t = qkv.clone().to(DEV)
+    ops.qk_norm_rope(t, qn.to(DEV), kn.to(DEV), cs.to(DEV), L, H, 128)
+    cos, sin = oracle.dit_rope(8, 12)
+    cos, sin = np.concatenate([cos, cos], -1)[:, None], np.concatenate([sin, sin], -1)[:, None]
+    q = oracle.rms_norm(qkv[:, :2048].numpy().reshape(L, H, 128), qn.numpy())
+    k = oracle.rms_norm(qkv[:, 2048:4096].numpy().reshape(L, H, 128), kn.numpy())
+    q = q * cos + oracle.rotate_half(q) * sin
+    k = k * cos + oracle.rotate_half(k) * sin
+    got = t.cpu().numpy()
+    assert rel_l2(got[:, :2048], q.reshape(L, -1)) < 2e-6
+    assert rel_l2(got[:, 2048:4096], k.reshape(L, -1)) < 2e-6
+    np.testing.assert_array_equal(got[:, 4096:], qkv[:, 4096:].numpy())
+
+
+def test_elementwise_patchify_timestep_euler(ops):
+    a, b = randn((1000,), 12), randn((1000,), 13)
+    for op, ref in (("copy", a), ("add", a + b), ("silu", oracle.silu(a.numpy())),
+                    ("silu_mul", oracle.silu(a.numpy()) * b.numpy())):
+        y = ops.elementwise(op, a.to(DEV), b.to(DEV)).cpu().numpy()
+        assert rel_l2(y, np.asarray(ref)) < 1e-6, op
+    lat = randn((2, 16, 12, 20), 14)
+    p = ops.patchify(lat.to(DEV)).cpu().numpy()
+    ref = np.concatenate([oracle.patchify(lat[i].numpy()) for i in range(2)])
+    np.testing.assert_array_equal(p, ref)
+    o = randn((2 * 6 * 10, 64), 15)
+    u = ops.unpatchify(o.to(DEV), 2, 12, 20).cpu().numpy()
+    ref = np.stack([oracle.unpatchify(o[i * 60:(i + 1) * 60].numpy(), 12, 20) for i in range(2)])
+    np.testing.assert_array_equal(u, ref)
+    sig = torch.tensor([0.9, 0.25, 1.0])
+    t = ops.timestep_embedding(sig.to(DEV)).cpu().numpy()
+    for i, s in enumerate(sig.tolist()):
+        assert np.abs(t[i] - oracle.timestep_embedding(s)[0]).max() < 2e-6
+    x, v, vn = randn((500,), 16), randn((500,), 17), randn((500,), 18)
+    xd = x.clone().to(DEV)
+    ops.euler_step(xd, v.to(DEV), 0.8, 0.5, v_uncond=vn.to(DEV), cfg=4.5)
+    vel = vn + (v - vn) * 4.5
+    den = x - vel * 0.8
+    assert rel_l2(xd.cpu().numpy(), (x + (x - den) / 0.8 * (0.5 - 0.8)).numpy()) < 1e-6
+    xd = x.clone().to(DEV)
+    ops.euler_step(xd, v.to(DEV), 0.3, 0.0)
+    assert rel_l2(xd.cpu().numpy(), (x - v * 0.3).numpy()) < 1e-6
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 6144, 2048), (64, 2048, 68), (130, 64, 2048)])
+@pytest.mark.parametrize("kind", ["bf16", "f32"])
+def test_matmul_simt(ops, M, N, K, kind):
+    W = pkg("weights")
+    x = randn((M, K), 19)
+    w = randn((N, K), 20, 0.02)
+    wt = w.to(torch.bfloat16) if kind == "bf16" else w
+    lin = W.Linear(kind, N, K, wt.to(DEV).contiguous())
+    y = ops.matmul(x.to(DEV), lin, act="silu").cpu().numpy()
+    ref = oracle.silu(x.numpy() @ wt.float().numpy().T)
+    assert rel_l2(y, ref) < 2e-6
+
+
+# ----------------------------------------------------------------------------- tcgen05 int8 GEMM
+
+def make_linear(N, K, seed):
+    W = pkg("weights")
+    g = gen(seed)
+    q = (torch.randn(N, K, generator=g) * 40).round().clamp(-127, 127).to(torch.int8)
+    s = 0.0005 * (1 + torch.rand(N, generator=g))
+    return W.Linear("i8", N, K, q.to(DEV), s.to(DEV)), q.float().numpy(), s.numpy()
+
+
+def gemm_ref(qa, wq, ws):
+    return qa.dequant().cpu().double().numpy() @ wq.astype(np.float64).T * ws.astype(np.float64)
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 256), (200, 2048, 2048), (4096, 6144, 2048), (333, 2048, 8192),
+                                   (512, 8192, 2048), (77, 2048, 1024), (256, 384, 256)])
+@pytest.mark.parametrize("planes", [2, 1])
+def test_linear_store_f32(ops, M, N, K, planes):
+    lin, wq, ws = make_linear(N, K, M + N + K)
+    x = randn((M, K), 21) * 2
+    qa = ops.rotate_quant(x.to(DEV), planes=planes)
+    y = ops.linear(qa, lin).cpu().numpy()
+    ref = gemm_ref(qa, wq, ws)
+    # integer accumulation is exact; the epilogue's fp32 scaling rounds at ~1e-7
+    assert rel_l2(y, ref) < 1e-6
+
+
+@pytest.mark.parametrize("out_dtype,tol", [(torch.bfloat16, 5e-3), (torch.float16, 6e-4)])
+def test_linear_store_16bit_gelu(ops, out_dtype, tol):
+    M, N, K = 300, 8192, 2048
+    lin, wq, ws = make_linear(N, K, 3)
+    qa = ops.rotate_quant((randn((M, K), 22) * 2).to(DEV))
+    y = ops.linear(qa, lin, act="gelu", out_dtype=out_dtype).float().cpu().numpy()
+    ref = oracle.gelu(gemm_ref(qa, wq, ws).astype(np.float32))
+    assert rel_l2(y, ref) < tol
+
+
+def test_linear_gated_residual_bias_add(ops):
+    M, N, K = 260, 2048, 2048
+    lin, wq, ws = make_linear(N, K, 4)
+    lin.bias = (randn((N,), 23, 0.1)).to(DEV)
+    qa = ops.rotate_quant((randn((M, K), 24)).to(DEV))
+    x0 = randn((M, N), 25)
+    add = randn((M, N), 26, 0.05)
+    mod = randn((6144,), 27, 0.5)
+    out = x0.clone().to(DEV)
+    ops.linear(qa, lin, out=out, resid=True, gate=mod.to(DEV), g_off=4096, add=add.to(DEV))
+    y = gemm_ref(qa, wq, ws) + lin.bias.cpu().numpy() + add.numpy()
+    ref = x0.numpy() + mod[4096:].numpy() * y
+    assert rel_l2(out.cpu().numpy(), ref) < 1e-6
+
+
+def test_linear_qkv_norm_rope_epilogue(ops):
+    Hp, Wp = 8, 12
+    L = Hp * Wp
+    B = 2
+    M, N, K = B * L, 6144, 2048
+    lin, wq, ws = make_linear(N, K, 5)
+    qa = ops.rotate_quant((randn((M, K), 28)).to(DEV))
+    qn, kn = 1 + randn((128,), 29, 0.1), 1 + randn((128,), 30, 0.1)
+    cs = torch.from_numpy(pkg("dit").rope_table(Hp, Wp)).to(DEV)
+    out = ops.linear(qa, lin, mode="qkv", qk=(qn.to(DEV), kn.to(DEV)), rope_cs=cs, n_q=2048,
+                     out_dtype=torch.float32).cpu().numpy()
+    y = gemm_ref(qa, wq, ws).astype(np.float32)
+    cos, sin = oracle.dit_rope(Hp, Wp)
+    cos = np.tile(np.concatenate([cos, cos], -1), (B, 1))[:, None]
+    sin = np.tile(np.concatenate([sin, sin], -1), (B, 1))[:, None]
+    q = oracle.rms_norm(y[:, :2048].reshape(M, 16, 128), qn.numpy())
+    k = oracle.rms_norm(y[:, 2048:4096].reshape(M, 16, 128), kn.numpy())
+    q = q * cos + oracle.rotate_half(q) * sin
+    k = k * cos + oracle.rotate_half(k) * sin
+    assert rel_l2(out[:, :2048], q.reshape(M, -1)) < 2e-6
+    assert rel_l2(out[:, 2048:4096], k.reshape(M, -1)) < 2e-6
+    assert rel_l2(out[:, 4096:], y[:, 4096:]) < 1e-6
+    # head-norm mode (cross q) on the first 2048 columns
+    lin2, wq2, ws2 = make_linear(2048, K, 6)
+    h = ops.linear(qa, lin2, mode="head_norm", qk=(qn.to(DEV),), out_dtype=torch.float32).cpu().numpy()
+    ref = oracle.rms_norm(gemm_ref(qa, wq2, ws2).astype(np.float32).reshape(M, 16, 128), qn.numpy())
+    assert rel_l2(h, ref.reshape(M, -1)) < 2e-6
+
+
+def test_linear_rejects_bad_shapes(ops):
+    dev = pkg("device")
+    lin, _, _ = make_linear(2048, 2048, 7)
+    qa = ops.rotate_quant(randn((16, 1024), 31).to(DEV))
+    with pytest.raises(dev.AnimaError, match="columns"):
+        ops.linear(qa, lin)
+
+
+# ----------------------------------------------------------------------------- attention
+
+def attn_ref(q, k, v, key_len=None):
+    """fp32 oracle attention on the same 16-bit inputs; q [H, Lq, D]."""
+    return oracle.attention(q.float().numpy(), k.float().numpy(), v.float().numpy(), key_len)
+
+
+@pytest.mark.parametrize("L", [128, 200, 1024])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_self_attention_qkv_layout(ops, L, dtype):
+    H = 16
+    qkv = (randn((L, 3 * 2048), 32 + L)).to(dtype)
+    out = ops.attention(qkv.to(DEV), qkv.to(DEV), qkv.to(DEV), Lq=L, Lk=L, H=H, ldq=6144, ldk=6144, ldv=6144,
+                        q_off=0, k_off=2048, v_off=4096, out_dtype=torch.float32).cpu().numpy()
+    q = qkv[:, :2048].reshape(L, H, 128).transpose(0, 1)
+    k = qkv[:, 2048:4096].reshape(L, H, 128).transpose(0, 1)
+    v = qkv[:, 4096:].reshape(L, H, 128).transpose(0, 1)
+    ref = attn_ref(q, k, v).transpose(1, 0, 2).reshape(L, 2048)
+    # P is rounded to the 16-bit input type before P V (bf16: ~2^-9 relative per probability)
+    tol = 6e-3 if dtype == torch.bfloat16 else 1e-3
+    assert rel_l2(out, ref) < tol
+
+
+def test_cross_attention_batched_masked(ops):
+    B, H, Lq, Lk = 2, 16, 300, 256
+    q = randn((B * Lq, 2048), 40).to(torch.bfloat16)
+    k = randn((B * Lk, 2048), 41).to(torch.bfloat16)
+    v = randn((B * Lk, 2048), 42).to(torch.bfloat16)
+    kl = torch.tensor([37, 256], dtype=torch.int32)
+    out = ops.attention(q.to(DEV), k.to(DEV), v.to(DEV), Lq=Lq, Lk=Lk, H=H, batch=B, q_bstride=Lq * 2048,
+                        k_bstride=Lk * 2048, v_bstride=Lk * 2048, key_len=kl.to(DEV),
+                        out_dtype=torch.float32).cpu().numpy()
+    for b in range(B):
+        qb = q[b * Lq:(b + 1) * Lq].reshape(Lq, H, 128).transpose(0, 1)
+        kb = k[b * Lk:(b + 1) * Lk].reshape(Lk, H, 128).transpose(0, 1)
+        vb = v[b * Lk:(b + 1) * Lk].reshape(Lk, H, 128).transpose(0, 1)
+        ref = attn_ref(qb, kb, vb, int(kl[b])).transpose(1, 0, 2).reshape(Lq, 2048)
+        assert rel_l2(out[b * Lq:(b + 1) * Lq], ref) < 6e-3, b
+
+
+def test_cross_attention_shared_kv_zero_padded(ops):
+    """The reference's semantics: context zero-padded to 512 rows, no mask (dit.js:185-190)."""
+    B, H, Lq, Lk = 2, 16, 256, 512
+    q = randn((B * Lq, 2048), 43).to(torch.bfloat16)
+    k = torch.cat([randn((200, 2048), 44), torch.zeros(312, 2048)]).to(torch.bfloat16)
+    v = torch.cat([randn((200, 2048), 45), torch.zeros(312, 2048)]).to(torch.bfloat16)
+    out = ops.attention(q.to(DEV), k.to(DEV), v.to(DEV), Lq=Lq, Lk=Lk, H=H, batch=B, q_bstride=Lq * 2048,
+                        k_bstride=0, v_bstride=0, out_dtype=torch.float32).cpu().numpy()
+    kb = k.reshape(Lk, H, 128).transpose(0, 1)
+    vb = v.reshape(Lk, H, 128).transpose(0, 1)
+    for b in range(B):
+        qb = q[b * Lq:(b + 1) * Lq].reshape(Lq, H, 128).transpose(0, 1)
+        ref = attn_ref(qb, kb, vb).transpose(1, 0, 2).reshape(Lq, 2048)
+        assert rel_l2(out[b * Lq:(b + 1) * Lq], ref) < 6e-3
+
+
+def test_device_errors_surface_at_sync(ops):
+    """Synchronising reports success when nothing faulted (the error word starts clear)."""
+    ctx = pkg("device").Context.get(0)
+    x = randn((4, 2048), 46).to(DEV)
+    ops.rotate(x)
+    ctx.sync()
