@@ -8,12 +8,13 @@
 // plane (lo == NULL) this is plain W8A8. Weights are int8 [N, K] K-major, i.e. the comfy_quant
 // `weight` tensor as stored.
 //
-// Structure: persistent CTAs (one per SM), 192 threads, warp-specialised:
-//   warp 0      TMA producer: A tile(s) 128 x 128 B and W tile BN x 128 B per stage (SWIZZLE_128B)
-//   warp 1      TMEM allocator + single-thread UMMA issuer (M = 128, N = BN, K = 32 per instruction)
-//   warps 2..5  epilogue: tcgen05.ld of the accumulator rows (thread = row), fused epilogue, stores
-// Accumulators are double-buffered in TMEM when they fit (NPLANES * BN <= 256 columns) so the
-// epilogue of tile i overlaps the MMAs of tile i+1.
+// Structure: persistent CTAs (one per SM), 320 threads:
+//   WG0, WG1    epilogue: tcgen05.ld of the accumulator rows (thread = row), fused epilogue, stores;
+//               WG0 takes the CTA's even tiles, WG1 the odd ones (two warps per scheduler)
+//   warp 8      TMA producer: A tile(s) 128 x 128 B and W tile BN x 128 B per stage (SWIZZLE_128B)
+//   warp 9      TMEM allocator + single-thread UMMA issuer (M = 128, N = BN, K = 32 per instruction)
+// The accumulators are double-buffered in TMEM (2 x NPLANES x BN = 512 columns), one buffer per
+// epilogue warpgroup, so the epilogues of two tiles overlap the MMAs of the next.
 
 #include "internal.h"
 #include "sm100.cuh"
@@ -24,7 +25,7 @@ namespace gemm {
 constexpr int BM = 128;
 constexpr int BK = 128;      // bytes of K per stage (one SWIZZLE_128B row)
 constexpr int UMMA_K = 32;   // K per kind::i8 instruction
-constexpr int THREADS = 192;
+constexpr int THREADS = 320;  // 8 epilogue warps + producer warp + MMA warp
 
 struct Params {
   int M, N, K;
@@ -46,8 +47,21 @@ struct Params {
   int rope_rows;
   int n_q;
   float eps;
-  int num_m_blocks, num_k_blocks, num_tiles;
+  int num_m_blocks, num_n_blocks, num_k_blocks, num_tiles;
 };
+
+// Tile order: groups of kGroupM m-blocks, n-blocks outermost within a group, so the CTAs in flight
+// share a few A row-blocks and sweep the weights (keeps A resident in L2 across the n sweep).
+constexpr int kGroupM = 8;
+__device__ __forceinline__ void tile_coords(const Params& p, int tile, int& mb, int& nb) {
+  const int per_group = kGroupM * p.num_n_blocks;
+  const int group = tile / per_group;
+  const int first_m = group * kGroupM;
+  const int gm = min(kGroupM, p.num_m_blocks - first_m);
+  const int within = tile - group * per_group;
+  mb = first_m + within % gm;
+  nb = within / gm;
+}
 
 template <int BN, int NPLANES>
 struct Cfg {
@@ -56,7 +70,10 @@ struct Cfg {
   static constexpr int STAGE_BYTES = NPLANES * A_BYTES + B_BYTES;
   static constexpr int STAGES = (200 * 1024) / STAGE_BYTES;
   static constexpr int ACC_COLS = NPLANES * BN;
+  // one accumulator buffer per epilogue warpgroup when two fit in TMEM, else one (the second
+  // epilogue warpgroup then idles and the epilogue of a tile delays the next tile's MMAs)
   static constexpr int ACC_BUFS = (2 * ACC_COLS <= 512) ? 2 : 1;
+  static_assert(ACC_BUFS * ACC_COLS <= 512, "accumulators exceed TMEM");
   static constexpr int TMEM_COLS = 512;
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
@@ -71,27 +88,28 @@ __device__ __forceinline__ float act_fn(float v, int act) {
   return v;
 }
 
-// Load 32 accumulator columns of this thread's row and apply scale, bias, add and activation.
+// Issue the TMEM loads of 32 accumulator columns (hi plane, and lo plane at +BN) of this row.
 template <int BN, int NPLANES>
-__device__ __forceinline__ void load_cols(const Params& p, uint32_t taddr, int col, int m, int n, bool row_ok,
-                                          float (&v)[32], bool apply_act) {
-  uint32_t rh[32];
+__device__ __forceinline__ void issue_cols(uint32_t taddr, int col, uint32_t (&rh)[32], uint32_t (&rl)[32]) {
   tmem_ld32(taddr + col, rh);
+  if constexpr (NPLANES == 2) tmem_ld32(taddr + BN + col, rl);
+}
+
+// After the loads landed: y = a_scale[m] w_scale[n] (hi + lo / 254) (+ bias) (+ add) (act).
+template <int NPLANES>
+__device__ __forceinline__ void finish_cols(const Params& p, int m, int n, bool row_ok, const uint32_t (&rh)[32],
+                                            const uint32_t (&rl)[32], float (&v)[32], bool apply_act) {
+  const float as = row_ok ? __ldg(p.a_scale + m) : 0.0f;
   if constexpr (NPLANES == 2) {
-    uint32_t rl[32];
-    tmem_ld32(taddr + BN + col, rl);
-    tmem_ld_wait();
+    const float as_lo = as * (1.0f / 254.0f);
 #pragma unroll
     for (int j = 0; j < 32; ++j)
-      v[j] = static_cast<float>(static_cast<int>(rh[j])) + static_cast<float>(static_cast<int>(rl[j])) * (1.0f / 254.0f);
+      v[j] = fmaf(static_cast<float>(static_cast<int>(rl[j])), as_lo, static_cast<float>(static_cast<int>(rh[j])) * as) *
+             __ldg(p.w_scale + n + j);
   } else {
-    tmem_ld_wait();
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = static_cast<float>(static_cast<int>(rh[j]));
+    for (int j = 0; j < 32; ++j) v[j] = static_cast<float>(static_cast<int>(rh[j])) * as * __ldg(p.w_scale + n + j);
   }
-  const float as = row_ok ? __ldg(p.a_scale + m) : 0.0f;
-#pragma unroll
-  for (int j = 0; j < 32; ++j) v[j] *= as * __ldg(p.w_scale + n + j);
   if (p.bias) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] += __ldg(p.bias + n + j);
@@ -111,6 +129,17 @@ __device__ __forceinline__ void load_cols(const Params& p, uint32_t taddr, int c
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = act_fn(v[j], p.act);
   }
+}
+
+// Load 32 accumulator columns and finish them (no overlap; used by the per-head epilogues).
+template <int BN, int NPLANES>
+__device__ __forceinline__ void load_cols(const Params& p, uint32_t taddr, int col, int m, int n, bool row_ok,
+                                          float (&v)[32], bool apply_act) {
+  uint32_t rh[32], rl[32];
+  issue_cols<BN, NPLANES>(taddr, col, rh, rl);
+  tmem_ld_wait(rh);
+  if constexpr (NPLANES == 2) tmem_ld_wait(rl);
+  finish_cols<NPLANES>(p, m, n, row_ok, rh, rl, v, apply_act);
 }
 
 __device__ __forceinline__ void store32(void* out, int dtype, int ldo, int m, int n, const float (&v)[32]) {
@@ -177,15 +206,26 @@ template <int BN, int NPLANES>
 __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t taddr, int m, int n0) {
   const bool row_ok = m < p.M;
   if (p.out_mode == ANIMA_OUT_STORE || p.out_mode == ANIMA_OUT_RESID) {
-#pragma unroll 1
-    for (int c = 0; c < BN; c += 32) {
+    // software pipeline: the TMEM loads of chunk c+1 are in flight while chunk c is finished
+    uint32_t rh[2][32], rl[2][32];
+    issue_cols<BN, NPLANES>(taddr, 0, rh[0], rl[0]);
+    tmem_ld_wait(rh[0]);
+    if constexpr (NPLANES == 2) tmem_ld_wait(rl[0]);
+#pragma unroll
+    for (int c = 0; c < BN / 32; ++c) {
+      const int cur = c & 1;
+      if (c + 1 < BN / 32) issue_cols<BN, NPLANES>(taddr, 32 * (c + 1), rh[cur ^ 1], rl[cur ^ 1]);
       float v[32];
-      load_cols<BN, NPLANES>(p, taddr, c, m, n0 + c, row_ok, v, true);
+      finish_cols<NPLANES>(p, m, n0 + 32 * c, row_ok, rh[cur], rl[cur], v, true);
       if (row_ok) {
         if (p.out_mode == ANIMA_OUT_STORE)
-          store32(p.out, p.out_dtype, p.ldo, m, n0 + c, v);
+          store32(p.out, p.out_dtype, p.ldo, m, n0 + 32 * c, v);
         else
-          resid32(p, m, n0 + c, v);
+          resid32(p, m, n0 + 32 * c, v);
+      }
+      if (c + 1 < BN / 32) {
+        tmem_ld_wait(rh[cur ^ 1]);
+        if constexpr (NPLANES == 2) tmem_ld_wait(rl[cur ^ 1]);
       }
     }
     return;
@@ -293,12 +333,13 @@ __global__ void __launch_bounds__(THREADS, 1)
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 0 && lane == 0) {
+  constexpr int kProducerWarp = 8, kMmaWarp = 9;
+  if (warp == kProducerWarp && lane == 0) {
     tma_prefetch_desc(&tm_hi);
     if (NPLANES == 2) tma_prefetch_desc(&tm_lo);
     tma_prefetch_desc(&tm_w);
   }
-  if (warp == 1) {
+  if (warp == kMmaWarp) {
     tmem_alloc(tmem_slot, C::TMEM_COLS);
     tmem_relinquish();
   }
@@ -307,15 +348,15 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  if (warp == 0) {
+  if (warp == kProducerWarp) {
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
       int armed_parity[C::STAGES];
       for (int s = 0; s < C::STAGES; ++s) armed_parity[s] = -1;
       for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
-        const int mb = tile % p.num_m_blocks;
-        const int nb = tile / p.num_m_blocks;
+        int mb, nb;
+        tile_coords(p, tile, mb, nb);
         for (int kb = 0; kb < p.num_k_blocks; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, kErrTimeoutEmpty)) goto producer_done;
           uint8_t* sa = smem + stage * C::STAGE_BYTES;
@@ -345,7 +386,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == kMmaWarp) {
     if (lane == 0) {
       const uint32_t idesc = idesc_i8(BM, BN);
       int stage = 0;
@@ -395,17 +436,20 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
     }
-  } else {
+  } else if (warp < 4 * C::ACC_BUFS) {
+    // epilogue warpgroup g = warp / 4 handles the CTA's local tiles t with t % ACC_BUFS == g
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    const int g = warp >> 2;
     const int row = quad * 32 + lane;
-    int t = 0;
-    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++t) {
-      const int buf = t % C::ACC_BUFS;
+    int t = g;
+    for (int tile = blockIdx.x + g * gridDim.x; tile < p.num_tiles;
+         tile += C::ACC_BUFS * gridDim.x, t += C::ACC_BUFS) {
+      const int buf = g;
       const uint32_t acc_phase = (t / C::ACC_BUFS) & 1;
       if (!warp_wait(&acc_full[buf], acc_phase, abort_flag, kErrTimeoutAcc)) break;
       tc_fence_after();
-      const int mb = tile % p.num_m_blocks;
-      const int nb = tile / p.num_m_blocks;
+      int mb, nb;
+      tile_coords(p, tile, mb, nb);
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + buf * C::ACC_COLS;
       epilogue_tile<BN, NPLANES>(p, taddr, mb * BM + row, nb * BN);
       tc_fence_before();
@@ -415,7 +459,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
@@ -466,8 +510,9 @@ int launch(anima_ctx* ctx, const anima_qact* x, const anima_weight* W, const ani
   p.n_q = o->n_q;
   p.eps = o->eps > 0 ? o->eps : 1e-6f;
   p.num_m_blocks = (M + BM - 1) / BM;
+  p.num_n_blocks = N / BN;
   p.num_k_blocks = K / BK;
-  p.num_tiles = p.num_m_blocks * (N / BN);
+  p.num_tiles = p.num_m_blocks * p.num_n_blocks;
 
   static bool attr_set = false;
   if (!attr_set) {
@@ -520,9 +565,15 @@ extern "C" int anima_linear(anima_ctx* ctx, const anima_qact* x, const anima_wei
     ANIMA_REQUIRE(o->n_q % 128 == 0 && 2 * o->n_q <= W->N, "anima_linear: bad n_q %d", o->n_q);
   }
   if (o->out_mode == ANIMA_OUT_HEAD_NORM) ANIMA_REQUIRE(o->norm_q, "anima_linear: head-norm epilogue needs norm_q");
+  // Two planes: 128-column tiles double-buffer both accumulators (2 x 2 x 128 TMEM columns) so the
+  // epilogue overlaps the next tile's MMAs; for long K (>= 4096) the MMA time per tile dwarfs the
+  // epilogue and 256-column tiles (one buffer) read 25% fewer shared-memory bytes per MMA.
+  // One plane: 256-column tiles, double-buffered.
   const bool two = x->lo != nullptr;
-  if (W->N % 256 == 0) {
-    return two ? gemm::launch<256, 2>(ctx, x, W, o) : gemm::launch<256, 1>(ctx, x, W, o);
+  if (two) {
+    if (W->N % 256 == 0 && W->K >= 4096) return gemm::launch<256, 2>(ctx, x, W, o);
+    return gemm::launch<128, 2>(ctx, x, W, o);
   }
-  return two ? gemm::launch<128, 2>(ctx, x, W, o) : gemm::launch<128, 1>(ctx, x, W, o);
+  if (W->N % 256 == 0) return gemm::launch<256, 1>(ctx, x, W, o);
+  return gemm::launch<128, 1>(ctx, x, W, o);
 }

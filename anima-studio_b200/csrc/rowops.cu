@@ -72,27 +72,6 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
-// Block-wide sum/max for up to 32 warps (red: shared scratch of 32 floats).
-__device__ __forceinline__ float block_sum(float v, float* red) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  v = warp_sum(v);
-  __syncthreads();
-  if (lane == 0) red[warp] = v;
-  __syncthreads();
-  float t = lane < nw ? red[lane] : 0.f;
-  return warp_sum(t);
-}
-
-__device__ __forceinline__ float block_max(float v, float* red) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  v = warp_max(v);
-  __syncthreads();
-  if (lane == 0) red[warp] = v;
-  __syncthreads();
-  float t = lane < nw ? red[lane] : 0.f;
-  return warp_max(t);
-}
-
 // 256-point ConvRot Hadamard of the group held by one warp, lane l holding elements 8l..8l+7:
 // y = x H, H = kron(H4, H4, H4, H4) / 16 with the regular H4 = [[1,1,1,-1],[1,1,-1,1],
 // [1,-1,1,1],[-1,1,1,1]] (tools/quant.py:30-38). Index i = d0 + 4 d1 + 16 d2 + 64 d3; each
@@ -145,113 +124,133 @@ __device__ __forceinline__ void fwht256_warp(float (&x)[8]) {
   for (int j = 0; j < 8; ++j) x[j] *= 0.0625f;
 }
 
-// Per-token quantization of one row held as G chunks of 8 floats per thread:
-//   s = amax / 127; a = x / s; hi = rne(a); lo = rne((a - hi) * 254)   (lo plane optional)
-template <int G>
-__device__ __forceinline__ void quantize_row(float (&x)[G][8], float* red, int8_t* hi, int8_t* lo, float* scale,
-                                             const int (&col)[G]) {
-  float amax = 0.f;
-#pragma unroll
-  for (int g = 0; g < G; ++g)
-#pragma unroll
-    for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(x[g][j]));
-  amax = block_max(amax, red);
-  const float s = amax > 0.f ? amax / 127.0f : 1.0f;
-  if (threadIdx.x == 0) *scale = s;
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    char4 h0, h1, l0, l1;
-    int8_t hv[8], lv[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float a = x[g][j] / s;
-      const float r = rintf(a);
-      hv[j] = static_cast<int8_t>(fminf(fmaxf(r, -127.f), 127.f));
-      lv[j] = static_cast<int8_t>(fminf(fmaxf(rintf((a - r) * 254.0f), -127.f), 127.f));
-    }
-    h0 = make_char4(hv[0], hv[1], hv[2], hv[3]);
-    h1 = make_char4(hv[4], hv[5], hv[6], hv[7]);
-    *reinterpret_cast<int2*>(hi + col[g]) = make_int2(*reinterpret_cast<int*>(&h0), *reinterpret_cast<int*>(&h1));
-    if (lo) {
-      l0 = make_char4(lv[0], lv[1], lv[2], lv[3]);
-      l1 = make_char4(lv[4], lv[5], lv[6], lv[7]);
-      *reinterpret_cast<int2*>(lo + col[g]) = make_int2(*reinterpret_cast<int*>(&l0), *reinterpret_cast<int*>(&l1));
-    }
-  }
-}
-
-// ------------------------------------------------------------------ LayerNorm + adaLN (+ rot) (+ quant)
-// One CTA per row; thread t holds elements [8 (t + T g), +8) for chunk g (T = blockDim.x), so each
-// warp holds whole 256-element ConvRot groups. Two-pass mean/variance in fp32 like the reference
-// (tools/reference.py:190-191: F.layer_norm, biased variance, eps 1e-6).
-template <int G, typename TOut>
-__global__ void __launch_bounds__(256) ln_mod_kernel(const float* __restrict__ x, int cols, const float* __restrict__ mod,
-                                                     int shift_off, int scale_off, float eps, int rotate, TOut* y,
-                                                     int8_t* qhi, int8_t* qlo, float* qscale, int qld) {
-  __shared__ float red[32];
-  const int row = blockIdx.x;
-  const int T = blockDim.x;
-  const float* xr = x + static_cast<size_t>(row) * cols;
-  float v[G][8];
-  int col[G];
-  float s = 0.f;
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    col[g] = 8 * (threadIdx.x + T * g);
-    load8(xr + col[g], v[g]);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) s += v[g][j];
-  }
-  const float mean = block_sum(s, red) / static_cast<float>(cols);
-  float q = 0.f;
-#pragma unroll
-  for (int g = 0; g < G; ++g)
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float d = v[g][j] - mean;
-      q += d * d;
-    }
-  const float var = block_sum(q, red) / static_cast<float>(cols);
-  const float rstd = 1.0f / sqrtf(var + eps);
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    float sc[8], sh[8];
-    load8(mod + scale_off + col[g], sc);
-    load8(mod + shift_off + col[g], sh);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) v[g][j] = (v[g][j] - mean) * rstd * (1.0f + sc[j]) + sh[j];
-    if (rotate) fwht256_warp(v[g]);
-  }
-  if (qhi) {
-    quantize_row<G>(v, red, qhi + static_cast<size_t>(row) * qld, qlo ? qlo + static_cast<size_t>(row) * qld : nullptr,
-                    qscale + row, col);
+// ------------------------------------------------------------------ row kernel: LN + adaLN, ConvRot, quant
+// One row per warp for rows up to 2048 wide (WPR = 1), WPR = cols / 2048 warps per row beyond;
+// 8 warps per CTA. Lane l holds, for each of the warp's G groups of 256 columns, the 8 consecutive
+// elements 8l..8l+7 of that group, so every warp access is a contiguous 256-element segment and
+// every ConvRot group lives in one warp (fwht256_warp). Reductions are warp shuffles, plus one
+// shared-memory step across the WPR warps of a row.
+//   LN      y = LN(x) * (1 + mod[scale_off + c]) + mod[shift_off + c]  (fp32 two-pass mean/var,
+//           biased variance, eps: tools/reference.py:190-191, kernels.js:95-145)
+//   act     y <- GELU(y) (the MLP's activation, applied here when the layer1 GEMM stored its
+//           pre-activation)
+//   rotate  y <- y H per 256 group (tools/quant.py:30-45)
+//   quant   s = amax / 127; a = y * (127 / amax); hi = rne(a); lo = rne((a - hi) * 254)
+template <int WPR>
+__device__ __forceinline__ float row_reduce(float v, float* red, bool is_max) {
+  v = is_max ? warp_max(v) : warp_sum(v);
+  if constexpr (WPR == 1) {
+    return v;
   } else {
+    const int warp = threadIdx.x >> 5;
+    const int base = (warp / WPR) * WPR;
+    if ((threadIdx.x & 31) == 0) red[warp] = v;
+    __syncthreads();
+    float t = red[base];
 #pragma unroll
-    for (int g = 0; g < G; ++g) store8(y + static_cast<size_t>(row) * cols + col[g], v[g]);
+    for (int i = 1; i < WPR; ++i) t = is_max ? fmaxf(t, red[base + i]) : t + red[base + i];
+    __syncthreads();
+    return t;
   }
 }
 
-// ------------------------------------------------------------------ ConvRot Hadamard (+ quant)
-template <int G, typename TIn, typename TOut>
-__global__ void __launch_bounds__(256) rot_kernel(const TIn* __restrict__ x, int cols, int ldx, int rotate, TOut* y,
-                                                  int8_t* qhi, int8_t* qlo, float* qscale, int qld) {
-  __shared__ float red[32];
-  const int row = blockIdx.x;
-  const int T = blockDim.x;
+template <int COLS, typename TIn, typename TOut, bool LN>
+__global__ void __launch_bounds__(256) rows_kernel(const TIn* __restrict__ x, int rows, int ldx,
+                                                   const float* __restrict__ mod, int shift_off, int scale_off,
+                                                   float eps, int rotate, TOut* y, int8_t* qhi, int8_t* qlo,
+                                                   float* qscale, int qld, int act) {
+  constexpr int WPR = COLS > 2048 ? COLS / 2048 : 1;
+  constexpr int G = COLS / 256 / WPR;
+  constexpr int RPC = 8 / WPR;
+  static_assert(G >= 1 && G <= 8 && COLS % 256 == 0, "unsupported row width");
+  __shared__ float red[8];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * RPC + warp / WPR;
+  const int wr = warp % WPR;
+  const bool valid = row < rows;
+  const size_t r = valid ? static_cast<size_t>(row) : 0;
   float v[G][8];
   int col[G];
 #pragma unroll
   for (int g = 0; g < G; ++g) {
-    col[g] = 8 * (threadIdx.x + T * g);
-    load8(x + static_cast<size_t>(row) * ldx + col[g], v[g]);
-    if (rotate) fwht256_warp(v[g]);
+    col[g] = (wr * G + g) * 256 + 8 * lane;
+    if (valid) {
+      load8(x + r * ldx + col[g], v[g]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[g][j] = 0.f;
+    }
+  }
+  if constexpr (LN) {
+    float sum = 0.f;
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) sum += v[g][j];
+    const float mean = row_reduce<WPR>(sum, red, false) / static_cast<float>(COLS);
+    float sq = 0.f;
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float d = v[g][j] - mean;
+        sq += d * d;
+      }
+    const float var = row_reduce<WPR>(sq, red, false) / static_cast<float>(COLS);
+    const float rstd = 1.0f / sqrtf(var + eps);
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float sc[8], sh[8];
+      load8(mod + scale_off + col[g], sc);
+      load8(mod + shift_off + col[g], sh);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[g][j] = (v[g][j] - mean) * rstd * (1.0f + sc[j]) + sh[j];
+    }
+  }
+  if (act == ANIMA_ACT_GELU) {
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[g][j] = gelu_erf(v[g][j]);
+  }
+  if (rotate) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) fwht256_warp(v[g]);
   }
   if (qhi) {
-    quantize_row<G>(v, red, qhi + static_cast<size_t>(row) * qld, qlo ? qlo + static_cast<size_t>(row) * qld : nullptr,
-                    qscale + row, col);
-  } else {
+    float amax = 0.f;
 #pragma unroll
-    for (int g = 0; g < G; ++g) store8(y + static_cast<size_t>(row) * cols + col[g], v[g]);
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[g][j]));
+    amax = row_reduce<WPR>(amax, red, true);
+    if (!valid) return;
+    const float inv = amax > 0.f ? 127.0f / amax : 0.f;
+    if (wr == 0 && lane == 0) qscale[r] = amax > 0.f ? amax / 127.0f : 1.0f;
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      uint32_t h2[2], l2[2];
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t hb = 0, lb = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float a = v[g][4 * half + j] * inv;
+          const float q = rintf(a);
+          const int hv = static_cast<int>(q);
+          const int lv = static_cast<int>(fminf(fmaxf(rintf((a - q) * 254.0f), -127.f), 127.f));
+          hb |= (static_cast<uint32_t>(hv) & 0xFFu) << (8 * j);
+          lb |= (static_cast<uint32_t>(lv) & 0xFFu) << (8 * j);
+        }
+        h2[half] = hb;
+        l2[half] = lb;
+      }
+      *reinterpret_cast<uint2*>(qhi + r * qld + col[g]) = make_uint2(h2[0], h2[1]);
+      if (qlo) *reinterpret_cast<uint2*>(qlo + r * qld + col[g]) = make_uint2(l2[0], l2[1]);
+    }
+  } else if (valid) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) store8(y + r * COLS + col[g], v[g]);
   }
 }
 
@@ -496,41 +495,44 @@ __global__ void __launch_bounds__(256) simt_gemm_kernel(int M, int N, int K, flo
   }
 }
 
+template <typename TIn, typename TOut, bool LN>
+int launch_rows(anima_ctx* ctx, const TIn* x, int rows, int cols, int ldx, const float* mod, int so, int sco,
+                float eps, int rotate, TOut* y, const anima_qact* q, int act = ANIMA_ACT_NONE) {
+  int8_t* hi = q ? q->hi : nullptr;
+  int8_t* lo = q ? q->lo : nullptr;
+  float* sc = q ? q->scale : nullptr;
+  const int qld = q ? q->ld : 0;
+#define ROWS_CASE(C)                                                                                             \
+  case C: {                                                                                                      \
+    constexpr int rpc = 8 / (C > 2048 ? C / 2048 : 1);                                                          \
+    rows_kernel<C, TIn, TOut, LN><<<(rows + rpc - 1) / rpc, 256, 0, ctx->stream>>>(x, rows, ldx, mod, so, sco,   \
+                                                                                  eps, rotate, y, hi, lo, sc, qld, act); \
+    break;                                                                                                       \
+  }
+  switch (cols) {
+    ROWS_CASE(256)
+    ROWS_CASE(512)
+    ROWS_CASE(1024)
+    ROWS_CASE(2048)
+    ROWS_CASE(4096)
+    ROWS_CASE(8192)
+    default:
+      return set_error(ANIMA_ERR_UNSUPPORTED, "row kernel: cols=%d (supported: 256, 512, 1024, 2048, 4096, 8192)", cols);
+  }
+#undef ROWS_CASE
+  return check_launch("rows_kernel");
+}
+
 template <typename TOut>
 int launch_ln(anima_ctx* ctx, const float* x, int rows, int cols, const float* mod, int so, int sco, float eps,
               int rotate, TOut* y, const anima_qact* q) {
-  int8_t* hi = q ? q->hi : nullptr;
-  int8_t* lo = q ? q->lo : nullptr;
-  float* sc = q ? q->scale : nullptr;
-  const int qld = q ? q->ld : 0;
-  switch (cols) {
-    case 256: ln_mod_kernel<1, TOut><<<rows, 32, 0, ctx->stream>>>(x, cols, mod, so, sco, eps, rotate, y, hi, lo, sc, qld); break;
-    case 512: ln_mod_kernel<1, TOut><<<rows, 64, 0, ctx->stream>>>(x, cols, mod, so, sco, eps, rotate, y, hi, lo, sc, qld); break;
-    case 1024: ln_mod_kernel<1, TOut><<<rows, 128, 0, ctx->stream>>>(x, cols, mod, so, sco, eps, rotate, y, hi, lo, sc, qld); break;
-    case 2048: ln_mod_kernel<1, TOut><<<rows, 256, 0, ctx->stream>>>(x, cols, mod, so, sco, eps, rotate, y, hi, lo, sc, qld); break;
-    case 4096: ln_mod_kernel<2, TOut><<<rows, 256, 0, ctx->stream>>>(x, cols, mod, so, sco, eps, rotate, y, hi, lo, sc, qld); break;
-    case 8192: ln_mod_kernel<4, TOut><<<rows, 256, 0, ctx->stream>>>(x, cols, mod, so, sco, eps, rotate, y, hi, lo, sc, qld); break;
-    default: return set_error(ANIMA_ERR_UNSUPPORTED, "layernorm_mod: cols=%d (supported: 256, 512, 1024, 2048, 4096, 8192)", cols);
-  }
-  return check_launch("ln_mod_kernel");
+  return launch_rows<float, TOut, true>(ctx, x, rows, cols, cols, mod, so, sco, eps, rotate, y, q);
 }
 
 template <typename TIn, typename TOut>
-int launch_rot(anima_ctx* ctx, const TIn* x, int rows, int cols, int ldx, int rotate, TOut* y, const anima_qact* q) {
-  int8_t* hi = q ? q->hi : nullptr;
-  int8_t* lo = q ? q->lo : nullptr;
-  float* sc = q ? q->scale : nullptr;
-  const int qld = q ? q->ld : 0;
-  switch (cols) {
-    case 256: rot_kernel<1, TIn, TOut><<<rows, 32, 0, ctx->stream>>>(x, cols, ldx, rotate, y, hi, lo, sc, qld); break;
-    case 512: rot_kernel<1, TIn, TOut><<<rows, 64, 0, ctx->stream>>>(x, cols, ldx, rotate, y, hi, lo, sc, qld); break;
-    case 1024: rot_kernel<1, TIn, TOut><<<rows, 128, 0, ctx->stream>>>(x, cols, ldx, rotate, y, hi, lo, sc, qld); break;
-    case 2048: rot_kernel<1, TIn, TOut><<<rows, 256, 0, ctx->stream>>>(x, cols, ldx, rotate, y, hi, lo, sc, qld); break;
-    case 4096: rot_kernel<2, TIn, TOut><<<rows, 256, 0, ctx->stream>>>(x, cols, ldx, rotate, y, hi, lo, sc, qld); break;
-    case 8192: rot_kernel<4, TIn, TOut><<<rows, 256, 0, ctx->stream>>>(x, cols, ldx, rotate, y, hi, lo, sc, qld); break;
-    default: return set_error(ANIMA_ERR_UNSUPPORTED, "rotate: cols=%d (supported: 256, 512, 1024, 2048, 4096, 8192)", cols);
-  }
-  return check_launch("rot_kernel");
+int launch_rot(anima_ctx* ctx, const TIn* x, int rows, int cols, int ldx, int rotate, TOut* y, const anima_qact* q,
+               int act = ANIMA_ACT_NONE) {
+  return launch_rows<TIn, TOut, false>(ctx, x, rows, cols, ldx, nullptr, 0, 0, 0.f, rotate, y, q, act);
 }
 
 inline bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
@@ -590,24 +592,31 @@ int anima_rotate(anima_ctx* ctx, const void* x, int in_dtype, int rows, int cols
 }
 
 static int rot_quant(anima_ctx* ctx, const void* x, int in_dtype, int rows, int cols, int ldx, const anima_qact* out,
-                     int rotate, const char* who) {
+                     int rotate, const char* who, int act = ANIMA_ACT_NONE) {
   ANIMA_REQUIRE(ctx && x, "%s: NULL argument", who);
   ANIMA_REQUIRE(rows > 0 && ldx >= cols && al16(x), "%s: bad shape or alignment", who);
   int st = check_qact(out, rows, cols, who);
   if (st) return st;
   const int esz = in_dtype == ANIMA_F32 ? 4 : 2;
   ANIMA_REQUIRE((static_cast<long long>(ldx) * esz) % 16 == 0, "%s: ldx must give 16-byte aligned rows", who);
-  ProfScope prof(ctx, rotate ? "hadamard+quant" : "quant", 0, rows * (double)cols * (esz + (out->lo ? 2 : 1)));
+  ANIMA_REQUIRE(act == ANIMA_ACT_NONE || act == ANIMA_ACT_GELU, "%s: act %d (none or gelu)", who, act);
+  ProfScope prof(ctx, act ? "gelu+hadamard+quant" : rotate ? "hadamard+quant" : "quant", 0,
+                 rows * (double)cols * (esz + (out->lo ? 2 : 1)));
   switch (in_dtype) {
-    case ANIMA_F32: return launch_rot<float, float>(ctx, (const float*)x, rows, cols, ldx, rotate, nullptr, out);
-    case ANIMA_BF16: return launch_rot<__nv_bfloat16, float>(ctx, (const __nv_bfloat16*)x, rows, cols, ldx, rotate, nullptr, out);
-    case ANIMA_F16: return launch_rot<__half, float>(ctx, (const __half*)x, rows, cols, ldx, rotate, nullptr, out);
+    case ANIMA_F32: return launch_rot<float, float>(ctx, (const float*)x, rows, cols, ldx, rotate, nullptr, out, act);
+    case ANIMA_BF16: return launch_rot<__nv_bfloat16, float>(ctx, (const __nv_bfloat16*)x, rows, cols, ldx, rotate, nullptr, out, act);
+    case ANIMA_F16: return launch_rot<__half, float>(ctx, (const __half*)x, rows, cols, ldx, rotate, nullptr, out, act);
   }
   return set_error(ANIMA_ERR_ARG, "%s: in_dtype %d", who, in_dtype);
 }
 
 int anima_rotate_quant(anima_ctx* ctx, const void* x, int in_dtype, int rows, int cols, int ldx, const anima_qact* out) {
   return rot_quant(ctx, x, in_dtype, rows, cols, ldx, out, 1, "anima_rotate_quant");
+}
+
+int anima_act_rotate_quant(anima_ctx* ctx, const void* x, int in_dtype, int rows, int cols, int ldx, int act,
+                           const anima_qact* out) {
+  return rot_quant(ctx, x, in_dtype, rows, cols, ldx, out, 1, "anima_act_rotate_quant", act);
 }
 
 int anima_quant_rows(anima_ctx* ctx, const void* x, int in_dtype, int rows, int cols, int ldx, const anima_qact* out) {

@@ -186,6 +186,29 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// tcgen05.wait::ld that also "redefines" the 32 destination registers of an earlier tcgen05.ld,
+// so the compiler cannot schedule any use of them before the wait.
+__device__ __forceinline__ void tmem_ld_wait(uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.wait::ld.sync.aligned;"
+      : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+        "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]),
+        "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]),
+        "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+      :
+      : "memory");
+}
+
+// Per-warpgroup register budget (all four warps of the warpgroup execute it).
+template <int N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // Shared-memory matrix descriptor for a SWIZZLE_128B canonical layout (sm_100 encoding):
 // start address, leading/stride byte offsets (16-byte units), version 1, layout type 2.
 __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
@@ -219,8 +242,31 @@ __device__ __forceinline__ bool elect_lane0() { return (threadIdx.x & 31) == 0; 
 
 // ------------------------------------------------------------------ small math
 
-// Exact-erf GELU, as the reference's F.gelu (tools/reference.py:242); erff is CUDA's.
-__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
+// int32 -> fp32, correctly rounded (same result as cvt.rn.f32.s32) but on the integer and FMA
+// pipes instead of the conversion unit: v = hi * 2^16 + lo with lo in [0, 2^16); each half is
+// placed in the mantissa of a float whose ulp is 1 (magic-number construction) and recovered
+// exactly by one subtraction; the final fma rounds once.
+__device__ __forceinline__ float i2f_rn(int v) {
+  const int hi = v >> 16;                       // |hi| < 2^15
+  const unsigned lo = static_cast<unsigned>(v) & 0xFFFFu;
+  const float fh = __int_as_float(0x4B400000 + hi) - 12582912.0f;           // 1.5 * 2^23
+  const float fl = __uint_as_float(0x4B000000u | lo) - 8388608.0f;          // 2^23
+  return fmaf(fh, 65536.0f, fl);
+}
+
+// GELU(x) = x/2 (1 + erf(x / sqrt 2)), erf by Abramowitz & Stegun 7.1.26 (|error| <= 1.5e-7):
+// erf(a) = 1 - (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) e^{-a^2}, t = 1 / (1 + p a), a >= 0.
+// The reference's own GPU kernels use the same approximation (app/gpu/gemm.js:25-35); its PyTorch
+// oracle uses exact erf, which this matches to ~1e-7.
+__device__ __forceinline__ float gelu_erf(float x) {
+  const float z = x * 0.70710678118654752f;
+  const float a = fabsf(z);
+  const float t = __fdividef(1.0f, fmaf(0.3275911f, a, 1.0f));
+  const float poly = fmaf(fmaf(fmaf(fmaf(1.061405429f, t, -1.453152027f), t, 1.421413741f), t, -0.284496736f), t,
+                          0.254829592f) * t;
+  const float erf_abs = 1.0f - poly * __expf(-a * a);
+  return 0.5f * x * (1.0f + copysignf(erf_abs, z));
+}
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
 
 }  // namespace anima

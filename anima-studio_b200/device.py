@@ -30,7 +30,7 @@ EXPORTS = [
     "anima_ctx_create", "anima_ctx_destroy", "anima_ctx_set_stream", "anima_sync", "anima_last_error",
     "anima_alloc", "anima_free", "anima_upload", "anima_download", "anima_profile_report", "anima_version",
     "anima_unpack_w4", "anima_linear", "anima_matmul", "anima_lora_down", "anima_layernorm_mod", "anima_layernorm_mod_quant",
-    "anima_rotate", "anima_rotate_quant", "anima_quant_rows", "anima_rmsnorm", "anima_qk_norm_rope", "anima_rope",
+    "anima_rotate", "anima_rotate_quant", "anima_act_rotate_quant", "anima_quant_rows", "anima_rmsnorm", "anima_qk_norm_rope", "anima_rope",
     "anima_attention", "anima_elementwise", "anima_zero", "anima_patchify", "anima_unpatchify",
     "anima_timestep_embedding", "anima_euler_step",
 ]
@@ -100,6 +100,7 @@ def load_library(path: str = LIB_PATH):
             "anima_rotate": [vp, vp, i, i, i, i, vp, i],
             "anima_rotate_quant": [vp, vp, i, i, i, i, C.POINTER(QAct)],
             "anima_quant_rows": [vp, vp, i, i, i, i, C.POINTER(QAct)],
+            "anima_act_rotate_quant": [vp, vp, i, i, i, i, i, C.POINTER(QAct)],
             "anima_rmsnorm": [vp, vp, i, i, i, vp, f, vp, i],
             "anima_qk_norm_rope": [vp, vp, i, i, i, i, i, vp, vp, vp, i, f],
             "anima_rope": [vp, vp, i, i, i, i, i, i, vp, i],

@@ -76,12 +76,17 @@ def rotate(x: torch.Tensor) -> torch.Tensor:
     return y.view(x.shape)
 
 
-def rotate_quant(x: torch.Tensor, planes: int = 2, out: QuantRows | None = None) -> QuantRows:
-    """rotate() fused with per-token quantization (input fp32/bf16/fp16 rows)."""
+def rotate_quant(x: torch.Tensor, planes: int = 2, out: QuantRows | None = None, act: str | None = None) -> QuantRows:
+    """rotate() fused with per-token quantization (input fp32/bf16/fp16 rows); act="gelu" applies
+    the MLP activation first (for a layer1 GEMM that stored its pre-activation)."""
     _contig_rows(x)
     q = out or QuantRows.empty(x.shape[0], x.shape[1], planes, x.device)
     qa = q.c()
-    ctx_for(x).call("anima_rotate_quant", ptr(x), _dt(x), x.shape[0], x.shape[1], x.stride(0), C.byref(qa))
+    if act:
+        ctx_for(x).call("anima_act_rotate_quant", ptr(x), _dt(x), x.shape[0], x.shape[1], x.stride(0), dev.ACT[act],
+                        C.byref(qa))
+    else:
+        ctx_for(x).call("anima_rotate_quant", ptr(x), _dt(x), x.shape[0], x.shape[1], x.stride(0), C.byref(qa))
     return q
 
 

@@ -201,8 +201,82 @@ def measure_int8_peak(torch):
     return 2.0 * n ** 3 / (best * 1e-3) / 1e12
 
 
+def kernel_case(args):
+    """One kernel of the 1024^2 workload in isolation (for ncu captures and kernel timing):
+    mlp1  the 2048->8192 block linear (M=4096, two activation planes, GELU, fp16 out)
+    mlp2  the 8192->2048 block linear with the gated residual
+    qkv   the 2048->6144 qkv linear with the per-head RMSNorm + RoPE epilogue
+    attn  self-attention, 16 heads x 4096 tokens x d=128 (fp16 q/k/v in the qkv layout)
+    ln    LayerNorm + adaLN + ConvRot + two-plane quantization of [4096, 2048]"""
+    import torch
+
+    syn, ditm, ops, W = pkg("synthetic"), pkg("dit"), pkg("ops"), pkg("weights")
+    dev = pkg("device")
+    torch.manual_seed(0)
+    M = 4096
+    planes = 2 if args.precision == "a16" else 1
+
+    def lin(N, K):
+        q = torch.randint(-127, 128, (N, K), dtype=torch.int8, device="cuda")
+        return W.Linear("i8", N, K, q, torch.full((N,), 1e-3, device="cuda"))
+
+    if args.kernel in ("mlp1", "mlp2", "qkv"):
+        N, K = {"mlp1": (8192, 2048), "mlp2": (2048, 8192), "qkv": (6144, 2048)}[args.kernel]
+        w = lin(N, K)
+        qa = ops.rotate_quant(torch.randn(M, K, device="cuda"), planes)
+        if args.kernel == "mlp1":
+            out = torch.empty(M, N, dtype=torch.float16 if args.out == "f16" else torch.float32, device="cuda")
+            act = None if args.act == "none" else args.act
+            fn = lambda: ops.linear(qa, w, out=out, act=act)  # noqa: E731
+        elif args.kernel == "mlp2":
+            out = torch.zeros(M, N, device="cuda")
+            gate = torch.randn(6144, device="cuda")
+            fn = lambda: ops.linear(qa, w, out=out, resid=True, gate=gate, g_off=4096)  # noqa: E731
+        else:
+            out = torch.empty(M, N, dtype=torch.float16, device="cuda")
+            nq, nk = torch.ones(128, device="cuda"), torch.ones(128, device="cuda")
+            cs = torch.from_numpy(ditm.rope_table(64, 64)).cuda()
+            fn = lambda: ops.linear(qa, w, out=out, mode="qkv", qk=(nq, nk), rope_cs=cs, n_q=2048)  # noqa: E731
+        work, unit = 2.0 * M * N * K, "TOPS"
+    elif args.kernel == "attn":
+        dt = torch.float16 if args.attn == "f16" else torch.bfloat16
+        qkv = torch.randn(M, 6144, device="cuda").to(dt)
+        out = torch.empty(M, 2048, dtype=dt, device="cuda")
+        fn = lambda: ops.attention(qkv, qkv, qkv, Lq=M, Lk=M, H=16, ldq=6144, ldk=6144, ldv=6144, q_off=0,  # noqa: E731
+                                   k_off=2048, v_off=4096, out=out)
+        work, unit = 4.0 * M * M * 128 * 16, "TFLOP/s"
+    elif args.kernel == "ln":
+        x = torch.randn(M, 2048, device="cuda")
+        mod = torch.randn(6144, device="cuda") * 0.5
+        q = ops.QuantRows.empty(M, 2048, planes, "cuda")
+        fn = lambda: ops.layernorm_mod_quant(x, mod, 0, 2048, 2048, out=q)  # noqa: E731
+        work, unit = M * 2048 * (4 + planes) + M * 4, "GB/s"
+    else:
+        raise SystemExit(f"unknown kernel case {args.kernel}")
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(args.reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        e1.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    dev.Context.get(0).sync()
+    ms = statistics.median(ts)
+    rate = work / (ms * 1e-3) / (1e9 if unit == "GB/s" else 1e12)
+    print(json.dumps({"kernel": args.kernel, "precision": args.precision, "attn": args.attn, "ms_median": ms,
+                      "ms_min": min(ts), "rate": rate, "unit": unit, "reps": args.reps}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--kernel", default=None, help="time one kernel case instead (mlp1|mlp2|qkv|attn|ln)")
+    ap.add_argument("--reps", type=int, default=20)
+    ap.add_argument("--act", default="gelu", help="kernel case mlp1: epilogue activation (gelu|none)")
+    ap.add_argument("--out", default="f16", help="kernel case mlp1: output dtype (f16|f32)")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=16)
     ap.add_argument("--warmup", type=int, default=3)
@@ -213,6 +287,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     args = ap.parse_args()
     world, rank, local = setup_dist()
+    if args.kernel:
+        return kernel_case(args)
     if args.impl == "reference":
         return run_reference(args, world, rank)
 

@@ -156,6 +156,10 @@ int anima_layernorm_mod_quant(anima_ctx* ctx, const float* x, int rows, int cols
 int anima_rotate(anima_ctx* ctx, const void* x, int in_dtype, int rows, int cols, int ldx, void* y, int out_dtype);
 /* ops.rotate fused with per-token quantization into anima_qact (input F32/BF16/F16). */
 int anima_rotate_quant(anima_ctx* ctx, const void* x, int in_dtype, int rows, int cols, int ldx, const anima_qact* out);
+/* Activation (GELU) then ConvRot then per-token quantization: the MLP hidden between layer1 (which
+ * stores its pre-activation) and layer2 (dit.js:308-310, reference.py:242). act: ANIMA_ACT_NONE/GELU. */
+int anima_act_rotate_quant(anima_ctx* ctx, const void* x, int in_dtype, int rows, int cols, int ldx, int act,
+                           const anima_qact* out);
 /* Per-token quantization without rotation (input already rotated). */
 int anima_quant_rows(anima_ctx* ctx, const void* x, int in_dtype, int rows, int cols, int ldx, const anima_qact* out);
 /* ops.rmsnorm (ops.js:111-117): y = x * rsqrt(mean(x^2) + eps) * w over rows of `cols`. */

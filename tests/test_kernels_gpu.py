@@ -94,6 +94,14 @@ def test_rotate_quant(ops, cols, dtype):
     assert rel_l2(q.dequant().cpu().numpy(), ref) < 6e-5
 
 
+def test_gelu_rotate_quant(ops):
+    """GELU -> ConvRot -> per-token quant of an fp16 MLP pre-activation [rows, 8192]."""
+    x = (randn((77, 8192), 47) * 3).to(torch.float16)
+    q = ops.rotate_quant(x.to(DEV), act="gelu")
+    ref = oracle.rotate(oracle.gelu(x.float().numpy()))
+    assert rel_l2(q.dequant().cpu().numpy(), ref) < 6e-5
+
+
 def test_rotate_plain(ops):
     x = randn((64, 2048), 6)
     y = ops.rotate(x.to(DEV)).cpu().numpy()
