@@ -1,18 +1,21 @@
 // Non-causal multi-head attention on tcgen05 (kind::f16), head_dim 128: the DiT's self-attention
 // (Lq = Lk = 4096 at 1024^2) and cross-attention against cached text keys (Lk = 256..512). The
-// reference's counterpart is the fp32 WGSL flash kernel of app/gpu/kernels.js:147-299; this one
-// keeps S = QK^T and O_j = P_j V_j in TMEM and does the online softmax in fp32 registers.
+// reference's counterpart is the fp32 WGSL flash kernel of app/gpu/kernels.js:147-299.
 //
-// One CTA = one (batch, head, 128-query tile); 192 threads:
-//   warp 0      TMA producer: Q once, then K_j / V_j tiles (128 keys) into two stages each
-//   warp 1      TMEM allocator + single-thread UMMA issuer:
-//                 S_j = Q K_j^T (M=128, N=128, K=16 x 8)   into S[j % 2]   (TMEM cols 0 / 128)
-//                 O_j = P_j V_j (M=128, N=128, K=16 x 8)   into O[j % 2]   (TMEM cols 256 / 384)
-//               issued as S_0, S_1, PV_0, S_2, PV_1, ... so QK^T of block j+1 overlaps softmax j.
-//   warps 2..5  softmax, one query row per thread: row max and exp2 of S_j, P_j (16-bit) into
-//               shared memory in the SWIZZLE_128B K-major layout, running sum l; O accumulated in
-//               registers one block behind (O = O * 2^(m_{j-1} - m_j) + O_j), normalised by l.
-// Keys >= key_len[b] (and >= Lk) get probability 0; key blocks entirely past key_len are skipped.
+// One CTA = one (batch, head) and two 128-query tiles A and B; 320 threads:
+//   warps 0-3   softmax for tile A, warps 4-7 for tile B: one query row per thread
+//   warp 8      TMA producer: Q_A, Q_B once, then K_j / V_j (128 keys) into two stages each
+//   warp 9      TMEM allocator + single-thread UMMA issuer
+// Tensor memory (512 columns): S_A [0,128) S_B [128,256) O_A [256,384) O_B [384,512).
+// Per key block j the tensor core runs S_X = Q_X K_j^T (smem x smem), the softmax threads read S_X,
+// write P_X = 2^(s - m) as 16-bit values back over the first 64 columns of S_X, and the tensor core
+// accumulates O_X += P_X V_j with P_X read from tensor memory. Issue order:
+//   S_A(0) S_B(0) | PV_A(j) PV_B(j) [wait PV_A(j)] S_A(j+1) [wait PV_B(j)] S_B(j+1) | ...
+// so S_X(j+1) never overwrites P_X(j) before PV_X(j) has read it, and while one tile's softmax
+// runs the tensor core works on the other tile. O stays in tensor memory; the running max is only
+// moved (and O rescaled in place) when it grows by more than 2^8, so P stays <= 256 in between
+// (lazy rescaling), and l is kept consistent with the max actually used. Keys >= key_len[b] (and
+// >= Lk) get probability 0; key blocks entirely past key_len are skipped.
 
 #include "internal.h"
 #include "sm100.cuh"
@@ -20,21 +23,21 @@
 namespace anima {
 namespace attn {
 
-constexpr int TILE = 128;     // query rows per CTA and keys per block
+constexpr int TILE = 128;     // query rows per tile and keys per block
 constexpr int HD = 128;       // head dim
-constexpr int THREADS = 192;
+constexpr int THREADS = 320;
 constexpr int ATOM = 16384;   // one SWIZZLE_128B atom column: 128 rows x 128 bytes
 constexpr int TILE_BYTES = 2 * ATOM;
-// shared memory: Q | K[2] | V[2] | P[2] | barriers
+// shared memory: Q_A | Q_B | K[2] | V[2] | barriers
 constexpr int OFF_Q = 0;
-constexpr int OFF_K = OFF_Q + TILE_BYTES;
+constexpr int OFF_K = OFF_Q + 2 * TILE_BYTES;
 constexpr int OFF_V = OFF_K + 2 * TILE_BYTES;
-constexpr int OFF_P = OFF_V + 2 * TILE_BYTES;
-constexpr int OFF_BAR = OFF_P + 2 * TILE_BYTES;
+constexpr int OFF_BAR = OFF_V + 2 * TILE_BYTES;
 constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O when the max grows by > 2^8
 
 struct Params {
-  int Lq, Lk, heads, q_tiles;
+  int Lq, Lk, heads, q_pairs;
   int q_col, k_col, v_col;  // column offsets of head 0
   void* out;
   long long ldo, o_bstride;
@@ -48,6 +51,21 @@ __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// 2^x on the FMA/ALU pipes, to take part of the softmax's exponentials off the MUFU unit (its
+// bottleneck): x = n + f with n = rne(x) by the 1.5 * 2^23 magic-number rounding and f in
+// [-1/2, 1/2]; 2^f by a degree-4 polynomial (coefficients fitted here by relative least squares on
+// 4000 Chebyshev nodes of [-1/2, 1/2]; max relative error 2.7e-6, far below the 16-bit rounding of
+// P); n is added to the exponent field. Valid for -125 <= x <= 125; callers pass x <= 8 and clamp.
+__device__ __forceinline__ float exp2_fma(float x) {
+  x = fmaxf(x, -125.0f);
+  const float t = x + 12582912.0f;
+  const int n = __float_as_int(t) - 0x4B400000;
+  const float f = x - (t - 12582912.0f);
+  const float p = fmaf(fmaf(fmaf(fmaf(0.009560510516f, f, 0.05591703951f), f, 0.2402498126f), f, 0.6931219697f), f,
+                       0.9999991655f);
+  return __int_as_float(__float_as_int(p) + (n << 23));
 }
 
 template <bool BF16>
@@ -67,7 +85,8 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
-template <bool BF16>
+// EMU: how many of every 4 exponentials run on the FMA pipes (exp2_fma) instead of MUFU.
+template <bool BF16, int EMU>
 __global__ void __launch_bounds__(THREADS, 1)
     attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                      const __grid_constant__ CUtensorMap tm_v, const Params p) {
@@ -79,25 +98,23 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* k_empty = bars + 3;  // [2]
   uint64_t* v_full = bars + 5;   // [2]
   uint64_t* v_empty = bars + 7;  // [2]
-  uint64_t* s_full = bars + 9;   // [2]
-  uint64_t* s_empty = bars + 11; // [2]
-  uint64_t* p_full = bars + 13;  // [2]
-  uint64_t* o_full = bars + 15;  // [2]
-  uint64_t* o_empty = bars + 17; // [2]
-  uint64_t* drain = bars + 19;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
+  uint64_t* s_full = bars + 9;   // [2] per tile: S_X(j) complete
+  uint64_t* p_full = bars + 11;  // [2] per tile: P_X(j) written (4 warp arrivals)
+  uint64_t* o_done = bars + 13;  // [2] per tile: PV_X(j) complete
+  uint64_t* drain = bars + 15;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qt = blockIdx.x % p.q_tiles;
-  const int bh = blockIdx.x / p.q_tiles;
+  const int qp = blockIdx.x % p.q_pairs;
+  const int bh = blockIdx.x / p.q_pairs;
   const int h = bh % p.heads;
   const int b = bh / p.heads;
-  const int q0 = qt * TILE;
-  int kv_len = p.Lk;
+  const int q0 = qp * 2 * TILE;
   const int kvb = p.kv_bcast ? 0 : b;
+  int kv_len = p.Lk;
   if (p.key_len) kv_len = min(kv_len, p.key_len[kvb]);
-  const int nblk = (kv_len + TILE - 1) / TILE;
+  const int nblk = kv_len > 0 ? (kv_len + TILE - 1) / TILE : 0;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -107,16 +124,15 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], 4);
       mbar_init(&p_full[i], 4);
-      mbar_init(&o_full[i], 1);
-      mbar_init(&o_empty[i], 4);
+      mbar_init(&o_done[i], 1);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 1) {
+  constexpr int kProducerWarp = 8, kMmaWarp = 9;
+  if (warp == kMmaWarp) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
@@ -125,16 +141,18 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
-    if (lane == 0) {
+  if (warp == kProducerWarp) {
+    if (lane == 0 && nblk > 0) {
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
       const int qc = p.q_col + h * HD, kc = p.k_col + h * HD, vc = p.v_col + h * HD;
       int armed[5] = {-1, -1, -1, -1, -1};  // parity of the last arm: q, k0, k1, v0, v1
-      mbar_arrive_expect_tx(q_full, TILE_BYTES);
+      mbar_arrive_expect_tx(q_full, 2 * TILE_BYTES);
       tma_load_3d(smem + OFF_Q, &tm_q, q_full, qc, q0, b);
       tma_load_3d(smem + OFF_Q + ATOM, &tm_q, q_full, qc + 64, q0, b);
+      tma_load_3d(smem + OFF_Q + TILE_BYTES, &tm_q, q_full, qc, q0 + TILE, b);
+      tma_load_3d(smem + OFF_Q + TILE_BYTES + ATOM, &tm_q, q_full, qc + 64, q0 + TILE, b);
       armed[0] = 0;
       for (int j = 0; j < nblk; ++j) {
         const int st = j & 1;
@@ -164,49 +182,66 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
     }
-  } else if (warp == 1) {
-    if (lane == 0) {
+  } else if (warp == kMmaWarp) {
+    if (lane == 0 && nblk > 0) {
       const uint32_t id_qk = idesc_f16(TILE, TILE, BF16, false);
       const uint32_t id_pv = idesc_f16(TILE, HD, BF16, true);
       const uint32_t sq = smem_u32(smem + OFF_Q);
-      bool ok = mbar_wait(q_full, 0, abort_flag, kErrTimeoutFull);
-      auto issue_pv = [&](int i) -> bool {
-        const int st = i & 1;
-        const uint32_t ph = (i >> 1) & 1;
-        if (!mbar_wait(&p_full[st], ph, abort_flag, kErrTimeoutFull)) return false;
-        if (!mbar_wait(&v_full[st], ph, abort_flag, kErrTimeoutFull)) return false;
-        if (!mbar_wait(&o_empty[st], ph ^ 1, abort_flag, kErrTimeoutAcc)) return false;
-        tc_fence_after();
-        const uint32_t sp = smem_u32(smem + OFF_P + st * TILE_BYTES);
-        const uint32_t sv = smem_u32(smem + OFF_V + st * TILE_BYTES);
-#pragma unroll
-        for (int k = 0; k < TILE / 16; ++k) {
-          const uint64_t ad = sdesc_sw128(sp + (k >> 2) * ATOM + (k & 3) * 32, 16, 1024);
-          const uint64_t bd = sdesc_sw128(sv + k * 16 * 128, ATOM, 1024);
-          umma_f16(tmem + 256 + st * 128, ad, bd, id_pv, k > 0 ? 1u : 0u);
-        }
-        umma_commit(&v_empty[st]);
-        umma_commit(&o_full[st]);
-        return true;
-      };
-      for (int j = 0; ok && j < nblk; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(&k_full[st], ph, abort_flag, kErrTimeoutFull)) { ok = false; break; }
-        if (!mbar_wait(&s_empty[st], ph ^ 1, abort_flag, kErrTimeoutAcc)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t sk = smem_u32(smem + OFF_K + st * TILE_BYTES);
+      auto issue_s = [&](int x, int j) {  // S_x(j) = Q_x K_j^T
+        const uint32_t sk = smem_u32(smem + OFF_K + (j & 1) * TILE_BYTES);
+        const uint32_t qx = sq + x * TILE_BYTES;
 #pragma unroll
         for (int k = 0; k < HD / 16; ++k) {
           const uint32_t off = (k >> 2) * ATOM + (k & 3) * 32;
-          umma_f16(tmem + st * 128, sdesc_sw128(sq + off, 16, 1024), sdesc_sw128(sk + off, 16, 1024), id_qk,
+          umma_f16(tmem + x * 128, sdesc_sw128(qx + off, 16, 1024), sdesc_sw128(sk + off, 16, 1024), id_qk,
                    k > 0 ? 1u : 0u);
         }
-        umma_commit(&k_empty[st]);
-        umma_commit(&s_full[st]);
-        if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
+        umma_commit(&s_full[x]);
+      };
+      auto issue_pv = [&](int x, int j) {  // O_x (+)= P_x(j) V_j, P from tensor memory
+        const uint32_t sv = smem_u32(smem + OFF_V + (j & 1) * TILE_BYTES);
+#pragma unroll
+        for (int k = 0; k < TILE / 16; ++k) {
+          const uint64_t bd = sdesc_sw128(sv + k * 16 * 128, ATOM, 1024);
+          umma_f16_ts(tmem + 256 + x * 128, tmem + x * 128 + k * 8, bd, id_pv, (j > 0 || k > 0) ? 1u : 0u);
+        }
+        umma_commit(&o_done[x]);
+      };
+      bool ok = mbar_wait(q_full, 0, abort_flag, kErrTimeoutFull) &&
+                mbar_wait(&k_full[0], 0, abort_flag, kErrTimeoutFull);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0);
+        issue_s(1, 0);
+        umma_commit(&k_empty[0]);
       }
-      if (ok && nblk > 0) ok = issue_pv(nblk - 1);
+      // Per tile: PV_x(j) as soon as P_x(j) is written, then (once PV_x(j) has read P_x(j), which
+      // lives in S_x's columns) S_x(j+1). The two tiles are serviced alternately, so one tile's
+      // softmax runs while the tensor core works on the other tile.
+      for (int j = 0; ok && j < nblk; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        const uint32_t jp = j & 1;
+        if (!mbar_wait(&v_full[st], ph, abort_flag, kErrTimeoutFull)) { ok = false; break; }
+        const bool more = j + 1 < nblk;
+        const int st1 = (j + 1) & 1;
+        for (int x = 0; x < 2; ++x) {
+          if (!mbar_wait(&p_full[x], jp, abort_flag, kErrTimeoutFull)) { ok = false; break; }
+          tc_fence_after();
+          issue_pv(x, j);
+          if (x == 1) umma_commit(&v_empty[st]);
+          if (more) {
+            if (x == 0 && !mbar_wait(&k_full[st1], ((j + 1) >> 1) & 1, abort_flag, kErrTimeoutFull)) {
+              ok = false;
+              break;
+            }
+            if (!mbar_wait(&o_done[x], jp, abort_flag, kErrTimeoutAcc)) { ok = false; break; }
+            tc_fence_after();
+            issue_s(x, j + 1);
+            if (x == 1) umma_commit(&k_empty[st1]);
+          }
+        }
+      }
       if (*abort_flag) {
         umma_commit(drain);
         const unsigned long long t0 = globaltimer();
@@ -219,138 +254,154 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
     }
   } else {
+    // softmax: tile x = warp / 4, row = (warp % 4) * 32 + lane
+    const int x = warp >> 2;
     const int quad = warp & 3;
     const int row = quad * 32 + lane;
     const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
-    float o[HD];
-#pragma unroll
-    for (int c = 0; c < HD; ++c) o[c] = 0.f;
-    float m_prev = -INFINITY;  // running max (log2 domain) after the previous block
-    float m_lag = -INFINITY;   // max of the block whose O_j is accumulated next
-    float m_acc = -INFINITY;   // max the register O is currently relative to
+    const uint32_t s_addr = tmem + lane_addr + x * 128;
+    const uint32_t o_addr = tmem + lane_addr + 256 + x * 128;
+    float m_used = -INFINITY;  // max the probabilities (and O, l) are relative to
     float l = 0.f;
     bool ok = true;
-
-    auto accumulate = [&](int i, float m_i) -> bool {
-      const int st = i & 1;
-      const uint32_t ph = (i >> 1) & 1;
-      if (!warp_wait(&o_full[st], ph, abort_flag, kErrTimeoutAcc)) return false;
-      tc_fence_after();
-      const float alpha = (m_acc == -INFINITY) ? 0.f : ex2(m_acc - m_i);
-#pragma unroll
-      for (int c = 0; c < HD; c += 32) {
-        uint32_t r[32];
-        tmem_ld32(tmem + lane_addr + 256 + st * 128 + c, r);
-        tmem_ld_wait();
-#pragma unroll
-        for (int t = 0; t < 32; ++t) o[c + t] = fmaf(o[c + t], alpha, __uint_as_float(r[t]));
-      }
-      m_acc = m_i;
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&o_empty[st]);
-      return true;
-    };
-
-    uint8_t* prow_base = smem + OFF_P + row * 128;
     for (int j = 0; j < nblk; ++j) {
-      const int st = j & 1;
-      const uint32_t ph = (j >> 1) & 1;
-      if (!warp_wait(&s_full[st], ph, abort_flag, kErrTimeoutFull)) { ok = false; break; }
+      const uint32_t jp = j & 1;
+      if (!warp_wait(&s_full[x], jp, abort_flag, kErrTimeoutFull)) { ok = false; break; }
       tc_fence_after();
-      const uint32_t s_addr = tmem + lane_addr + st * 128;
+      uint32_t sr[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(s_addr + 32 * c, sr[c]);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld_wait(sr[c]);
       const int kbase = j * TILE;
-      // pass 1: row max
+      const bool masked = kbase + TILE > kv_len;  // only the last block can hold keys past kv_len
       float mx = -INFINITY;
+      if (masked) {
 #pragma unroll
-      for (int c = 0; c < TILE; c += 32) {
-        uint32_t r[32];
-        tmem_ld32(s_addr + c, r);
-        tmem_ld_wait();
+        for (int c = 0; c < 4; ++c)
 #pragma unroll
-        for (int t = 0; t < 32; ++t) {
-          const float s = (kbase + c + t < kv_len) ? __uint_as_float(r[t]) * p.scale_log2 : -INFINITY;
-          mx = fmaxf(mx, s);
-        }
+          for (int t = 0; t < 32; ++t)
+            if (kbase + 32 * c + t >= kv_len) sr[c][t] = __float_as_uint(-INFINITY);
       }
-      const float m_new = fmaxf(m_prev, mx);
-      // pass 2: probabilities -> shared memory (16-bit, SWIZZLE_128B K-major), row sum
-      float rs = 0.f;
-      uint8_t* prow = prow_base + st * TILE_BYTES;
+      {  // eight independent partial maxima (short dependency chains)
+        float pm[8];
 #pragma unroll
-      for (int c = 0; c < TILE; c += 32) {
-        uint32_t r[32];
-        tmem_ld32(s_addr + c, r);
-        tmem_ld_wait();
+        for (int i = 0; i < 8; ++i) pm[i] = -INFINITY;
 #pragma unroll
-        for (int t = 0; t < 32; ++t) {
-          const bool valid = kbase + c + t < kv_len;
-          const float e = valid ? ex2(fmaf(__uint_as_float(r[t]), p.scale_log2, -m_new)) : 0.f;
-          rs += e;
-          r[t] = __float_as_uint(e);
-        }
-        // 32 keys = 4 chunks of 8; chunk index within the 64-key atom: (c % 64) / 8 + q
+        for (int c = 0; c < 4; ++c)
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int key0 = c + 8 * q;
-          const int atom = key0 >> 6;
-          const int chunk = (key0 & 63) >> 3;
-          uint4 u;
-          u.x = pack2<BF16>(__uint_as_float(r[8 * q + 0]), __uint_as_float(r[8 * q + 1]));
-          u.y = pack2<BF16>(__uint_as_float(r[8 * q + 2]), __uint_as_float(r[8 * q + 3]));
-          u.z = pack2<BF16>(__uint_as_float(r[8 * q + 4]), __uint_as_float(r[8 * q + 5]));
-          u.w = pack2<BF16>(__uint_as_float(r[8 * q + 6]), __uint_as_float(r[8 * q + 7]));
-          *reinterpret_cast<uint4*>(prow + atom * ATOM + ((chunk ^ (row & 7)) << 4)) = u;
-        }
+          for (int t = 0; t < 32; ++t) pm[t & 7] = fmaxf(pm[t & 7], __uint_as_float(sr[c][t]));
+        mx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])), fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
       }
-      tc_fence_before();
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&s_empty[st]);
-        mbar_arrive(&p_full[st]);
+      mx *= p.scale_log2;
+      // lazy rescale: keep the old max unless the new one is more than 2^8 larger
+      float alpha = 1.f;
+      bool rescale = false;
+      if (mx > m_used + kRescaleThreshold) {
+        rescale = j > 0;
+        alpha = (m_used == -INFINITY) ? 0.f : ex2(m_used - mx);
+        m_used = mx;
       }
-      l = (m_prev == -INFINITY ? 0.f : l * ex2(m_prev - m_new)) + rs;
-      if (j >= 1 && !accumulate(j - 1, m_lag)) { ok = false; break; }
-      m_lag = m_new;
-      m_prev = m_new;
-    }
-    if (ok && nblk > 0) ok = accumulate(nblk - 1, m_lag);
-    // normalised output row
-    const int qrow = q0 + row;
-    if (ok && qrow < p.Lq) {
-      const float inv = l > 0.f ? 1.0f / l : 0.f;
-      const size_t base = static_cast<size_t>(b) * p.o_bstride + static_cast<size_t>(qrow) * p.ldo + static_cast<size_t>(h) * HD;
-      if (p.out_dtype == ANIMA_F32) {
-        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + base);
+      float rsp[4] = {0.f, 0.f, 0.f, 0.f};  // partial row sums
+      uint32_t pk[2][32];
 #pragma unroll
-        for (int c = 0; c < HD / 4; ++c)
-          dst[c] = make_float4(o[4 * c] * inv, o[4 * c + 1] * inv, o[4 * c + 2] * inv, o[4 * c + 3] * inv);
-      } else {
-        uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + base);
-        const bool obf = p.out_dtype == ANIMA_BF16;
+      for (int c = 0; c < 4; ++c)
 #pragma unroll
-        for (int c = 0; c < HD / 8; ++c) {
-          uint4 u;
-          if (obf) {
-            u.x = pack2<true>(o[8 * c] * inv, o[8 * c + 1] * inv);
-            u.y = pack2<true>(o[8 * c + 2] * inv, o[8 * c + 3] * inv);
-            u.z = pack2<true>(o[8 * c + 4] * inv, o[8 * c + 5] * inv);
-            u.w = pack2<true>(o[8 * c + 6] * inv, o[8 * c + 7] * inv);
-          } else {
-            u.x = pack2<false>(o[8 * c] * inv, o[8 * c + 1] * inv);
-            u.y = pack2<false>(o[8 * c + 2] * inv, o[8 * c + 3] * inv);
-            u.z = pack2<false>(o[8 * c + 4] * inv, o[8 * c + 5] * inv);
-            u.w = pack2<false>(o[8 * c + 6] * inv, o[8 * c + 7] * inv);
+        for (int t = 0; t < 32; t += 2) {
+          const float a0 = fmaf(__uint_as_float(sr[c][t]), p.scale_log2, -m_used);
+          const float a1 = fmaf(__uint_as_float(sr[c][t + 1]), p.scale_log2, -m_used);
+          float e0 = (EMU >= 2 && (t & 2)) ? exp2_fma(a0) : ex2(a0);
+          float e1 = (EMU >= 1 && (t & 2)) ? exp2_fma(a1) : ex2(a1);
+          if (masked) {  // -inf scores: exactly zero probability
+            if (kbase + 32 * c + t >= kv_len) e0 = 0.f;
+            if (kbase + 32 * c + t + 1 >= kv_len) e1 = 0.f;
           }
-          dst[c] = u;
+          rsp[(t >> 1) & 3] += e0 + e1;
+          pk[c >> 1][(c & 1) * 16 + t / 2] = pack2<BF16>(e0, e1);
         }
+      const float rs = (rsp[0] + rsp[1]) + (rsp[2] + rsp[3]);
+      l = l * alpha + rs;
+      // P over the first 64 columns of S (two 16-bit probabilities per column)
+      tmem_st32(s_addr, pk[0]);
+      tmem_st32(s_addr + 32, pk[1]);
+      if (rescale) {
+        // O holds sum_{i<j} P_i V_i relative to the old max: wait for PV(j-1), then scale in place
+        if (!warp_wait(&o_done[x], jp ^ 1, abort_flag, kErrTimeoutAcc)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t orr[32];
+          tmem_ld32(o_addr + 32 * c, orr);
+          tmem_ld_wait(orr);
+#pragma unroll
+          for (int t = 0; t < 32; ++t) orr[t] = __float_as_uint(__uint_as_float(orr[t]) * alpha);
+          tmem_st32(o_addr + 32 * c, orr);
+        }
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[x]);
+    }
+    // normalised output row once the last PV has landed
+    if (ok && nblk > 0 && warp_wait(&o_done[x], (nblk - 1) & 1, abort_flag, kErrTimeoutAcc)) {
+      tc_fence_after();
+      const int qrow = q0 + x * TILE + row;
+      const float inv = l > 0.f ? 1.0f / l : 0.f;
+      const size_t base = static_cast<size_t>(b) * p.o_bstride + static_cast<size_t>(qrow) * p.ldo +
+                          static_cast<size_t>(h) * HD;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t orr[32];
+        tmem_ld32(o_addr + 32 * c, orr);
+        tmem_ld_wait(orr);
+        if (qrow < p.Lq) {
+          if (p.out_dtype == ANIMA_F32) {
+            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + base + 32 * c);
+#pragma unroll
+            for (int t = 0; t < 8; ++t)
+              dst[t] = make_float4(__uint_as_float(orr[4 * t]) * inv, __uint_as_float(orr[4 * t + 1]) * inv,
+                                   __uint_as_float(orr[4 * t + 2]) * inv, __uint_as_float(orr[4 * t + 3]) * inv);
+          } else {
+            uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + base + 32 * c);
+            const bool obf = p.out_dtype == ANIMA_BF16;
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+              float v[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(orr[8 * t + e]) * inv;
+              uint4 u;
+              if (obf) {
+                u.x = pack2<true>(v[0], v[1]);
+                u.y = pack2<true>(v[2], v[3]);
+                u.z = pack2<true>(v[4], v[5]);
+                u.w = pack2<true>(v[6], v[7]);
+              } else {
+                u.x = pack2<false>(v[0], v[1]);
+                u.y = pack2<false>(v[2], v[3]);
+                u.z = pack2<false>(v[4], v[5]);
+                u.w = pack2<false>(v[6], v[7]);
+              }
+              dst[t] = u;
+            }
+          }
+        }
+      }
+    } else if (nblk == 0) {
+      // no keys: zero rows (the softmax of an empty set is taken as 0)
+      const int qrow = q0 + x * TILE + row;
+      if (qrow < p.Lq) {
+        const size_t base = static_cast<size_t>(b) * p.o_bstride + static_cast<size_t>(qrow) * p.ldo +
+                            static_cast<size_t>(h) * HD;
+        const int esz = p.out_dtype == ANIMA_F32 ? 4 : 2;
+        uint4* dst = reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.out) + base * esz);
+        for (int t = 0; t < HD * esz / 16; ++t) dst[t] = make_uint4(0, 0, 0, 0);
       }
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -415,7 +466,7 @@ extern "C" int anima_attention(anima_ctx* ctx, const anima_attention_args* a) {
   p.Lq = a->Lq;
   p.Lk = a->Lk;
   p.heads = a->heads;
-  p.q_tiles = (a->Lq + attn::TILE - 1) / attn::TILE;
+  p.q_pairs = (a->Lq + 2 * attn::TILE - 1) / (2 * attn::TILE);
   p.q_col = a->q_off;
   p.k_col = a->k_off;
   p.v_col = a->v_off;
@@ -428,25 +479,25 @@ extern "C" int anima_attention(anima_ctx* ctx, const anima_attention_args* a) {
   const float scale = a->scale > 0.f ? a->scale : 1.0f / sqrtf(static_cast<float>(a->head_dim));
   p.scale_log2 = scale * 1.4426950408889634f;
 
-  const long long grid = static_cast<long long>(p.q_tiles) * a->heads * a->batch;
+  const long long grid = static_cast<long long>(p.q_pairs) * a->heads * a->batch;
   ANIMA_REQUIRE(grid < (1LL << 31), "anima_attention: problem too large");
   ProfScope prof(ctx, "attn.flash", 4.0 * a->batch * a->heads * static_cast<double>(a->Lq) * a->Lk * a->head_dim, 0);
-  if (a->dtype == ANIMA_BF16) {
-    static bool set = false;
-    if (!set) {
-      ANIMA_CUDA(cudaFuncSetAttribute(attn::attention_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      attn::SMEM_BYTES));
-      set = true;
-    }
-    attn::attention_kernel<true><<<static_cast<int>(grid), attn::THREADS, attn::SMEM_BYTES, ctx->stream>>>(tq, tk, tv, p);
-  } else {
-    static bool set = false;
-    if (!set) {
-      ANIMA_CUDA(cudaFuncSetAttribute(attn::attention_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      attn::SMEM_BYTES));
-      set = true;
-    }
-    attn::attention_kernel<false><<<static_cast<int>(grid), attn::THREADS, attn::SMEM_BYTES, ctx->stream>>>(tq, tk, tv, p);
+  // share of the exponentials computed on the FMA pipes (ANIMA_ATTN_EMU = 0, 1 or 2 of 4)
+  static const int emu = [] {
+    const char* e = getenv("ANIMA_ATTN_EMU");
+    const int v = e ? atoi(e) : 0;
+    return v < 0 ? 0 : (v > 2 ? 2 : v);
+  }();
+  const bool bf16 = a->dtype == ANIMA_BF16;
+  using Kfn = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const attn::Params);
+  Kfn fns[2][3] = {{attn::attention_kernel<false, 0>, attn::attention_kernel<false, 1>, attn::attention_kernel<false, 2>},
+                   {attn::attention_kernel<true, 0>, attn::attention_kernel<true, 1>, attn::attention_kernel<true, 2>}};
+  static bool set[2][3] = {};
+  Kfn fn = fns[bf16 ? 1 : 0][emu];
+  if (!set[bf16 ? 1 : 0][emu]) {
+    ANIMA_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, attn::SMEM_BYTES));
+    set[bf16 ? 1 : 0][emu] = true;
   }
+  fn<<<static_cast<int>(grid), attn::THREADS, attn::SMEM_BYTES, ctx->stream>>>(tq, tk, tv, p);
   return check_launch("attention_kernel");
 }

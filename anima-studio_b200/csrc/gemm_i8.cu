@@ -48,16 +48,16 @@ struct Params {
   int n_q;
   float eps;
   int num_m_blocks, num_n_blocks, num_k_blocks, num_tiles;
+  int group_m;
 };
 
-// Tile order: groups of kGroupM m-blocks, n-blocks outermost within a group, so the CTAs in flight
+// Tile order: groups of group_m m-blocks, n-blocks outermost within a group, so the CTAs in flight
 // share a few A row-blocks and sweep the weights (keeps A resident in L2 across the n sweep).
-constexpr int kGroupM = 8;
 __device__ __forceinline__ void tile_coords(const Params& p, int tile, int& mb, int& nb) {
-  const int per_group = kGroupM * p.num_n_blocks;
+  const int per_group = p.group_m * p.num_n_blocks;
   const int group = tile / per_group;
-  const int first_m = group * kGroupM;
-  const int gm = min(kGroupM, p.num_m_blocks - first_m);
+  const int first_m = group * p.group_m;
+  const int gm = min(p.group_m, p.num_m_blocks - first_m);
   const int within = tile - group * per_group;
   mb = first_m + within % gm;
   nb = within / gm;
@@ -88,115 +88,129 @@ __device__ __forceinline__ float act_fn(float v, int act) {
   return v;
 }
 
-// Issue the TMEM loads of 32 accumulator columns (hi plane, and lo plane at +BN) of this row.
-template <int BN, int NPLANES>
-__device__ __forceinline__ void issue_cols(uint32_t taddr, int col, uint32_t (&rh)[32], uint32_t (&rl)[32]) {
-  tmem_ld32(taddr + col, rh);
-  if constexpr (NPLANES == 2) tmem_ld32(taddr + BN + col, rl);
+// CH consecutive fp32 values through the read-only path as 16-byte loads (p 16-byte aligned).
+template <int CH>
+__device__ __forceinline__ void ldv(const float* p, float (&v)[CH]) {
+  const float4* q = reinterpret_cast<const float4*>(p);
+#pragma unroll
+  for (int j = 0; j < CH / 4; ++j) {
+    const float4 t = __ldg(q + j);
+    v[4 * j] = t.x;
+    v[4 * j + 1] = t.y;
+    v[4 * j + 2] = t.z;
+    v[4 * j + 3] = t.w;
+  }
+}
+__device__ __forceinline__ void ld32(const float* p, float (&v)[32]) { ldv<32>(p, v); }
+
+template <int CH>
+__device__ __forceinline__ void tmem_ldc(uint32_t taddr, uint32_t (&r)[CH]) {
+  if constexpr (CH == 32) tmem_ld32(taddr, r); else tmem_ld16(taddr, r);
+}
+
+// Issue the TMEM loads of CH accumulator columns (hi plane, and lo plane at +BN) of this row.
+template <int BN, int NPLANES, int CH>
+__device__ __forceinline__ void issue_cols(uint32_t taddr, int col, uint32_t (&rh)[CH], uint32_t (&rl)[CH]) {
+  tmem_ldc<CH>(taddr + col, rh);
+  if constexpr (NPLANES == 2) tmem_ldc<CH>(taddr + BN + col, rl);
 }
 
 // After the loads landed: y = a_scale[m] w_scale[n] (hi + lo / 254) (+ bias) (+ add) (act).
-template <int NPLANES>
-__device__ __forceinline__ void finish_cols(const Params& p, int m, int n, bool row_ok, const uint32_t (&rh)[32],
-                                            const uint32_t (&rl)[32], float (&v)[32], bool apply_act) {
+template <int NPLANES, int CH>
+__device__ __forceinline__ void finish_cols(const Params& p, int m, int n, bool row_ok, const uint32_t (&rh)[CH],
+                                            const uint32_t (&rl)[CH], float (&v)[CH], bool apply_act) {
   const float as = row_ok ? __ldg(p.a_scale + m) : 0.0f;
+  float ws[CH];
+  ldv<CH>(p.w_scale + n, ws);
   if constexpr (NPLANES == 2) {
     const float as_lo = as * (1.0f / 254.0f);
 #pragma unroll
-    for (int j = 0; j < 32; ++j)
+    for (int j = 0; j < CH; ++j)
       v[j] = fmaf(static_cast<float>(static_cast<int>(rl[j])), as_lo, static_cast<float>(static_cast<int>(rh[j])) * as) *
-             __ldg(p.w_scale + n + j);
+             ws[j];
   } else {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = static_cast<float>(static_cast<int>(rh[j])) * as * __ldg(p.w_scale + n + j);
+    for (int j = 0; j < CH; ++j) v[j] = static_cast<float>(static_cast<int>(rh[j])) * as * ws[j];
   }
   if (p.bias) {
+    float bv[CH];
+    ldv<CH>(p.bias + n, bv);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] += __ldg(p.bias + n + j);
+    for (int j = 0; j < CH; ++j) v[j] += bv[j];
   }
   if (p.add && row_ok) {
-    const float4* a4 = reinterpret_cast<const float4*>(p.add + static_cast<size_t>(m) * p.ld_add + n);
+    float av[CH];
+    ldv<CH>(p.add + static_cast<size_t>(m) * p.ld_add + n, av);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      float4 t = __ldg(a4 + j);
-      v[4 * j] += t.x;
-      v[4 * j + 1] += t.y;
-      v[4 * j + 2] += t.z;
-      v[4 * j + 3] += t.w;
-    }
+    for (int j = 0; j < CH; ++j) v[j] += av[j];
   }
   if (apply_act && p.act != ANIMA_ACT_NONE) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = act_fn(v[j], p.act);
+    for (int j = 0; j < CH; ++j) v[j] = act_fn(v[j], p.act);
   }
 }
 
-// Load 32 accumulator columns and finish them (no overlap; used by the per-head epilogues).
-template <int BN, int NPLANES>
+// Load CH accumulator columns and finish them (no overlap; used by the per-head epilogues).
+template <int BN, int NPLANES, int CH = 16>
 __device__ __forceinline__ void load_cols(const Params& p, uint32_t taddr, int col, int m, int n, bool row_ok,
-                                          float (&v)[32], bool apply_act) {
-  uint32_t rh[32], rl[32];
-  issue_cols<BN, NPLANES>(taddr, col, rh, rl);
+                                          float (&v)[CH], bool apply_act) {
+  uint32_t rh[CH], rl[CH];
+  issue_cols<BN, NPLANES, CH>(taddr, col, rh, rl);
   tmem_ld_wait(rh);
   if constexpr (NPLANES == 2) tmem_ld_wait(rl);
-  finish_cols<NPLANES>(p, m, n, row_ok, rh, rl, v, apply_act);
+  finish_cols<NPLANES, CH>(p, m, n, row_ok, rh, rl, v, apply_act);
 }
 
-__device__ __forceinline__ void store32(void* out, int dtype, int ldo, int m, int n, const float (&v)[32]) {
+template <int CH>
+__device__ __forceinline__ void store_cols(void* out, int dtype, int ldo, int m, int n, const float (&v)[CH]) {
   if (dtype == ANIMA_F32) {
     float4* o = reinterpret_cast<float4*>(static_cast<float*>(out) + static_cast<size_t>(m) * ldo + n);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) o[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-  } else if (dtype == ANIMA_BF16) {
-    uint4* o = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(out) + static_cast<size_t>(m) * ldo + n);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      uint4 u;
-      __nv_bfloat162 h0 = __floats2bfloat162_rn(v[8 * j], v[8 * j + 1]);
-      __nv_bfloat162 h1 = __floats2bfloat162_rn(v[8 * j + 2], v[8 * j + 3]);
-      __nv_bfloat162 h2 = __floats2bfloat162_rn(v[8 * j + 4], v[8 * j + 5]);
-      __nv_bfloat162 h3 = __floats2bfloat162_rn(v[8 * j + 6], v[8 * j + 7]);
-      u.x = *reinterpret_cast<uint32_t*>(&h0);
-      u.y = *reinterpret_cast<uint32_t*>(&h1);
-      u.z = *reinterpret_cast<uint32_t*>(&h2);
-      u.w = *reinterpret_cast<uint32_t*>(&h3);
-      o[j] = u;
-    }
+    for (int j = 0; j < CH / 4; ++j) o[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
   } else {
-    uint4* o = reinterpret_cast<uint4*>(static_cast<__half*>(out) + static_cast<size_t>(m) * ldo + n);
+    uint4* o = reinterpret_cast<uint4*>(static_cast<uint16_t*>(out) + static_cast<size_t>(m) * ldo + n);
+    const bool bf = dtype == ANIMA_BF16;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      uint4 u;
-      __half2 h0 = __floats2half2_rn(v[8 * j], v[8 * j + 1]);
-      __half2 h1 = __floats2half2_rn(v[8 * j + 2], v[8 * j + 3]);
-      __half2 h2 = __floats2half2_rn(v[8 * j + 4], v[8 * j + 5]);
-      __half2 h3 = __floats2half2_rn(v[8 * j + 6], v[8 * j + 7]);
-      u.x = *reinterpret_cast<uint32_t*>(&h0);
-      u.y = *reinterpret_cast<uint32_t*>(&h1);
-      u.z = *reinterpret_cast<uint32_t*>(&h2);
-      u.w = *reinterpret_cast<uint32_t*>(&h3);
-      o[j] = u;
+    for (int j = 0; j < CH / 8; ++j) {
+      uint32_t w[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float a = v[8 * j + 2 * q], b = v[8 * j + 2 * q + 1];
+        if (bf) {
+          __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+          w[q] = *reinterpret_cast<uint32_t*>(&h);
+        } else {
+          __half2 h = __floats2half2_rn(a, b);
+          w[q] = *reinterpret_cast<uint32_t*>(&h);
+        }
+      }
+      o[j] = make_uint4(w[0], w[1], w[2], w[3]);
     }
   }
 }
+__device__ __forceinline__ void store32(void* out, int dtype, int ldo, int m, int n, const float (&v)[32]) {
+  store_cols<32>(out, dtype, ldo, m, n, v);
+}
 
-__device__ __forceinline__ void resid32(const Params& p, int m, int n, const float (&v)[32]) {
+// out[m, n..n+CH-1] = xo + gate[gate_off + n..] * v  (xo: the residual row chunk, loaded earlier)
+template <int CH>
+__device__ __forceinline__ void resid_cols(const Params& p, int m, int n, const float4 (&xo)[CH / 4],
+                                           const float (&v)[CH]) {
+  float g[CH];
+  if (p.gate) {
+    ldv<CH>(p.gate + p.gate_off + n, g);
+  } else {
+#pragma unroll
+    for (int j = 0; j < CH; ++j) g[j] = 1.f;
+  }
   float4* o = reinterpret_cast<float4*>(static_cast<float*>(p.out) + static_cast<size_t>(m) * p.ldo + n);
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    float4 c = o[j];
-    float g0 = 1.f, g1 = 1.f, g2 = 1.f, g3 = 1.f;
-    if (p.gate) {
-      const float* g = p.gate + p.gate_off + n + 4 * j;
-      g0 = __ldg(g);
-      g1 = __ldg(g + 1);
-      g2 = __ldg(g + 2);
-      g3 = __ldg(g + 3);
-    }
-    c.x += g0 * v[4 * j];
-    c.y += g1 * v[4 * j + 1];
-    c.z += g2 * v[4 * j + 2];
-    c.w += g3 * v[4 * j + 3];
+  for (int j = 0; j < CH / 4; ++j) {
+    float4 c = xo[j];
+    c.x = fmaf(g[4 * j], v[4 * j], c.x);
+    c.y = fmaf(g[4 * j + 1], v[4 * j + 1], c.y);
+    c.z = fmaf(g[4 * j + 2], v[4 * j + 2], c.z);
+    c.w = fmaf(g[4 * j + 3], v[4 * j + 3], c.w);
     o[j] = c;
   }
 }
@@ -206,24 +220,34 @@ template <int BN, int NPLANES>
 __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t taddr, int m, int n0) {
   const bool row_ok = m < p.M;
   if (p.out_mode == ANIMA_OUT_STORE || p.out_mode == ANIMA_OUT_RESID) {
-    // software pipeline: the TMEM loads of chunk c+1 are in flight while chunk c is finished
-    uint32_t rh[2][32], rl[2][32];
-    issue_cols<BN, NPLANES>(taddr, 0, rh[0], rl[0]);
+    // software pipeline over 16-column chunks: the TMEM loads of chunk c+1 are in flight while
+    // chunk c is finished; the residual chunk is requested before the math that precedes its use
+    constexpr int CH = 16;
+    uint32_t rh[2][CH], rl[2][CH];
+    issue_cols<BN, NPLANES, CH>(taddr, 0, rh[0], rl[0]);
     tmem_ld_wait(rh[0]);
     if constexpr (NPLANES == 2) tmem_ld_wait(rl[0]);
+    const bool resid = p.out_mode == ANIMA_OUT_RESID;
 #pragma unroll
-    for (int c = 0; c < BN / 32; ++c) {
+    for (int c = 0; c < BN / CH; ++c) {
       const int cur = c & 1;
-      if (c + 1 < BN / 32) issue_cols<BN, NPLANES>(taddr, 32 * (c + 1), rh[cur ^ 1], rl[cur ^ 1]);
-      float v[32];
-      finish_cols<NPLANES>(p, m, n0 + 32 * c, row_ok, rh[cur], rl[cur], v, true);
-      if (row_ok) {
-        if (p.out_mode == ANIMA_OUT_STORE)
-          store32(p.out, p.out_dtype, p.ldo, m, n0 + 32 * c, v);
-        else
-          resid32(p, m, n0 + 32 * c, v);
+      if (c + 1 < BN / CH) issue_cols<BN, NPLANES, CH>(taddr, CH * (c + 1), rh[cur ^ 1], rl[cur ^ 1]);
+      float4 xo[CH / 4];
+      if (resid && row_ok) {
+        const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(p.out) +
+                                                            static_cast<size_t>(m) * p.ldo + n0 + CH * c);
+#pragma unroll
+        for (int j = 0; j < CH / 4; ++j) xo[j] = src[j];
       }
-      if (c + 1 < BN / 32) {
+      float v[CH];
+      finish_cols<NPLANES, CH>(p, m, n0 + CH * c, row_ok, rh[cur], rl[cur], v, true);
+      if (row_ok) {
+        if (resid)
+          resid_cols<CH>(p, m, n0 + CH * c, xo, v);
+        else
+          store_cols<CH>(p.out, p.out_dtype, p.ldo, m, n0 + CH * c, v);
+      }
+      if (c + 1 < BN / CH) {
         tmem_ld_wait(rh[cur ^ 1]);
         if constexpr (NPLANES == 2) tmem_ld_wait(rl[cur ^ 1]);
       }
@@ -231,7 +255,9 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t taddr, i
     return;
   }
   // Per-head RMSNorm (+ split-half RoPE for q/k heads of a fused qkv projection): a head is 128
-  // consecutive columns and never straddles a tile (BN is a multiple of 128).
+  // consecutive columns and never straddles a tile (BN is a multiple of 128). Two passes over the
+  // accumulator: sum of squares, then normalise (+ rotate) 16-column pieces.
+  constexpr int CH = 16;
 #pragma unroll 1
   for (int h0 = 0; h0 < BN; h0 += 128) {
     const int nh = n0 + h0;
@@ -240,20 +266,20 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t taddr, i
     const bool is_k = qkv && !is_q && nh < 2 * p.n_q;
     if (qkv && !is_q && !is_k) {  // v heads: plain store
 #pragma unroll 1
-      for (int c = 0; c < 128; c += 32) {
-        float v[32];
-        load_cols<BN, NPLANES>(p, taddr, h0 + c, m, nh + c, row_ok, v, true);
-        if (row_ok) store32(p.out, p.out_dtype, p.ldo, m, nh + c, v);
+      for (int c = 0; c < 128; c += CH) {
+        float v[CH];
+        load_cols<BN, NPLANES, CH>(p, taddr, h0 + c, m, nh + c, row_ok, v, true);
+        if (row_ok) store_cols<CH>(p.out, p.out_dtype, p.ldo, m, nh + c, v);
       }
       continue;
     }
     float ss = 0.f;
 #pragma unroll 1
-    for (int c = 0; c < 128; c += 32) {
-      float v[32];
-      load_cols<BN, NPLANES>(p, taddr, h0 + c, m, nh + c, row_ok, v, true);
+    for (int c = 0; c < 128; c += CH) {
+      float v[CH];
+      load_cols<BN, NPLANES, CH>(p, taddr, h0 + c, m, nh + c, row_ok, v, true);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) ss += v[j] * v[j];
+      for (int j = 0; j < CH; ++j) ss += v[j] * v[j];
     }
     const float rs = 1.0f / sqrtf(ss * (1.0f / 128.0f) + p.eps);
     const float* w = is_k ? p.norm_k : p.norm_q;
@@ -262,32 +288,42 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t taddr, i
       const float* cs = p.rope + static_cast<size_t>(tok) * 64;
       const float* sn = p.rope + static_cast<size_t>(p.rope_rows) * 64 + static_cast<size_t>(tok) * 64;
 #pragma unroll 1
-      for (int c = 0; c < 64; c += 32) {
-        float v1[32], v2[32];
-        load_cols<BN, NPLANES>(p, taddr, h0 + c, m, nh + c, row_ok, v1, true);
-        load_cols<BN, NPLANES>(p, taddr, h0 + 64 + c, m, nh + 64 + c, row_ok, v2, true);
+      for (int c = 0; c < 64; c += CH) {
+        float v1[CH], v2[CH];
+        load_cols<BN, NPLANES, CH>(p, taddr, h0 + c, m, nh + c, row_ok, v1, true);
+        load_cols<BN, NPLANES, CH>(p, taddr, h0 + 64 + c, m, nh + 64 + c, row_ok, v2, true);
         if (row_ok) {
+          float a[CH], b[CH];
+          ldv<CH>(w + c, a);
+          ldv<CH>(w + 64 + c, b);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float y1 = v1[j] * rs * __ldg(w + c + j);
-            const float y2 = v2[j] * rs * __ldg(w + 64 + c + j);
-            const float co = __ldg(cs + c + j), si = __ldg(sn + c + j);
-            v1[j] = y1 * co - y2 * si;
-            v2[j] = y2 * co + y1 * si;
+          for (int j = 0; j < CH; ++j) {
+            v1[j] *= rs * a[j];
+            v2[j] *= rs * b[j];
           }
-          store32(p.out, p.out_dtype, p.ldo, m, nh + c, v1);
-          store32(p.out, p.out_dtype, p.ldo, m, nh + 64 + c, v2);
+          ldv<CH>(cs + c, a);  // cos
+          ldv<CH>(sn + c, b);  // sin
+#pragma unroll
+          for (int j = 0; j < CH; ++j) {
+            const float y1 = v1[j], y2 = v2[j];
+            v1[j] = y1 * a[j] - y2 * b[j];
+            v2[j] = y2 * a[j] + y1 * b[j];
+          }
+          store_cols<CH>(p.out, p.out_dtype, p.ldo, m, nh + c, v1);
+          store_cols<CH>(p.out, p.out_dtype, p.ldo, m, nh + 64 + c, v2);
         }
       }
     } else {
 #pragma unroll 1
-      for (int c = 0; c < 128; c += 32) {
-        float v[32];
-        load_cols<BN, NPLANES>(p, taddr, h0 + c, m, nh + c, row_ok, v, true);
+      for (int c = 0; c < 128; c += CH) {
+        float v[CH];
+        load_cols<BN, NPLANES, CH>(p, taddr, h0 + c, m, nh + c, row_ok, v, true);
         if (row_ok) {
+          float wv[CH];
+          ldv<CH>(w + c, wv);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = v[j] * rs * __ldg(w + c + j);
-          store32(p.out, p.out_dtype, p.ldo, m, nh + c, v);
+          for (int j = 0; j < CH; ++j) v[j] = v[j] * rs * wv[j];
+          store_cols<CH>(p.out, p.out_dtype, p.ldo, m, nh + c, v);
         }
       }
     }
@@ -513,6 +549,11 @@ int launch(anima_ctx* ctx, const anima_qact* x, const anima_weight* W, const ani
   p.num_n_blocks = N / BN;
   p.num_k_blocks = K / BK;
   p.num_tiles = p.num_m_blocks * p.num_n_blocks;
+  static const int group_m_env = [] {
+    const char* e = getenv("ANIMA_GEMM_GROUP_M");  // tile-order experiments; default 8
+    return e ? atoi(e) : 8;
+  }();
+  p.group_m = group_m_env > 0 ? group_m_env : 8;
 
   static bool attr_set = false;
   if (!attr_set) {
@@ -565,6 +606,11 @@ extern "C" int anima_linear(anima_ctx* ctx, const anima_qact* x, const anima_wei
     ANIMA_REQUIRE(o->n_q % 128 == 0 && 2 * o->n_q <= W->N, "anima_linear: bad n_q %d", o->n_q);
   }
   if (o->out_mode == ANIMA_OUT_HEAD_NORM) ANIMA_REQUIRE(o->norm_q, "anima_linear: head-norm epilogue needs norm_q");
+  // the epilogue reads per-column vectors 16 bytes at a time
+  ANIMA_REQUIRE(aligned16(W->scale) && (!W->bias || aligned16(W->bias)) && (!o->norm_q || aligned16(o->norm_q)) &&
+                    (!o->norm_k || aligned16(o->norm_k)) && (!o->rope || aligned16(o->rope)) &&
+                    (!o->gate || (aligned16(o->gate) && o->gate_off % 4 == 0)),
+                "anima_linear: scale/bias/gate/norm/rope vectors must be 16-byte aligned (gate_off a multiple of 4)");
   // Two planes: 128-column tiles double-buffer both accumulators (2 x 2 x 128 TMEM columns) so the
   // epilogue overlaps the next tile's MMAs; for long K (>= 4096) the MMA time per tile dwarfs the
   // epilogue and 256-column tiles (one buffer) read 25% fewer shared-memory bytes per MMA.

@@ -220,15 +220,15 @@ def kernel_case(args):
         q = torch.randint(-127, 128, (N, K), dtype=torch.int8, device="cuda")
         return W.Linear("i8", N, K, q, torch.full((N,), 1e-3, device="cuda"))
 
-    if args.kernel in ("mlp1", "mlp2", "qkv"):
-        N, K = {"mlp1": (8192, 2048), "mlp2": (2048, 8192), "qkv": (6144, 2048)}[args.kernel]
+    if args.kernel in ("mlp1", "mlp2", "qkv", "oproj"):
+        N, K = {"mlp1": (8192, 2048), "mlp2": (2048, 8192), "qkv": (6144, 2048), "oproj": (2048, 2048)}[args.kernel]
         w = lin(N, K)
         qa = ops.rotate_quant(torch.randn(M, K, device="cuda"), planes)
         if args.kernel == "mlp1":
             out = torch.empty(M, N, dtype=torch.float16 if args.out == "f16" else torch.float32, device="cuda")
             act = None if args.act == "none" else args.act
             fn = lambda: ops.linear(qa, w, out=out, act=act)  # noqa: E731
-        elif args.kernel == "mlp2":
+        elif args.kernel in ("mlp2", "oproj"):
             out = torch.zeros(M, N, device="cuda")
             gate = torch.randn(6144, device="cuda")
             fn = lambda: ops.linear(qa, w, out=out, resid=True, gate=gate, g_off=4096)  # noqa: E731
@@ -431,6 +431,8 @@ def main():
                           "peak_bf16_tflops": peaks.get("bf16_tflops"),
                           "frac": (att_work / (att_ms * 1e-3) / 1e12) / peaks["bf16_tflops"]
                           if att_ms and peaks.get("bf16_tflops") else None},
+            "per_op_ms_per_step": {f"{k[0].replace('anima_', '')}:{k[1]}": round(v[1] / replay_steps, 3)
+                                   for k, v in sorted(summ.items(), key=lambda kv: -kv[1][1])},
             "note": "achieved = algorithmic 2MNK ops / CUDA-event time per launch (instrumented replay); "
                     "a16 runs two int8 MMAs per product, so hw_ops_frac = planes x frac"}
     line = {"metric": METRIC, "value": value, "unit": "steps/s", "n_gpus": world, "steps": args.steps,
