@@ -125,7 +125,7 @@ __device__ __forceinline__ void fwht256_warp(float (&x)[8]) {
 }
 
 // ------------------------------------------------------------------ row kernel: LN + adaLN, ConvRot, quant
-// One row per warp for rows up to 2048 wide (WPR = 1), WPR = cols / 2048 warps per row beyond;
+// One row per warp for rows up to 1024 wide (WPR = 1), WPR = cols / 1024 warps per row beyond;
 // 8 warps per CTA. Lane l holds, for each of the warp's G groups of 256 columns, the 8 consecutive
 // elements 8l..8l+7 of that group, so every warp access is a contiguous 256-element segment and
 // every ConvRot group lives in one warp (fwht256_warp). Reductions are warp shuffles, plus one
@@ -136,6 +136,7 @@ __device__ __forceinline__ void fwht256_warp(float (&x)[8]) {
 //           pre-activation)
 //   rotate  y <- y H per 256 group (tools/quant.py:30-45)
 //   quant   s = amax / 127; a = y * (127 / amax); hi = rne(a); lo = rne((a - hi) * 254)
+//           (|a| <= 127 and |a - hi| <= 1/2, so neither needs clamping)
 template <int WPR>
 __device__ __forceinline__ float row_reduce(float v, float* red, bool is_max) {
   v = is_max ? warp_max(v) : warp_sum(v);
@@ -159,7 +160,7 @@ __global__ void __launch_bounds__(256) rows_kernel(const TIn* __restrict__ x, in
                                                    const float* __restrict__ mod, int shift_off, int scale_off,
                                                    float eps, int rotate, TOut* y, int8_t* qhi, int8_t* qlo,
                                                    float* qscale, int qld, int act) {
-  constexpr int WPR = COLS > 2048 ? COLS / 2048 : 1;
+  constexpr int WPR = COLS > 1024 ? COLS / 1024 : 1;  // warps per row: at most 4 groups of 256 per warp
   constexpr int G = COLS / 256 / WPR;
   constexpr int RPC = 8 / WPR;
   static_assert(G >= 1 && G <= 8 && COLS % 256 == 0, "unsupported row width");
@@ -232,18 +233,19 @@ __global__ void __launch_bounds__(256) rows_kernel(const TIn* __restrict__ x, in
       uint32_t h2[2], l2[2];
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
-        uint32_t hb = 0, lb = 0;
+        // round to nearest even through the 1.5 * 2^23 magic number (|a| <= 127, |lo| <= 127):
+        // integer values come straight out of the float's mantissa, no conversion unit needed
+        int hv[4], lv[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const float a = v[g][4 * half + j] * inv;
-          const float q = rintf(a);
-          const int hv = static_cast<int>(q);
-          const int lv = static_cast<int>(fminf(fmaxf(rintf((a - q) * 254.0f), -127.f), 127.f));
-          hb |= (static_cast<uint32_t>(hv) & 0xFFu) << (8 * j);
-          lb |= (static_cast<uint32_t>(lv) & 0xFFu) << (8 * j);
+          const float t = a + 12582912.0f;
+          hv[j] = __float_as_int(t) - 0x4B400000;
+          const float rem = a - (t - 12582912.0f);
+          lv[j] = __float_as_int(fmaf(rem, 254.0f, 12582912.0f)) - 0x4B400000;
         }
-        h2[half] = hb;
-        l2[half] = lb;
+        h2[half] = __byte_perm(__byte_perm(hv[0], hv[1], 0x0040), __byte_perm(hv[2], hv[3], 0x0040), 0x5410);
+        l2[half] = __byte_perm(__byte_perm(lv[0], lv[1], 0x0040), __byte_perm(lv[2], lv[3], 0x0040), 0x5410);
       }
       *reinterpret_cast<uint2*>(qhi + r * qld + col[g]) = make_uint2(h2[0], h2[1]);
       if (qlo) *reinterpret_cast<uint2*>(qlo + r * qld + col[g]) = make_uint2(l2[0], l2[1]);
@@ -504,7 +506,7 @@ int launch_rows(anima_ctx* ctx, const TIn* x, int rows, int cols, int ldx, const
   const int qld = q ? q->ld : 0;
 #define ROWS_CASE(C)                                                                                             \
   case C: {                                                                                                      \
-    constexpr int rpc = 8 / (C > 2048 ? C / 2048 : 1);                                                          \
+    constexpr int rpc = 8 / (C > 1024 ? C / 1024 : 1);                                                          \
     rows_kernel<C, TIn, TOut, LN><<<(rows + rpc - 1) / rpc, 256, 0, ctx->stream>>>(x, rows, ldx, mod, so, sco,   \
                                                                                   eps, rotate, y, hi, lo, sc, qld, act); \
     break;                                                                                                       \

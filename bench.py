@@ -417,15 +417,19 @@ def main():
     planes = 2 if args.precision == "a16" else 1
     achieved = lin_work / (lin_ms * 1e-3) / 1e12 if lin_ms else 0.0
     traffic = traffic_from_profile()
-    roof = {"kernel": "gemm_i8_kernel (all block linears)", "bound": "tensor", "achieved": achieved,
-            "peak": int8_peak, "unit": "TOPS", "frac": achieved / int8_peak if int8_peak else None,
-            "peak_source": "measured: cuBLASLt int8 GEMM 8192^3 (torch._int_mm) on this GPU",
+    mlp1_n = max(mlp1[0], 1)
+    mlp1_ms = mlp1[1] / mlp1_n
+    mlp1_work = mlp1[2] / mlp1_n
+    mlp1_ach = mlp1_work / (mlp1_ms * 1e-3) / 1e12 if mlp1_ms else 0.0
+    roof = {"kernel": "gemm_i8_kernel, the 2048->8192 block linear (dit.mlp1): M=4096 N=8192 K=2048",
+            "bound": "tensor", "achieved": mlp1_ach, "peak": int8_peak, "unit": "TOPS",
+            "frac": mlp1_ach / int8_peak if int8_peak else None,
+            "peak_source": "measured: cuBLASLt int8 GEMM 8192^3 (torch._int_mm) on this GPU (MEASURED_PEAKS.json has no int8 entry)",
             "traffic": traffic,
-            "hw_ops_frac": planes * achieved / int8_peak if int8_peak else None,
-            "launches_per_step": lin_n / replay_steps, "ms_per_step": lin_ms / replay_steps,
-            "mlp1": {"shape": "4096x8192x2048 (+GELU)", "ms": mlp1[1] / max(mlp1[0], 1),
-                     "achieved_tops": mlp1[2] / max(mlp1[0], 1) / (mlp1[1] / max(mlp1[0], 1) * 1e-3) / 1e12
-                     if mlp1[1] else None},
+            "launch_ms": mlp1_ms, "work_per_launch": mlp1_work,
+            "hw_ops_frac": planes * mlp1_ach / int8_peak if int8_peak else None,
+            "all_linears": {"achieved_tops": achieved, "frac": achieved / int8_peak if int8_peak else None,
+                            "launches_per_step": lin_n / replay_steps, "ms_per_step": lin_ms / replay_steps},
             "attention": {"ms_per_step": att_ms / replay_steps,
                           "achieved_tflops": att_work / (att_ms * 1e-3) / 1e12 if att_ms else None,
                           "peak_bf16_tflops": peaks.get("bf16_tflops"),
@@ -433,8 +437,10 @@ def main():
                           if att_ms and peaks.get("bf16_tflops") else None},
             "per_op_ms_per_step": {f"{k[0].replace('anima_', '')}:{k[1]}": round(v[1] / replay_steps, 3)
                                    for k, v in sorted(summ.items(), key=lambda kv: -kv[1][1])},
-            "note": "achieved = algorithmic 2MNK ops / CUDA-event time per launch (instrumented replay); "
-                    "a16 runs two int8 MMAs per product, so hw_ops_frac = planes x frac"}
+            "note": "achieved = algorithmic 2MNK ops per launch / CUDA-event time per launch, measured on the "
+                    "launching stream in an instrumented replay of the timed steps; a16 runs two int8 MMAs per "
+                    "product, so hw_ops_frac = planes x frac; traffic = DRAM bytes per launch from the ncu capture "
+                    "in profiles/gemm_i8_mlp1_L4096.md"}
     line = {"metric": METRIC, "value": value, "unit": "steps/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8", "data": "synthetic",
