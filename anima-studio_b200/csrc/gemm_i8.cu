@@ -68,7 +68,8 @@ struct Cfg {
   static constexpr int A_BYTES = BM * BK;
   static constexpr int B_BYTES = BN * BK;
   static constexpr int STAGE_BYTES = NPLANES * A_BYTES + B_BYTES;
-  static constexpr int STAGES = (200 * 1024) / STAGE_BYTES;
+  static constexpr int STAGING_BYTES = 8 * 2 * 32 * 128;  // 8 epilogue warps x 2 x 4 KB
+  static constexpr int STAGES = (216 * 1024 - STAGING_BYTES) / STAGE_BYTES;
   static constexpr int ACC_COLS = NPLANES * BN;
   // one accumulator buffer per epilogue warpgroup when two fit in TMEM, else one (the second
   // epilogue warpgroup then idles and the epilogue of a tile delays the next tile's MMAs)
@@ -76,7 +77,7 @@ struct Cfg {
   static_assert(ACC_BUFS * ACC_COLS <= 512, "accumulators exceed TMEM");
   static constexpr int TMEM_COLS = 512;
   static constexpr int BAR_BYTES = 256;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + STAGING_BYTES + BAR_BYTES + 1024;
   static_assert(STAGES >= 2, "need at least two pipeline stages");
 };
 
@@ -161,92 +162,106 @@ __device__ __forceinline__ void load_cols(const Params& p, uint32_t taddr, int c
   finish_cols<NPLANES, CH>(p, m, n, row_ok, rh, rl, v, apply_act);
 }
 
-template <int CH>
-__device__ __forceinline__ void store_cols(void* out, int dtype, int ldo, int m, int n, const float (&v)[CH]) {
-  if (dtype == ANIMA_F32) {
-    float4* o = reinterpret_cast<float4*>(static_cast<float*>(out) + static_cast<size_t>(m) * ldo + n);
+// ------------------------------------------------------------------ staged stores
+// Each epilogue warp owns two 4 KB staging buffers: 32 rows (its TMEM lane quadrant) x 128 bytes,
+// in the SWIZZLE_128B layout (16-byte chunk j of row r at r * 128 + ((j ^ (r & 7)) << 4)), so the
+// row-per-lane writes are bank-conflict free. A full buffer is written to global memory by one
+// TMA tile store (or, for the fp32 residual, a TMA reduce-add), so no lane touches global memory
+// row by row. A 128-byte staging row holds CHC = 32 fp32 or 64 16-bit columns.
+constexpr int STAGE_BUF = 32 * 128;
+
+// Write a 16-column piece (position q within the 128-byte chunk) of this lane's row.
+__device__ __forceinline__ void stage_piece(uint8_t* buf, int lane, int dtype, int q, const float (&v)[16]) {
+  uint8_t* row = buf + lane * 128;
+  if (dtype == ANIMA_F32) {  // 64 bytes: chunks 4q .. 4q+3
 #pragma unroll
-    for (int j = 0; j < CH / 4; ++j) o[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-  } else {
-    uint4* o = reinterpret_cast<uint4*>(static_cast<uint16_t*>(out) + static_cast<size_t>(m) * ldo + n);
+    for (int j = 0; j < 4; ++j) {
+      const int chunk = 4 * q + j;
+      *reinterpret_cast<float4*>(row + ((chunk ^ (lane & 7)) << 4)) =
+          make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    }
+  } else {  // 32 bytes: chunks 2q, 2q+1
     const bool bf = dtype == ANIMA_BF16;
 #pragma unroll
-    for (int j = 0; j < CH / 8; ++j) {
+    for (int j = 0; j < 2; ++j) {
       uint32_t w[4];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float a = v[8 * j + 2 * q], b = v[8 * j + 2 * q + 1];
+      for (int e = 0; e < 4; ++e) {
+        const float a = v[8 * j + 2 * e], b = v[8 * j + 2 * e + 1];
         if (bf) {
           __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-          w[q] = *reinterpret_cast<uint32_t*>(&h);
+          w[e] = *reinterpret_cast<uint32_t*>(&h);
         } else {
           __half2 h = __floats2half2_rn(a, b);
-          w[q] = *reinterpret_cast<uint32_t*>(&h);
+          w[e] = *reinterpret_cast<uint32_t*>(&h);
         }
       }
-      o[j] = make_uint4(w[0], w[1], w[2], w[3]);
+      const int chunk = 2 * q + j;
+      *reinterpret_cast<uint4*>(row + ((chunk ^ (lane & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
     }
   }
 }
-__device__ __forceinline__ void store32(void* out, int dtype, int ldo, int m, int n, const float (&v)[32]) {
-  store_cols<32>(out, dtype, ldo, m, n, v);
+
+// Hand a filled staging buffer to the TMA unit: box (CHC columns x 32 rows) at (x, y).
+__device__ __forceinline__ void stage_flush(const CUtensorMap* tm, const uint8_t* buf, int x, int y, bool reduce) {
+  fence_proxy_async_smem();
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) {
+    if (reduce)
+      tma_reduce_add_2d(tm, buf, x, y);
+    else
+      tma_store_2d(tm, buf, x, y);
+    bulk_commit();
+  }
+  __syncwarp();
 }
 
-// out[m, n..n+CH-1] = xo + gate[gate_off + n..] * v  (xo: the residual row chunk, loaded earlier)
-template <int CH>
-__device__ __forceinline__ void resid_cols(const Params& p, int m, int n, const float4 (&xo)[CH / 4],
-                                           const float (&v)[CH]) {
-  float g[CH];
-  if (p.gate) {
-    ldv<CH>(p.gate + p.gate_off + n, g);
-  } else {
-#pragma unroll
-    for (int j = 0; j < CH; ++j) g[j] = 1.f;
-  }
-  float4* o = reinterpret_cast<float4*>(static_cast<float*>(p.out) + static_cast<size_t>(m) * p.ldo + n);
-#pragma unroll
-  for (int j = 0; j < CH / 4; ++j) {
-    float4 c = xo[j];
-    c.x = fmaf(g[4 * j], v[4 * j], c.x);
-    c.y = fmaf(g[4 * j + 1], v[4 * j + 1], c.y);
-    c.z = fmaf(g[4 * j + 2], v[4 * j + 2], c.z);
-    c.w = fmaf(g[4 * j + 3], v[4 * j + 3], c.w);
-    o[j] = c;
-  }
+// Before rewriting a staging buffer: at most N of this warp's stores may still be reading.
+template <int N>
+__device__ __forceinline__ void stage_acquire() {
+  if ((threadIdx.x & 31) == 0) bulk_wait_read<N>();
+  __syncwarp();
 }
 
-// One tile's epilogue for this thread's row (m) over BN columns starting at n0.
+// One tile's epilogue for this warp's 32 rows (m = row of this lane) over BN columns from n0.
+// stage: this warp's two staging buffers; y0: first row of the warp's quadrant.
 template <int BN, int NPLANES>
-__device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t taddr, int m, int n0) {
+__device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap* tm_out, uint8_t* stage,
+                                              uint32_t taddr, int m, int y0, int n0) {
   const bool row_ok = m < p.M;
+  const int lane = threadIdx.x & 31;
+  const int esz = p.out_dtype == ANIMA_F32 ? 4 : 2;
+  const int chc = 128 / esz;      // columns per staging chunk
+  const int ppc = chc / 16;       // 16-column pieces per chunk
+  constexpr int CH = 16;
   if (p.out_mode == ANIMA_OUT_STORE || p.out_mode == ANIMA_OUT_RESID) {
-    // software pipeline over 16-column chunks: the TMEM loads of chunk c+1 are in flight while
-    // chunk c is finished; the residual chunk is requested before the math that precedes its use
-    constexpr int CH = 16;
+    // software pipeline over 16-column pieces: the TMEM loads of piece c+1 are in flight while
+    // piece c is finished and staged
+    const bool resid = p.out_mode == ANIMA_OUT_RESID;
     uint32_t rh[2][CH], rl[2][CH];
     issue_cols<BN, NPLANES, CH>(taddr, 0, rh[0], rl[0]);
     tmem_ld_wait(rh[0]);
     if constexpr (NPLANES == 2) tmem_ld_wait(rl[0]);
-    const bool resid = p.out_mode == ANIMA_OUT_RESID;
 #pragma unroll
     for (int c = 0; c < BN / CH; ++c) {
       const int cur = c & 1;
       if (c + 1 < BN / CH) issue_cols<BN, NPLANES, CH>(taddr, CH * (c + 1), rh[cur ^ 1], rl[cur ^ 1]);
-      float4 xo[CH / 4];
-      if (resid && row_ok) {
-        const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(p.out) +
-                                                            static_cast<size_t>(m) * p.ldo + n0 + CH * c);
-#pragma unroll
-        for (int j = 0; j < CH / 4; ++j) xo[j] = src[j];
-      }
+      const int col = CH * c;
+      const int chunk = col / chc, q = (col % chc) / CH;
+      uint8_t* buf = stage + (chunk & 1) * STAGE_BUF;
+      if (q == 0) stage_acquire<1>();
       float v[CH];
-      finish_cols<NPLANES, CH>(p, m, n0 + CH * c, row_ok, rh[cur], rl[cur], v, true);
-      if (row_ok) {
-        if (resid)
-          resid_cols<CH>(p, m, n0 + CH * c, xo, v);
-        else
-          store_cols<CH>(p.out, p.out_dtype, p.ldo, m, n0 + CH * c, v);
+      finish_cols<NPLANES, CH>(p, m, n0 + col, row_ok, rh[cur], rl[cur], v, true);
+      if (resid) {
+        float g[CH];
+        if (p.gate) {
+          ldv<CH>(p.gate + p.gate_off + n0 + col, g);
+#pragma unroll
+          for (int j = 0; j < CH; ++j) v[j] *= g[j];
+        }
       }
+      stage_piece(buf, lane, p.out_dtype, q, v);
+      if (q == ppc - 1) stage_flush(tm_out, buf, n0 + chunk * chc, y0, resid);
       if (c + 1 < BN / CH) {
         tmem_ld_wait(rh[cur ^ 1]);
         if constexpr (NPLANES == 2) tmem_ld_wait(rl[cur ^ 1]);
@@ -257,7 +272,6 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t taddr, i
   // Per-head RMSNorm (+ split-half RoPE for q/k heads of a fused qkv projection): a head is 128
   // consecutive columns and never straddles a tile (BN is a multiple of 128). Two passes over the
   // accumulator: sum of squares, then normalise (+ rotate) 16-column pieces.
-  constexpr int CH = 16;
 #pragma unroll 1
   for (int h0 = 0; h0 < BN; h0 += 128) {
     const int nh = n0 + h0;
@@ -266,10 +280,14 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t taddr, i
     const bool is_k = qkv && !is_q && nh < 2 * p.n_q;
     if (qkv && !is_q && !is_k) {  // v heads: plain store
 #pragma unroll 1
-      for (int c = 0; c < 128; c += CH) {
+      for (int col = 0; col < 128; col += CH) {
+        const int chunk = col / chc, q = (col % chc) / CH;
+        uint8_t* buf = stage + (chunk & 1) * STAGE_BUF;
+        if (q == 0) stage_acquire<1>();
         float v[CH];
-        load_cols<BN, NPLANES, CH>(p, taddr, h0 + c, m, nh + c, row_ok, v, true);
-        if (row_ok) store_cols<CH>(p.out, p.out_dtype, p.ldo, m, nh + c, v);
+        load_cols<BN, NPLANES, CH>(p, taddr, h0 + col, m, nh + col, row_ok, v, true);
+        stage_piece(buf, lane, p.out_dtype, q, v);
+        if (q == ppc - 1) stage_flush(tm_out, buf, nh + chunk * chc, y0, false);
       }
       continue;
     }
@@ -284,47 +302,55 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t taddr, i
     const float rs = 1.0f / sqrtf(ss * (1.0f / 128.0f) + p.eps);
     const float* w = is_k ? p.norm_k : p.norm_q;
     if (qkv) {
+      // pieces arrive in pairs (c, 64 + c): the two halves of the head fill buffers 0 and 1
       const int tok = row_ok ? (m % p.rope_rows) : 0;
       const float* cs = p.rope + static_cast<size_t>(tok) * 64;
       const float* sn = p.rope + static_cast<size_t>(p.rope_rows) * 64 + static_cast<size_t>(tok) * 64;
 #pragma unroll 1
       for (int c = 0; c < 64; c += CH) {
+        const int q = (c % chc) / CH;
+        if (q == 0) stage_acquire<0>();
         float v1[CH], v2[CH];
         load_cols<BN, NPLANES, CH>(p, taddr, h0 + c, m, nh + c, row_ok, v1, true);
         load_cols<BN, NPLANES, CH>(p, taddr, h0 + 64 + c, m, nh + 64 + c, row_ok, v2, true);
-        if (row_ok) {
-          float a[CH], b[CH];
-          ldv<CH>(w + c, a);
-          ldv<CH>(w + 64 + c, b);
+        float a[CH], b[CH];
+        ldv<CH>(w + c, a);
+        ldv<CH>(w + 64 + c, b);
 #pragma unroll
-          for (int j = 0; j < CH; ++j) {
-            v1[j] *= rs * a[j];
-            v2[j] *= rs * b[j];
-          }
-          ldv<CH>(cs + c, a);  // cos
-          ldv<CH>(sn + c, b);  // sin
+        for (int j = 0; j < CH; ++j) {
+          v1[j] *= rs * a[j];
+          v2[j] *= rs * b[j];
+        }
+        ldv<CH>(cs + c, a);  // cos
+        ldv<CH>(sn + c, b);  // sin
 #pragma unroll
-          for (int j = 0; j < CH; ++j) {
-            const float y1 = v1[j], y2 = v2[j];
-            v1[j] = y1 * a[j] - y2 * b[j];
-            v2[j] = y2 * a[j] + y1 * b[j];
-          }
-          store_cols<CH>(p.out, p.out_dtype, p.ldo, m, nh + c, v1);
-          store_cols<CH>(p.out, p.out_dtype, p.ldo, m, nh + 64 + c, v2);
+        for (int j = 0; j < CH; ++j) {
+          const float y1 = v1[j], y2 = v2[j];
+          v1[j] = y1 * a[j] - y2 * b[j];
+          v2[j] = y2 * a[j] + y1 * b[j];
+        }
+        stage_piece(stage, lane, p.out_dtype, q, v1);
+        stage_piece(stage + STAGE_BUF, lane, p.out_dtype, q, v2);
+        if (q == ppc - 1) {
+          const int x0 = nh + (c / chc) * chc;
+          stage_flush(tm_out, stage, x0, y0, false);
+          stage_flush(tm_out, stage + STAGE_BUF, x0 + 64, y0, false);
         }
       }
     } else {
 #pragma unroll 1
-      for (int c = 0; c < 128; c += CH) {
+      for (int col = 0; col < 128; col += CH) {
+        const int chunk = col / chc, q = (col % chc) / CH;
+        uint8_t* buf = stage + (chunk & 1) * STAGE_BUF;
+        if (q == 0) stage_acquire<1>();
         float v[CH];
-        load_cols<BN, NPLANES, CH>(p, taddr, h0 + c, m, nh + c, row_ok, v, true);
-        if (row_ok) {
-          float wv[CH];
-          ldv<CH>(w + c, wv);
+        load_cols<BN, NPLANES, CH>(p, taddr, h0 + col, m, nh + col, row_ok, v, true);
+        float wv[CH];
+        ldv<CH>(w + col, wv);
 #pragma unroll
-          for (int j = 0; j < CH; ++j) v[j] = v[j] * rs * wv[j];
-          store_cols<CH>(p.out, p.out_dtype, p.ldo, m, nh + c, v);
-        }
+        for (int j = 0; j < CH; ++j) v[j] = v[j] * rs * wv[j];
+        stage_piece(buf, lane, p.out_dtype, q, v);
+        if (q == ppc - 1) stage_flush(tm_out, buf, nh + chunk * chc, y0, false);
       }
     }
   }
@@ -341,11 +367,13 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
 template <int BN, int NPLANES>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tm_hi, const __grid_constant__ CUtensorMap tm_lo,
-                   const __grid_constant__ CUtensorMap tm_w, const Params p) {
+                   const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_out,
+                   const Params p) {
   using C = Cfg<BN, NPLANES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  uint8_t* staging = smem + C::STAGES * C::STAGE_BYTES;  // 1024-aligned (stage sizes are)
+  uint64_t* full = reinterpret_cast<uint64_t*>(staging + C::STAGING_BYTES);
   uint64_t* empty = full + C::STAGES;
   uint64_t* acc_full = empty + C::STAGES;
   uint64_t* acc_empty = acc_full + 2;
@@ -374,6 +402,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     tma_prefetch_desc(&tm_hi);
     if (NPLANES == 2) tma_prefetch_desc(&tm_lo);
     tma_prefetch_desc(&tm_w);
+    tma_prefetch_desc(&tm_out);
   }
   if (warp == kMmaWarp) {
     tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -487,11 +516,15 @@ __global__ void __launch_bounds__(THREADS, 1)
       int mb, nb;
       tile_coords(p, tile, mb, nb);
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + buf * C::ACC_COLS;
-      epilogue_tile<BN, NPLANES>(p, taddr, mb * BM + row, nb * BN);
+      epilogue_tile<BN, NPLANES>(p, &tm_out, staging + warp * 2 * STAGE_BUF, taddr, mb * BM + row,
+                                 mb * BM + quad * 32, nb * BN);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
     }
+    // every staged store has finished (shared memory is read and the global writes are done)
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
   }
   tc_fence_before();
   __syncthreads();
@@ -522,6 +555,19 @@ int launch(anima_ctx* ctx, const anima_qact* x, const anima_weight* W, const ani
   uint32_t wbox[2] = {BK, BN};
   st = make_tmap(&tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, W->data, wdims, wstr, wbox, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st) return st;
+  // output: boxes of 128 bytes (32 fp32 or 64 16-bit columns) x 32 rows, one per epilogue warp chunk
+  CUtensorMap tm_out;
+  {
+    const int esz = o->out_dtype == ANIMA_F32 ? 4 : 2;
+    const CUtensorMapDataType odt = o->out_dtype == ANIMA_F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                    : o->out_dtype == ANIMA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                                 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    uint64_t odims[2] = {static_cast<uint64_t>(N), static_cast<uint64_t>(M)};
+    uint64_t ostr[1] = {static_cast<uint64_t>(o->ldo) * esz};
+    uint32_t obox[2] = {static_cast<uint32_t>(128 / esz), 32};
+    st = make_tmap(&tm_out, odt, 2, o->out, odims, ostr, obox, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+  }
 
   Params p{};
   p.M = M;
@@ -564,7 +610,7 @@ int launch(anima_ctx* ctx, const anima_qact* x, const anima_weight* W, const ani
   const int grid = p.num_tiles < ctx->num_sms ? p.num_tiles : ctx->num_sms;
   ProfScope prof(ctx, NPLANES == 2 ? "linear.i8x2" : "linear.i8", 2.0 * M * N * K,
                  static_cast<double>(M) * K * NPLANES + static_cast<double>(N) * K);
-  gemm_i8_kernel<BN, NPLANES><<<grid, THREADS, C::SMEM_BYTES, ctx->stream>>>(tm_hi, tm_lo, tm_w, p);
+  gemm_i8_kernel<BN, NPLANES><<<grid, THREADS, C::SMEM_BYTES, ctx->stream>>>(tm_hi, tm_lo, tm_w, tm_out, p);
   return check_launch("gemm_i8_kernel");
 }
 

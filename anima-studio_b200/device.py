@@ -15,7 +15,7 @@ import threading
 import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libanima_b200.so")
+LIB_PATH = os.environ.get("ANIMA_LIB", os.path.join(HERE, "libanima_b200.so"))
 
 ANIMA_F32, ANIMA_BF16, ANIMA_F16, ANIMA_I8, ANIMA_U8 = range(5)
 ACT = {None: 0, "none": 0, "gelu": 1, "silu": 2}

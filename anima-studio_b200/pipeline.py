@@ -49,6 +49,69 @@ def denoise_loop(dit: AnimaDiT, noise: torch.Tensor, cond: Cond, steps: int, cfg
     return x
 
 
+class GraphedSampler:
+    """The denoising loop captured as CUDA graphs, one per step (forward + CFG + Euler update), so a
+    step replays ~400 kernel launches without host work in between. The latent lives in a static
+    device buffer; load() copies a new starting latent in (x = noise * sigma_0 is done by the
+    caller or by start()). Graphs share one memory pool and are replayed in order. Each replay adds
+    the number of library kernels its capture enqueued to device.Context.launches."""
+
+    def __init__(self, dit: AnimaDiT, cond: Cond, steps: int, batch: int, h: int, w: int, cfg: float = 1.0,
+                 uncond: Cond | None = None, shift: float = 3.0):
+        self.dit, self.steps = dit, steps
+        self.sig = sigmas_simple(steps, shift)
+        self.tcs = dit.time_cond_batch(self.sig[:-1])
+        self.guided = uncond is not None and cfg != 1.0
+        self.cond = Cond.stack([cond, uncond]) if self.guided else cond
+        self.cfg = cfg
+        self.x = torch.zeros(batch, 16, h, w, dtype=torch.float32, device=dit.device)
+        self.B = batch
+        self.pool = None
+        self.graphs = []
+        stream = torch.cuda.Stream(device=dit.device)
+        stream.wait_stream(torch.cuda.current_stream(dit.device))
+        with torch.cuda.stream(stream):
+            self._step(0)  # warm-up outside capture: kernel attributes, buffers, tensor maps
+        torch.cuda.current_stream(dit.device).wait_stream(stream)
+        torch.cuda.synchronize(dit.device)
+        self.x.zero_()
+        self.launches = []  # library kernels in each captured step
+        from .device import Context
+        for i in range(steps):
+            g = torch.cuda.CUDAGraph()
+            n0 = Context.launches
+            with torch.cuda.graph(g, pool=self.pool, stream=stream):
+                self._step(i)
+            self.launches.append(Context.launches - n0)
+            self.pool = g.pool()
+            self.graphs.append(g)
+        torch.cuda.synchronize(dit.device)
+
+    def _step(self, i: int):
+        s, s1 = self.sig[i], self.sig[i + 1]
+        if self.guided:
+            v2 = self.dit.forward(torch.cat([self.x, self.x]), self.cond, self.tcs[i])
+            ops.euler_step(self.x, v2[: self.B].contiguous(), s, s1, v_uncond=v2[self.B:].contiguous(), cfg=self.cfg)
+        else:
+            v = self.dit.forward(self.x, self.cond, self.tcs[i])
+            ops.euler_step(self.x, v, s, s1)
+
+    def start(self, noise: torch.Tensor):
+        """x <- noise * sigma_0 (the first Euler state)."""
+        self.x.copy_(noise.to(self.x.device, torch.float32) * np.float32(self.sig[0]))
+
+    def replay(self, i: int):
+        from .device import Context
+        self.graphs[i].replay()
+        Context.launches += self.launches[i]
+
+    def run(self, noise: torch.Tensor) -> torch.Tensor:
+        self.start(noise)
+        for g in self.graphs:
+            g.replay()
+        return self.x
+
+
 def generate(dit: AnimaDiT, noise, ctx, steps: int = 8, cfg: float = 1.0, ctx_neg=None, key_len=None,
              key_len_neg=None, shift: float = 3.0) -> np.ndarray:
     """The public end-to-end call: host noise [B, 16, h, w] and text context(s) [Lk, 1024] in,

@@ -285,6 +285,7 @@ def main():
     ap.add_argument("--attn", default="f16", choices=["bf16", "f16"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-graph", action="store_true", help="launch kernels from Python per step instead of CUDA graphs")
     args = ap.parse_args()
     world, rank, local = setup_dist()
     if args.kernel:
@@ -318,12 +319,21 @@ def main():
     tcs = dit.time_cond_batch(sig[:-1])
     noise = syn.randn(seed + rank, "noise", (1, 16, 128, 128)).cuda()
     x = noise * sig[0]
+    graphed = None
+    if not args.no_graph:
+        graphed = pl.GraphedSampler(dit, cond, 8, 1, 128, 128)
+        graphed.start(noise)
 
     def step(i):
         j = i % 8
+        if graphed is not None:
+            graphed.replay(j)
+            if j == 7:  # next image: restart from the noise
+                graphed.start(noise)
+            return
         v = dit.forward(x, cond, tcs[j])
         ops.euler_step(x, v, sig[j], sig[j + 1])
-        if j == 7:  # next image: restart from the noise
+        if j == 7:
             x.copy_(noise * sig[0])
 
     def barrier():
@@ -355,8 +365,11 @@ def main():
     # Per-kernel durations: an instrumented replay of the same steps (CUDA events around each
     # launch on the launching stream), for the roofline of the dominant kernel.
     with dev.KernelTimer({"anima_linear", "anima_attention"}) as kt:
-        for i in range(min(args.steps, 8)):
-            step(args.warmup + args.steps + i)
+        xr = noise * sig[0]
+        for i in range(min(args.steps, 8)):  # eager launches, so each kernel is bracketed by events
+            j = i % 8
+            v = dit.forward(xr, cond, tcs[j])
+            ops.euler_step(xr, v, sig[j], sig[j + 1])
     summ = kt.summary()
     replay_steps = min(args.steps, 8)
 
@@ -366,24 +379,26 @@ def main():
     if not args.no_e2e:
         xh = torch.empty(1, 16, 128, 128, pin_memory=True)
         xh.copy_(x.cpu())
-        xd = torch.empty_like(x)
-        for i in range(2):
+        xd = graphed.x if graphed is not None else torch.empty_like(x)
+
+        def e2e_step(j):
             xd.copy_(xh, non_blocking=True)
-            v = dit.forward(xd, cond, tcs[i])
-            ops.euler_step(xd, v, sig[i], sig[i + 1])
+            if graphed is not None:
+                graphed.replay(j)
+            else:
+                v = dit.forward(xd, cond, tcs[j])
+                ops.euler_step(xd, v, sig[j], sig[j + 1])
             xh.copy_(xd, non_blocking=True)
+
+        for i in range(2):
+            e2e_step(i)
         torch.cuda.synchronize()
         barrier()
         t0 = time.perf_counter()
         f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         f0.record()
         for i in range(args.steps):
-            j = i % 8
-            xd.copy_(xh, non_blocking=True)
-            tc = dit.time_cond(sig[j])
-            v = dit.forward(xd, cond, tc)
-            ops.euler_step(xd, v, sig[j], sig[j + 1])
-            xh.copy_(xd, non_blocking=True)
+            e2e_step(i % 8)
         f1.record()
         torch.cuda.synchronize()
         wall = time.perf_counter() - t0
@@ -394,8 +409,9 @@ def main():
         nbytes = xh.numel() * 4
         e2e = {"value": world * args.steps / (float(et.item()) * 1e-3), "unit": "steps/s",
                "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes,
-               "api": "per step: pinned host latent -> device, time_cond(sigma), AnimaDiT.forward, "
-                      "euler_step, latent -> pinned host (the reference's per-pass host round trip, dit.js:256,322)"}
+               "api": "per step: pinned host latent -> device, pipeline.GraphedSampler step (AnimaDiT.forward + "
+                      "euler_step as one CUDA graph), latent -> pinned host (the reference's per-pass host round trip, "
+                      "dit.js:256,322)"}
 
     peaks = load_peaks()
     int8_peak = measure_int8_peak(torch) if rank == 0 else None
@@ -445,6 +461,7 @@ def main():
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8", "data": "synthetic",
             "config": {"workload": WORKLOAD, "tokens": 4096, "blocks": 28, "batch_per_gpu": 1,
+                       "launch": "CUDA graph per step" if graphed is not None else "eager",
                        "precision": args.precision, "attention": args.attn, "ctx_rows": 512,
                        "parallelism": f"dp{world}", "images_per_s": value / 8,
                        "l2": "inputs larger than L2: 1.5 GB of int8 weights stream through every step"},
