@@ -72,64 +72,231 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
-// 256-point ConvRot Hadamard of the group held by one warp, lane l holding elements 8l..8l+7:
-// y = x H, H = kron(H4, H4, H4, H4) / 16 with the regular H4 = [[1,1,1,-1],[1,1,-1,1],
-// [1,-1,1,1],[-1,1,1,1]] (tools/quant.py:30-38). Index i = d0 + 4 d1 + 16 d2 + 64 d3; each
-// base-4 digit gets one 4-point transform, y[d] = (x0 + x1 + x2 + x3) - 2 x[3 - d].
-// d0 and the low bit of d1 are within the thread; the rest of d1 is lane bit 0, d2 lane bits
-// 1-2 and d3 lane bits 3-4, reached with xor shuffles.
-__device__ __forceinline__ void fwht256_warp(float (&x)[8]) {
-  const int lane = threadIdx.x & 31;
-  // digit 0: elements j, j+1, j+2, j+3 of each half
+// ------------------------------------------------------------------ packed fp32 pairs
+// sm_100 issues two fp32 adds, multiplies or FMAs per instruction on a register pair; the row
+// kernels keep their data as float2 pairs of neighbouring elements so the bulk of the arithmetic
+// uses these.
+using f2 = float2;
+__device__ __forceinline__ f2 dup2(float a) { return make_float2(a, a); }
+__device__ __forceinline__ f2 add2(f2 a, f2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ f2 mul2(f2 a, f2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ f2 fma2(f2 a, f2 b, f2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ f2 sub2(f2 a, f2 b) { return __ffma2_rn(b, dup2(-1.0f), a); }
+
+template <typename T>
+__device__ __forceinline__ void load16p(const T* p, f2 (&x)[8]) {
+  if constexpr (sizeof(T) == 4) {
 #pragma unroll
-  for (int h = 0; h < 8; h += 4) {
-    const float s = x[h] + x[h + 1] + x[h + 2] + x[h + 3];
-    const float a0 = x[h], a1 = x[h + 1], a2 = x[h + 2], a3 = x[h + 3];
-    x[h] = s - 2.f * a3;
-    x[h + 1] = s - 2.f * a2;
-    x[h + 2] = s - 2.f * a1;
-    x[h + 3] = s - 2.f * a0;
-  }
-  // digit 1: e = (j >> 2) + 2 (lane & 1); partner lane ^ 1 holds the other two values
-  {
-    float p[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) p[j] = __shfl_xor_sync(0xffffffffu, x[j], 1);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float s = x[j] + x[j + 4] + p[j] + p[j + 4];
-      // own d = 2b + t; x[3 - d] lives in the partner at t' = 1 - t
-      const float y0 = s - 2.f * p[j + 4];
-      const float y1 = s - 2.f * p[j];
-      x[j] = y0;
-      x[j + 4] = y1;
+    for (int k = 0; k < 4; ++k) {
+      const float4 a = reinterpret_cast<const float4*>(p)[k];
+      x[2 * k] = make_float2(a.x, a.y);
+      x[2 * k + 1] = make_float2(a.z, a.w);
     }
-    (void)lane;
-  }
-  // digit 2: lanes differing in bits 1-2; x[3 - d] sits at lane ^ 6
+  } else {
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const float a = x[j] + __shfl_xor_sync(0xffffffffu, x[j], 2);
-    const float s = a + __shfl_xor_sync(0xffffffffu, a, 4);
-    x[j] = s - 2.f * __shfl_xor_sync(0xffffffffu, x[j], 6);
-  }
-  // digit 3: lanes differing in bits 3-4; x[3 - d] sits at lane ^ 24
+    for (int k = 0; k < 2; ++k) {
+      const uint4 u = reinterpret_cast<const uint4*>(p)[k];
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const float a = x[j] + __shfl_xor_sync(0xffffffffu, x[j], 8);
-    const float s = a + __shfl_xor_sync(0xffffffffu, a, 16);
-    x[j] = s - 2.f * __shfl_xor_sync(0xffffffffu, x[j], 24);
+      for (int i = 0; i < 4; ++i) {
+        if constexpr (std::is_same<T, __half>::value)
+          x[4 * k + i] = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+        else
+          x[4 * k + i] = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+      }
+    }
   }
-#pragma unroll
-  for (int j = 0; j < 8; ++j) x[j] *= 0.0625f;
 }
 
+template <typename T>
+__device__ __forceinline__ void store16p(T* p, const f2 (&x)[8]) {
+  if constexpr (sizeof(T) == 4) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      reinterpret_cast<float4*>(p)[k] = make_float4(x[2 * k].x, x[2 * k].y, x[2 * k + 1].x, x[2 * k + 1].y);
+  } else {
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      uint32_t w[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        if constexpr (std::is_same<T, __half>::value) {
+          const __half2 h = __floats2half2_rn(x[4 * k + i].x, x[4 * k + i].y);
+          w[i] = *reinterpret_cast<const uint32_t*>(&h);
+        } else {
+          const __nv_bfloat162 h = __floats2bfloat162_rn(x[4 * k + i].x, x[4 * k + i].y);
+          w[i] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+      }
+      reinterpret_cast<uint4*>(p)[k] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+}
+
+__device__ __forceinline__ float rcp_approx(float x) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+__device__ __forceinline__ float ex2_approx(float x) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
+// GELU(x) = x Phi(x) on a pair, with erf from Abramowitz & Stegun 7.1.26 (|error| <= 1.5e-7):
+// erf(a) = 1 - t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) exp(-a^2), t = 1 / (1 + p a)
+__device__ __forceinline__ f2 gelu2(f2 x) {
+  const f2 z = mul2(x, dup2(0.70710678118654752f));
+  const f2 a = make_float2(fabsf(z.x), fabsf(z.y));
+  const f2 d = fma2(a, dup2(0.3275911f), dup2(1.0f));
+  const f2 t = make_float2(rcp_approx(d.x), rcp_approx(d.y));
+  f2 q = fma2(dup2(1.061405429f), t, dup2(-1.453152027f));
+  q = fma2(q, t, dup2(1.421413741f));
+  q = fma2(q, t, dup2(-0.284496736f));
+  q = fma2(q, t, dup2(0.254829592f));
+  q = mul2(q, t);
+  const f2 n = mul2(a, mul2(a, dup2(-1.4426950408889634f)));  // -a^2 log2(e)
+  const f2 e = make_float2(ex2_approx(n.x), ex2_approx(n.y));
+  const f2 r = fma2(q, e, dup2(-1.0f));  // -erf(|z|)
+  // w = sign(z) erf(|z|): flip r unless z is negative
+  const f2 w = make_float2(__uint_as_float(__float_as_uint(r.x) ^ (~__float_as_uint(z.x) & 0x80000000u)),
+                           __uint_as_float(__float_as_uint(r.y) ^ (~__float_as_uint(z.y) & 0x80000000u)));
+  const f2 h = mul2(x, dup2(0.5f));
+  return fma2(h, w, h);
+}
+
+// ------------------------------------------------------------------ ConvRot Hadamard (256-point)
+// y = x H per group of 256, H = kron(H4, H4, H4, H4) / 16 with the regular
+// H4 = [[1,1,1,-1],[1,1,-1,1],[1,-1,1,1],[-1,1,1,1]] (tools/quant.py:30-38). Within a group,
+// element i = d0 + 4 d1 + 16 d2 + 64 d3 (base-4 digits, d3 the outermost kron factor).
+//
+// With D = diag(1,1,1,-1), D H4 D is the Sylvester (Walsh) matrix with rows 1 and 2 swapped, so
+// H4 = D W4 P D per digit and, for the whole group,
+//     y[j] = sigma(j) * WHT(sigma * x)[swap(j)] / 16
+// where sigma(i) = (-1)^(number of digits equal to 3), WHT is the natural-order Walsh-Hadamard
+// transform over the 8 index bits (radix-2 butterflies) and swap() exchanges the two bits of
+// every digit. sigma on the input is folded into the first butterfly stage, swap() into the
+// shared-memory addressing, sigma on the output into the caller's per-element multiplier.
+//
+// A half-warp holds one group, lane t the 16 consecutive elements 16t..16t+15 as 8 float2 pairs,
+// so index bits 0-3 are in the thread (bit 0 within a pair) and bits 4-7 pick the lane. The
+// transform runs bits 0-3 in registers, transposes the 16 x 16 tile through shared memory
+// (lane c then holds elements c + 16 b, b = 0..15, pairs (b, b+1)), runs bits 4-7, and
+// transposes back with swap() applied, leaving lane t with y[16t .. 16t+15] up to sigma and 1/16.
+
+// sigma over a 4-bit index (two base-4 digits)
+__host__ __device__ constexpr float sgn4(int a) { return ((a & 3) == 3) != ((a >> 2) == 3) ? -1.f : 1.f; }
+__host__ __device__ constexpr int swap4(int a) { return ((a & 5) << 1) | ((a >> 1) & 5); }
+
+// natural-order WHT over 4 bits held as 8 pairs, with sigma applied to the input
+__device__ __forceinline__ void wht16(f2 (&P)[8]) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {  // bit 0, within the pair
+    const float p = sgn4(2 * j) < 0 ? -P[j].x : P[j].x;
+    const float q = sgn4(2 * j + 1) < 0 ? -P[j].y : P[j].y;
+    P[j] = make_float2(p + q, p - q);
+  }
+#pragma unroll
+  for (int m = 1; m < 8; m <<= 1)  // bits 1-3, across pairs
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (!(j & m)) {
+        const f2 a = P[j], b = P[j | m];
+        P[j] = add2(a, b);
+        P[j | m] = sub2(a, b);
+      }
+}
+
+// One 16 x 16 fp32 tile per half-warp, row stride 20 words. The second half-warp's tile starts 336
+// words (16 mod 32) after the first, so a column access by the whole warp touches each bank once;
+// the 16-byte row accesses are conflict-free because 20 t mod 32 differs for any 8 consecutive t.
+constexpr int kTileStride = 20;
+constexpr int kTileHalf = 336;
+constexpr int kTileWords = kTileHalf + 16 * kTileStride;  // per warp
+
+// P: lane t's 16 consecutive elements of a group. Returns them transformed (unscaled, without the
+// output sigma), still lane t's 16 consecutive output positions.
+__device__ __forceinline__ void hadamard256(float* tb, int t, f2 (&P)[8]) {
+  wht16(P);  // bits 0-3
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+    *reinterpret_cast<float4*>(tb + t * kTileStride + 4 * k) = make_float4(P[2 * k].x, P[2 * k].y, P[2 * k + 1].x, P[2 * k + 1].y);
+  __syncwarp();
+#pragma unroll
+  for (int j = 0; j < 8; ++j) P[j] = make_float2(tb[(2 * j) * kTileStride + t], tb[(2 * j + 1) * kTileStride + t]);
+  __syncwarp();
+  wht16(P);  // bits 4-7; P[j] = u[t + 16 (2j)], u[t + 16 (2j + 1)]
+  const int ct = swap4(t);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    tb[swap4(2 * j) * kTileStride + ct] = P[j].x;
+    tb[swap4(2 * j + 1) * kTileStride + ct] = P[j].y;
+  }
+  __syncwarp();
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float4 q = *reinterpret_cast<const float4*>(tb + t * kTileStride + 4 * k);
+    P[2 * k] = make_float2(q.x, q.y);
+    P[2 * k + 1] = make_float2(q.z, q.w);
+  }
+  __syncwarp();
+}
+
+// Per-pair multipliers that apply the output sigma: sigma(16 t + a) = sgn4(t) sgn4(a), and over
+// the pair (a, a + 1) = (2j, 2j + 1) sgn4 takes the patterns (+,+), (+,-), (-,-), (-,+).
+struct PairScale {
+  f2 pp, pm, mm, mp;
+  __device__ __forceinline__ PairScale(float w, bool signed_out) {
+    pp = dup2(w);
+    pm = signed_out ? make_float2(w, -w) : pp;
+    mm = signed_out ? dup2(-w) : pp;
+    mp = signed_out ? make_float2(-w, w) : pp;
+  }
+  __device__ __forceinline__ f2 of(int j) const {
+    const bool lo = sgn4(2 * j) > 0, hi = sgn4(2 * j + 1) > 0;
+    return lo ? (hi ? pp : pm) : (hi ? mp : mm);
+  }
+};
+
 // ------------------------------------------------------------------ row kernel: LN + adaLN, ConvRot, quant
-// One row per warp for rows up to 1024 wide (WPR = 1), WPR = cols / 1024 warps per row beyond;
-// 8 warps per CTA. Lane l holds, for each of the warp's G groups of 256 columns, the 8 consecutive
-// elements 8l..8l+7 of that group, so every warp access is a contiguous 256-element segment and
-// every ConvRot group lives in one warp (fwht256_warp). Reductions are warp shuffles, plus one
-// shared-memory step across the WPR warps of a row.
+// Geometry: a warp pass covers two groups of 256 columns, one per half-warp; a warp makes G2
+// passes and WPR warps share a row. Rows of a single group are handled by one half-warp each.
+// Every warp access is a contiguous 1 KB (fp32) or 512 B (16-bit) segment.
+template <int COLS>
+struct RowGeom {
+  static constexpr int NG = COLS / 256;
+  static constexpr bool HALF = NG == 1;
+  static constexpr int G2 = NG >= 4 ? 2 : 1;
+  static constexpr int WPR = HALF ? 1 : NG / (2 * G2);
+  static constexpr int RPC = HALF ? 16 : 8 / WPR;  // rows per 256-thread CTA
+  static_assert(COLS % 256 == 0 && NG <= 64 && (HALF || NG % (2 * G2) == 0) && WPR <= 8, "unsupported row width");
+};
+
+// Sum or max over the row: (half-)warp shuffles, then one shared-memory step across the WPR warps.
+template <int COLS, bool MAX>
+__device__ __forceinline__ float row_reduce(float v, float* red) {
+  using Gm = RowGeom<COLS>;
+#pragma unroll
+  for (int o = Gm::HALF ? 8 : 16; o > 0; o >>= 1) {
+    const float w = __shfl_xor_sync(0xffffffffu, v, o);
+    v = MAX ? fmaxf(v, w) : v + w;
+  }
+  if constexpr (Gm::WPR == 1) {
+    return v;
+  } else {
+    const int warp = threadIdx.x >> 5;
+    const int base = (warp / Gm::WPR) * Gm::WPR;
+    if ((threadIdx.x & 31) == 0) red[warp] = v;
+    __syncthreads();
+    float s = red[base];
+#pragma unroll
+    for (int i = 1; i < Gm::WPR; ++i) s = MAX ? fmaxf(s, red[base + i]) : s + red[base + i];
+    __syncthreads();
+    return s;
+  }
+}
+
 //   LN      y = LN(x) * (1 + mod[scale_off + c]) + mod[shift_off + c]  (fp32 two-pass mean/var,
 //           biased variance, eps: tools/reference.py:190-191, kernels.js:95-145)
 //   act     y <- GELU(y) (the MLP's activation, applied here when the layer1 GEMM stored its
@@ -137,122 +304,124 @@ __device__ __forceinline__ void fwht256_warp(float (&x)[8]) {
 //   rotate  y <- y H per 256 group (tools/quant.py:30-45)
 //   quant   s = amax / 127; a = y * (127 / amax); hi = rne(a); lo = rne((a - hi) * 254)
 //           (|a| <= 127 and |a - hi| <= 1/2, so neither needs clamping)
-template <int WPR>
-__device__ __forceinline__ float row_reduce(float v, float* red, bool is_max) {
-  v = is_max ? warp_max(v) : warp_sum(v);
-  if constexpr (WPR == 1) {
-    return v;
-  } else {
-    const int warp = threadIdx.x >> 5;
-    const int base = (warp / WPR) * WPR;
-    if ((threadIdx.x & 31) == 0) red[warp] = v;
-    __syncthreads();
-    float t = red[base];
-#pragma unroll
-    for (int i = 1; i < WPR; ++i) t = is_max ? fmaxf(t, red[base + i]) : t + red[base + i];
-    __syncthreads();
-    return t;
-  }
-}
-
 template <int COLS, typename TIn, typename TOut, bool LN>
-__global__ void __launch_bounds__(256) rows_kernel(const TIn* __restrict__ x, int rows, int ldx,
+__global__ void __launch_bounds__(256, 4) rows_kernel(const TIn* __restrict__ x, int rows, int ldx,
                                                    const float* __restrict__ mod, int shift_off, int scale_off,
                                                    float eps, int rotate, TOut* y, int8_t* qhi, int8_t* qlo,
                                                    float* qscale, int qld, int act) {
-  constexpr int WPR = COLS > 1024 ? COLS / 1024 : 1;  // warps per row: at most 4 groups of 256 per warp
-  constexpr int G = COLS / 256 / WPR;
-  constexpr int RPC = 8 / WPR;
-  static_assert(G >= 1 && G <= 8 && COLS % 256 == 0, "unsupported row width");
+  using Gm = RowGeom<COLS>;
+  constexpr int G2 = Gm::G2;
   __shared__ float red[8];
+  __shared__ __align__(16) float tiles[8 * kTileWords];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row = blockIdx.x * RPC + warp / WPR;
-  const int wr = warp % WPR;
+  const int half = lane >> 4, t = lane & 15;
+  const int row = Gm::HALF ? blockIdx.x * 16 + warp * 2 + half : blockIdx.x * Gm::RPC + warp / Gm::WPR;
+  const int wr = Gm::HALF ? 0 : warp % Gm::WPR;
   const bool valid = row < rows;
   const size_t r = valid ? static_cast<size_t>(row) : 0;
-  float v[G][8];
-  int col[G];
+  float* tb = tiles + warp * kTileWords + half * kTileHalf;
+  f2 v[G2][8];
+  int col[G2];
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    col[g] = (wr * G + g) * 256 + 8 * lane;
+  for (int p = 0; p < G2; ++p) {
+    col[p] = Gm::HALF ? 16 * t : ((wr * G2 + p) * 2 + half) * 256 + 16 * t;
     if (valid) {
-      load8(x + r * ldx + col[g], v[g]);
+      load16p(x + r * ldx + col[p], v[p]);
     } else {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) v[g][j] = 0.f;
+      for (int j = 0; j < 8; ++j) v[p][j] = dup2(0.f);
     }
   }
   if constexpr (LN) {
-    float sum = 0.f;
+    f2 s2 = dup2(0.f);
 #pragma unroll
-    for (int g = 0; g < G; ++g)
+    for (int p = 0; p < G2; ++p)
 #pragma unroll
-      for (int j = 0; j < 8; ++j) sum += v[g][j];
-    const float mean = row_reduce<WPR>(sum, red, false) / static_cast<float>(COLS);
-    float sq = 0.f;
+      for (int j = 0; j < 8; ++j) s2 = add2(s2, v[p][j]);
+    const float mean = row_reduce<COLS, false>(s2.x + s2.y, red) / static_cast<float>(COLS);
+    const f2 nm = dup2(-mean);
+    f2 q2 = dup2(0.f);
 #pragma unroll
-    for (int g = 0; g < G; ++g)
+    for (int p = 0; p < G2; ++p)
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const float d = v[g][j] - mean;
-        sq += d * d;
+        v[p][j] = add2(v[p][j], nm);
+        q2 = fma2(v[p][j], v[p][j], q2);
       }
-    const float var = row_reduce<WPR>(sq, red, false) / static_cast<float>(COLS);
-    const float rstd = 1.0f / sqrtf(var + eps);
+    const float var = row_reduce<COLS, false>(q2.x + q2.y, red) / static_cast<float>(COLS);
+    const f2 rs = dup2(1.0f / sqrtf(var + eps));
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      float sc[8], sh[8];
-      load8(mod + scale_off + col[g], sc);
-      load8(mod + shift_off + col[g], sh);
+    for (int p = 0; p < G2; ++p)
 #pragma unroll
-      for (int j = 0; j < 8; ++j) v[g][j] = (v[g][j] - mean) * rstd * (1.0f + sc[j]) + sh[j];
-    }
+      for (int k = 0; k < 4; ++k) {
+        const float4 sc = *reinterpret_cast<const float4*>(mod + scale_off + col[p] + 4 * k);
+        const float4 sh = *reinterpret_cast<const float4*>(mod + shift_off + col[p] + 4 * k);
+        // (x - mean) * (rstd * (1 + scale)) + shift
+        v[p][2 * k] = fma2(v[p][2 * k], fma2(rs, make_float2(sc.x, sc.y), rs), make_float2(sh.x, sh.y));
+        v[p][2 * k + 1] = fma2(v[p][2 * k + 1], fma2(rs, make_float2(sc.z, sc.w), rs), make_float2(sh.z, sh.w));
+      }
   }
   if (act == ANIMA_ACT_GELU) {
 #pragma unroll
-    for (int g = 0; g < G; ++g)
+    for (int p = 0; p < G2; ++p)
 #pragma unroll
-      for (int j = 0; j < 8; ++j) v[g][j] = gelu_erf(v[g][j]);
+      for (int j = 0; j < 8; ++j) v[p][j] = gelu2(v[p][j]);
   }
   if (rotate) {
 #pragma unroll
-    for (int g = 0; g < G; ++g) fwht256_warp(v[g]);
+    for (int p = 0; p < G2; ++p) hadamard256(tb, t, v[p]);
   }
+  // the output sigma of the Hadamard for this lane's 16 positions (index bits 4-7 are t)
+  const float lane_sign = rotate ? sgn4(t) : 1.0f;
   if (qhi) {
     float amax = 0.f;
 #pragma unroll
-    for (int g = 0; g < G; ++g)
+    for (int p = 0; p < G2; ++p)
 #pragma unroll
-      for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[g][j]));
-    amax = row_reduce<WPR>(amax, red, true);
+      for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fmaxf(fabsf(v[p][j].x), fabsf(v[p][j].y)));
+    amax = row_reduce<COLS, true>(amax, red);
     if (!valid) return;
+    // a = (y / 16) * 127 / (amax / 16) = y * (127 / amax) for the unscaled y: the 1/16 is a power of
+    // two, so this is the same fp32 value as quantizing the scaled y
+    const float post = rotate ? 0.0625f : 1.0f;
     const float inv = amax > 0.f ? 127.0f / amax : 0.f;
-    if (wr == 0 && lane == 0) qscale[r] = amax > 0.f ? amax / 127.0f : 1.0f;
+    if (wr == 0 && (Gm::HALF ? t : lane) == 0) qscale[r] = amax > 0.f ? (amax * post) / 127.0f : 1.0f;
+    const PairScale ps(inv * lane_sign, rotate != 0);
+    const f2 magic = dup2(12582912.0f), nmagic = dup2(-12582912.0f), c254 = dup2(254.0f);
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      uint32_t h2[2], l2[2];
+    for (int p = 0; p < G2; ++p) {
+      uint32_t hw[4], lw[4];
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        // round to nearest even through the 1.5 * 2^23 magic number (|a| <= 127, |lo| <= 127):
-        // integer values come straight out of the float's mantissa, no conversion unit needed
-        int hv[4], lv[4];
+      for (int k = 0; k < 4; ++k) {
+        // round to nearest even through the 1.5 * 2^23 magic number: the float's low byte is then
+        // the two's-complement int8 of the rounded value (|a| <= 127, |lo| <= 127)
+        uint32_t hb[4], lb[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float a = v[g][4 * half + j] * inv;
-          const float t = a + 12582912.0f;
-          hv[j] = __float_as_int(t) - 0x4B400000;
-          const float rem = a - (t - 12582912.0f);
-          lv[j] = __float_as_int(fmaf(rem, 254.0f, 12582912.0f)) - 0x4B400000;
+        for (int i = 0; i < 2; ++i) {
+          const int j = 2 * k + i;
+          const f2 a = mul2(v[p][j], ps.of(j));
+          const f2 m = add2(a, magic);
+          const f2 rem = sub2(a, add2(m, nmagic));
+          const f2 l = fma2(rem, c254, magic);
+          hb[2 * i] = __float_as_uint(m.x);
+          hb[2 * i + 1] = __float_as_uint(m.y);
+          lb[2 * i] = __float_as_uint(l.x);
+          lb[2 * i + 1] = __float_as_uint(l.y);
         }
-        h2[half] = __byte_perm(__byte_perm(hv[0], hv[1], 0x0040), __byte_perm(hv[2], hv[3], 0x0040), 0x5410);
-        l2[half] = __byte_perm(__byte_perm(lv[0], lv[1], 0x0040), __byte_perm(lv[2], lv[3], 0x0040), 0x5410);
+        hw[k] = __byte_perm(__byte_perm(hb[0], hb[1], 0x0040), __byte_perm(hb[2], hb[3], 0x0040), 0x5410);
+        lw[k] = __byte_perm(__byte_perm(lb[0], lb[1], 0x0040), __byte_perm(lb[2], lb[3], 0x0040), 0x5410);
       }
-      *reinterpret_cast<uint2*>(qhi + r * qld + col[g]) = make_uint2(h2[0], h2[1]);
-      if (qlo) *reinterpret_cast<uint2*>(qlo + r * qld + col[g]) = make_uint2(l2[0], l2[1]);
+      *reinterpret_cast<uint4*>(qhi + r * qld + col[p]) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+      if (qlo) *reinterpret_cast<uint4*>(qlo + r * qld + col[p]) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
     }
   } else if (valid) {
+    const PairScale ps((rotate ? 0.0625f : 1.0f) * lane_sign, rotate != 0);
 #pragma unroll
-    for (int g = 0; g < G; ++g) store8(y + r * COLS + col[g], v[g]);
+    for (int p = 0; p < G2; ++p) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[p][j] = mul2(v[p][j], ps.of(j));
+      store16p(y + r * COLS + col[p], v[p]);
+    }
   }
 }
 
@@ -506,7 +675,7 @@ int launch_rows(anima_ctx* ctx, const TIn* x, int rows, int cols, int ldx, const
   const int qld = q ? q->ld : 0;
 #define ROWS_CASE(C)                                                                                             \
   case C: {                                                                                                      \
-    constexpr int rpc = 8 / (C > 1024 ? C / 1024 : 1);                                                          \
+    constexpr int rpc = RowGeom<C>::RPC;                                                                         \
     rows_kernel<C, TIn, TOut, LN><<<(rows + rpc - 1) / rpc, 256, 0, ctx->stream>>>(x, rows, ldx, mod, so, sco,   \
                                                                                   eps, rotate, y, hi, lo, sc, qld, act); \
     break;                                                                                                       \

@@ -207,7 +207,9 @@ def kernel_case(args):
     mlp2  the 8192->2048 block linear with the gated residual
     qkv   the 2048->6144 qkv linear with the per-head RMSNorm + RoPE epilogue
     attn  self-attention, 16 heads x 4096 tokens x d=128 (fp16 q/k/v in the qkv layout)
-    ln    LayerNorm + adaLN + ConvRot + two-plane quantization of [4096, 2048]"""
+    ln    LayerNorm + adaLN + ConvRot + two-plane quantization of [4096, 2048]
+    gelu  GELU + ConvRot + quantization of the fp16 MLP hidden [4096, 8192]
+    rotq  ConvRot + quantization of the fp16 attention output [4096, 2048]"""
     import torch
 
     syn, ditm, ops, W = pkg("synthetic"), pkg("dit"), pkg("ops"), pkg("weights")
@@ -251,19 +253,29 @@ def kernel_case(args):
         q = ops.QuantRows.empty(M, 2048, planes, "cuda")
         fn = lambda: ops.layernorm_mod_quant(x, mod, 0, 2048, 2048, out=q)  # noqa: E731
         work, unit = M * 2048 * (4 + planes) + M * 4, "GB/s"
+    elif args.kernel in ("gelu", "rotq"):
+        K = 8192 if args.kernel == "gelu" else 2048
+        h = torch.randn(M, K, device="cuda").half()
+        q = ops.QuantRows.empty(M, K, planes, "cuda")
+        act = "gelu" if args.kernel == "gelu" else None
+        fn = lambda: ops.rotate_quant(h, planes, out=q, act=act)  # noqa: E731
+        work, unit = M * K * (2 + planes) + M * 4, "GB/s"
     else:
         raise SystemExit(f"unknown kernel case {args.kernel}")
     for _ in range(3):
         fn()
     torch.cuda.synchronize()
+    # each sample times `batch` back-to-back launches, so short kernels are not measured with the
+    # host's launch latency; inputs stay L2-resident between launches when they fit
     ts = []
     for _ in range(args.reps):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        fn()
+        for _ in range(args.batch):
+            fn()
         e1.record()
         e1.synchronize()
-        ts.append(e0.elapsed_time(e1))
+        ts.append(e0.elapsed_time(e1) / args.batch)
     dev.Context.get(0).sync()
     ms = statistics.median(ts)
     rate = work / (ms * 1e-3) / (1e9 if unit == "GB/s" else 1e12)
@@ -273,8 +285,9 @@ def kernel_case(args):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--kernel", default=None, help="time one kernel case instead (mlp1|mlp2|qkv|attn|ln)")
+    ap.add_argument("--kernel", default=None, help="time one kernel case instead (mlp1|mlp2|qkv|oproj|attn|ln|gelu|rotq)")
     ap.add_argument("--reps", type=int, default=20)
+    ap.add_argument("--batch", type=int, default=10, help="kernel cases: launches per timed sample")
     ap.add_argument("--act", default="gelu", help="kernel case mlp1: epilogue activation (gelu|none)")
     ap.add_argument("--out", default="f16", help="kernel case mlp1: output dtype (f16|f32)")
     ap.add_argument("--gpus", type=int, default=1)

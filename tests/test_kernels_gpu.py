@@ -85,7 +85,7 @@ def test_layernorm_mod_quant(ops, planes, tol):
     np.testing.assert_allclose(s, np.abs(ref).max(1) / 127, rtol=1e-5)
 
 
-@pytest.mark.parametrize("cols", [1024, 2048, 8192])
+@pytest.mark.parametrize("cols", [256, 512, 1024, 2048, 4096, 8192])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
 def test_rotate_quant(ops, cols, dtype):
     x = (randn((130, cols), 5) * 1.5).to(dtype)
@@ -102,8 +102,9 @@ def test_gelu_rotate_quant(ops):
     assert rel_l2(q.dequant().cpu().numpy(), ref) < 6e-5
 
 
-def test_rotate_plain(ops):
-    x = randn((64, 2048), 6)
+@pytest.mark.parametrize("cols", [256, 2048])
+def test_rotate_plain(ops, cols):
+    x = randn((67, cols), 6)
     y = ops.rotate(x.to(DEV)).cpu().numpy()
     assert rel_l2(y, oracle.rotate(x.numpy())) < 1e-6
 
