@@ -2,10 +2,13 @@
 // (Lq = Lk = 4096 at 1024^2) and cross-attention against cached text keys (Lk = 256..512). The
 // reference's counterpart is the fp32 WGSL flash kernel of app/gpu/kernels.js:147-299.
 //
-// One CTA = one (batch, head) and two 128-query tiles A and B; 320 threads:
-//   warps 0-3   softmax for tile A, warps 4-7 for tile B: one query row per thread
-//   warp 8      TMA producer: Q_A, Q_B once, then K_j / V_j (128 keys) into two stages each
-//   warp 9      TMEM allocator + single-thread UMMA issuer
+// One CTA = one (batch, head) and two 128-query tiles A and B; 576 threads:
+//   warps 0-7   softmax for tile A, warps 8-15 for tile B. Warp w serves the 32 query rows of
+//               lane quadrant w % 4 (the tensor-memory lanes it may access) and the key columns
+//               [64 h, 64 h + 64) with h = (w / 4) % 2, so two warps on the same SM sub-partition
+//               share each row; they exchange the row maximum through shared memory.
+//   warp 16     TMA producer: Q_A, Q_B once, then K_j / V_j (128 keys) into two stages each
+//   warp 17     TMEM allocator + single-thread UMMA issuer
 // Tensor memory (512 columns): S_A [0,128) S_B [128,256) O_A [256,384) O_B [384,512).
 // Per key block j the tensor core runs S_X = Q_X K_j^T (smem x smem), the softmax threads read S_X,
 // write P_X = 2^(s - m) as 16-bit values back over the first 64 columns of S_X, and the tensor core
@@ -25,7 +28,8 @@ namespace attn {
 
 constexpr int TILE = 128;     // query rows per tile and keys per block
 constexpr int HD = 128;       // head dim
-constexpr int THREADS = 320;
+constexpr int THREADS = 576;
+constexpr int SOFTMAX_WARPS = 16;
 constexpr int ATOM = 16384;   // one SWIZZLE_128B atom column: 128 rows x 128 bytes
 constexpr int TILE_BYTES = 2 * ATOM;
 // shared memory: Q_A | Q_B | K[2] | V[2] | barriers
@@ -33,7 +37,9 @@ constexpr int OFF_Q = 0;
 constexpr int OFF_K = OFF_Q + 2 * TILE_BYTES;
 constexpr int OFF_V = OFF_K + 2 * TILE_BYTES;
 constexpr int OFF_BAR = OFF_V + 2 * TILE_BYTES;
-constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
+constexpr int OFF_RED = OFF_BAR + 256;                 // row max exchange [2 parity][2 tiles][2 halves][128]
+constexpr int OFF_RED_L = OFF_RED + 2 * 2 * 2 * 128 * 4;  // row sum exchange [2 tiles][2 halves][128]
+constexpr int SMEM_BYTES = OFF_RED_L + 2 * 2 * 128 * 4 + 1024;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O when the max grows by > 2^8
 
 struct Params {
@@ -45,27 +51,13 @@ struct Params {
   const int* key_len;
   int kv_bcast;      // one K/V (and key_len) shared by every batch item
   float scale_log2;  // softmax scale * log2(e)
+  int pv_wait;       // issue S_x(j+1) only after PV_x(j) has completed
 };
 
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
-}
-
-// 2^x on the FMA/ALU pipes, to take part of the softmax's exponentials off the MUFU unit (its
-// bottleneck): x = n + f with n = rne(x) by the 1.5 * 2^23 magic-number rounding and f in
-// [-1/2, 1/2]; 2^f by a degree-4 polynomial (coefficients fitted here by relative least squares on
-// 4000 Chebyshev nodes of [-1/2, 1/2]; max relative error 2.7e-6, far below the 16-bit rounding of
-// P); n is added to the exponent field. Valid for -125 <= x <= 125; callers pass x <= 8 and clamp.
-__device__ __forceinline__ float exp2_fma(float x) {
-  x = fmaxf(x, -125.0f);
-  const float t = x + 12582912.0f;
-  const int n = __float_as_int(t) - 0x4B400000;
-  const float f = x - (t - 12582912.0f);
-  const float p = fmaf(fmaf(fmaf(fmaf(0.009560510516f, f, 0.05591703951f), f, 0.2402498126f), f, 0.6931219697f), f,
-                       0.9999991655f);
-  return __int_as_float(__float_as_int(p) + (n << 23));
 }
 
 template <bool BF16>
@@ -85,8 +77,8 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
-// EMU: how many of every 4 exponentials run on the FMA pipes (exp2_fma) instead of MUFU.
-template <bool BF16, int EMU>
+// 18 warps are allocated registers as 20: 96 x 32 x 20 = 61440 of the SM's 65536
+template <bool BF16>
 __global__ void __launch_bounds__(THREADS, 1)
     attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                      const __grid_constant__ CUtensorMap tm_v, const Params p) {
@@ -99,7 +91,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* v_full = bars + 5;   // [2]
   uint64_t* v_empty = bars + 7;  // [2]
   uint64_t* s_full = bars + 9;   // [2] per tile: S_X(j) complete
-  uint64_t* p_full = bars + 11;  // [2] per tile: P_X(j) written (4 warp arrivals)
+  uint64_t* p_full = bars + 11;  // [2] per tile: P_X(j) written (8 warp arrivals)
   uint64_t* o_done = bars + 13;  // [2] per tile: PV_X(j) complete
   uint64_t* drain = bars + 15;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
@@ -124,14 +116,14 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 4);
+      mbar_init(&p_full[i], SOFTMAX_WARPS / 2);
       mbar_init(&o_done[i], 1);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  constexpr int kProducerWarp = 8, kMmaWarp = 9;
+  constexpr int kProducerWarp = SOFTMAX_WARPS, kMmaWarp = SOFTMAX_WARPS + 1;
   if (warp == kMmaWarp) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
@@ -235,8 +227,12 @@ __global__ void __launch_bounds__(THREADS, 1)
               ok = false;
               break;
             }
-            if (!mbar_wait(&o_done[x], jp, abort_flag, kErrTimeoutAcc)) { ok = false; break; }
-            tc_fence_after();
+            // S_x(j+1) overwrites P_x(j): the tensor core runs this thread's MMAs in issue order,
+            // so PV_x(j) has read P_x(j) by then (pv_wait: wait for PV_x(j) explicitly instead)
+            if (p.pv_wait) {
+              if (!mbar_wait(&o_done[x], jp, abort_flag, kErrTimeoutAcc)) { ok = false; break; }
+              tc_fence_after();
+            }
             issue_s(x, j + 1);
             if (x == 1) umma_commit(&k_empty[st1]);
           }
@@ -254,47 +250,67 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
     }
   } else {
-    // softmax: tile x = warp / 4, row = (warp % 4) * 32 + lane
-    const int x = warp >> 2;
+    // softmax: tile x, lane quadrant `quad` (rows quad * 32 + lane), key-column half hf
+    const int x = warp >> 3;
+    const int hf = (warp >> 2) & 1;
     const int quad = warp & 3;
     const int row = quad * 32 + lane;
     const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
-    const uint32_t s_addr = tmem + lane_addr + x * 128;
-    const uint32_t o_addr = tmem + lane_addr + 256 + x * 128;
+    const uint32_t s_addr = tmem + lane_addr + x * 128 + 64 * hf;  // fp32 scores of this half
+    const uint32_t p_addr = tmem + lane_addr + x * 128 + 32 * hf;  // its 64 probabilities, 2 per column
+    const uint32_t o_addr = tmem + lane_addr + 256 + x * 128 + 64 * hf;
+    float* red = reinterpret_cast<float*>(smem + OFF_RED);  // [parity][tile][half][row]
+    const int bar_id = 1 + x * 4 + quad;                      // named barrier of the two warps of a row
+    auto pair_sync = [&]() { asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory"); };
     float m_used = -INFINITY;  // max the probabilities (and O, l) are relative to
-    float l = 0.f;
+    float l = 0.f;             // this half's share of the row sum
     bool ok = true;
+    // Every iteration meets pair_sync exactly once, also after a failed wait (the warp then skips
+    // the work), so the two warps of a row always agree on the barrier count.
     for (int j = 0; j < nblk; ++j) {
       const uint32_t jp = j & 1;
-      if (!warp_wait(&s_full[x], jp, abort_flag, kErrTimeoutFull)) { ok = false; break; }
+      if (ok && !warp_wait(&s_full[x], jp, abort_flag, kErrTimeoutFull)) ok = false;
+      if (!ok) {
+        pair_sync();
+        continue;
+      }
       tc_fence_after();
-      uint32_t sr[4][32];
+      uint32_t sr[2][32];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(s_addr + 32 * c, sr[c]);
+      for (int c = 0; c < 2; ++c) tmem_ld32(s_addr + 32 * c, sr[c]);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld_wait(sr[c]);
-      const int kbase = j * TILE;
-      const bool masked = kbase + TILE > kv_len;  // only the last block can hold keys past kv_len
-      float mx = -INFINITY;
+      for (int c = 0; c < 2; ++c) tmem_ld_wait(sr[c]);
+      const int kbase = j * TILE + 64 * hf;
+      const bool masked = j * TILE + TILE > kv_len;  // only the last block can hold keys past kv_len
       if (masked) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
+        for (int c = 0; c < 2; ++c)
 #pragma unroll
           for (int t = 0; t < 32; ++t)
             if (kbase + 32 * c + t >= kv_len) sr[c][t] = __float_as_uint(-INFINITY);
       }
-      {  // eight independent partial maxima (short dependency chains)
-        float pm[8];
+      float mx;
+      {  // four independent partial maxima, two new values per max
+        float pm[4];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) pm[i] = -INFINITY;
+        for (int i = 0; i < 4; ++i) pm[i] = -INFINITY;
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
+        for (int c = 0; c < 2; ++c)
 #pragma unroll
-          for (int t = 0; t < 32; ++t) pm[t & 7] = fmaxf(pm[t & 7], __uint_as_float(sr[c][t]));
-        mx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])), fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
+          for (int t = 0; t < 32; t += 2)
+            pm[(t >> 1) & 3] = fmax3(pm[(t >> 1) & 3], __uint_as_float(sr[c][t]), __uint_as_float(sr[c][t + 1]));
+        mx = fmax3(fmaxf(pm[0], pm[1]), pm[2], pm[3]);
       }
-      mx *= p.scale_log2;
-      // lazy rescale: keep the old max unless the new one is more than 2^8 larger
+      // the row maximum over both halves (double-buffered by block parity: the partner reads this
+      // block's value before it can reach the next block's barrier). The barrier also orders both
+      // warps' reads of S before either overwrites S's first 64 columns with P.
+      red[((jp * 2 + x) * 2 + hf) * 128 + row] = mx;
+      tc_fence_before();
+      pair_sync();
+      tc_fence_after();
+      mx = fmaxf(mx, red[((jp * 2 + x) * 2 + (hf ^ 1)) * 128 + row]) * p.scale_log2;
+      // lazy rescale: keep the old max unless the new one is more than 2^8 larger (both halves
+      // see the same maximum and take the same decision)
       float alpha = 1.f;
       bool rescale = false;
       if (mx > m_used + kRescaleThreshold) {
@@ -302,34 +318,35 @@ __global__ void __launch_bounds__(THREADS, 1)
         alpha = (m_used == -INFINITY) ? 0.f : ex2(m_used - mx);
         m_used = mx;
       }
-      float rsp[4] = {0.f, 0.f, 0.f, 0.f};  // partial row sums
-      uint32_t pk[2][32];
+      f2 rsp[2] = {dup2(0.f), dup2(0.f)};  // partial row sums
+      const f2 sc2 = dup2(p.scale_log2), nm2 = dup2(-m_used);
+      // P over the first 64 columns of S (two 16-bit probabilities per column), 32 keys at a time
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
+      for (int c = 0; c < 2; ++c) {
+        uint32_t pk[16];
 #pragma unroll
         for (int t = 0; t < 32; t += 2) {
-          const float a0 = fmaf(__uint_as_float(sr[c][t]), p.scale_log2, -m_used);
-          const float a1 = fmaf(__uint_as_float(sr[c][t + 1]), p.scale_log2, -m_used);
-          float e0 = (EMU >= 2 && (t & 2)) ? exp2_fma(a0) : ex2(a0);
-          float e1 = (EMU >= 1 && (t & 2)) ? exp2_fma(a1) : ex2(a1);
+          const f2 a = fma2(make_float2(__uint_as_float(sr[c][t]), __uint_as_float(sr[c][t + 1])), sc2, nm2);
+          float e0 = ex2(a.x), e1 = ex2(a.y);
           if (masked) {  // -inf scores: exactly zero probability
             if (kbase + 32 * c + t >= kv_len) e0 = 0.f;
             if (kbase + 32 * c + t + 1 >= kv_len) e1 = 0.f;
           }
-          rsp[(t >> 1) & 3] += e0 + e1;
-          pk[c >> 1][(c & 1) * 16 + t / 2] = pack2<BF16>(e0, e1);
+          rsp[(t >> 1) & 1] = add2(rsp[(t >> 1) & 1], make_float2(e0, e1));
+          pk[t / 2] = pack2<BF16>(e0, e1);
         }
-      const float rs = (rsp[0] + rsp[1]) + (rsp[2] + rsp[3]);
-      l = l * alpha + rs;
-      // P over the first 64 columns of S (two 16-bit probabilities per column)
-      tmem_st32(s_addr, pk[0]);
-      tmem_st32(s_addr + 32, pk[1]);
+        tmem_st16(p_addr + 16 * c, pk);
+      }
+      l = l * alpha + ((rsp[0].x + rsp[0].y) + (rsp[1].x + rsp[1].y));
       if (rescale) {
         // O holds sum_{i<j} P_i V_i relative to the old max: wait for PV(j-1), then scale in place
-        if (!warp_wait(&o_done[x], jp ^ 1, abort_flag, kErrTimeoutAcc)) { ok = false; break; }
+        if (!warp_wait(&o_done[x], jp ^ 1, abort_flag, kErrTimeoutAcc)) {
+          ok = false;
+          continue;
+        }
         tc_fence_after();
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 2; ++c) {
           uint32_t orr[32];
           tmem_ld32(o_addr + 32 * c, orr);
           tmem_ld_wait(orr);
@@ -343,15 +360,20 @@ __global__ void __launch_bounds__(THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[x]);
     }
-    // normalised output row once the last PV has landed
+    // the row sum over both halves; a warp that failed still takes part so its partner is released
+    float* red_l = reinterpret_cast<float*>(smem + OFF_RED_L);
+    red_l[(x * 2 + hf) * 128 + row] = l;
+    pair_sync();
+    const float l_row = l + red_l[(x * 2 + (hf ^ 1)) * 128 + row];
+    // normalised output (this half's 64 columns) once the last PV has landed
     if (ok && nblk > 0 && warp_wait(&o_done[x], (nblk - 1) & 1, abort_flag, kErrTimeoutAcc)) {
       tc_fence_after();
       const int qrow = q0 + x * TILE + row;
-      const float inv = l > 0.f ? 1.0f / l : 0.f;
+      const float inv = l_row > 0.f ? 1.0f / l_row : 0.f;
       const size_t base = static_cast<size_t>(b) * p.o_bstride + static_cast<size_t>(qrow) * p.ldo +
-                          static_cast<size_t>(h) * HD;
+                          static_cast<size_t>(h) * HD + 64 * hf;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         uint32_t orr[32];
         tmem_ld32(o_addr + 32 * c, orr);
         tmem_ld_wait(orr);
@@ -392,10 +414,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int qrow = q0 + x * TILE + row;
       if (qrow < p.Lq) {
         const size_t base = static_cast<size_t>(b) * p.o_bstride + static_cast<size_t>(qrow) * p.ldo +
-                            static_cast<size_t>(h) * HD;
+                            static_cast<size_t>(h) * HD + 64 * hf;
         const int esz = p.out_dtype == ANIMA_F32 ? 4 : 2;
         uint4* dst = reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.out) + base * esz);
-        for (int t = 0; t < HD * esz / 16; ++t) dst[t] = make_uint4(0, 0, 0, 0);
+        for (int t = 0; t < 64 * esz / 16; ++t) dst[t] = make_uint4(0, 0, 0, 0);
       }
     }
   }
@@ -478,25 +500,23 @@ extern "C" int anima_attention(anima_ctx* ctx, const anima_attention_args* a) {
   p.kv_bcast = kv_bcast ? 1 : 0;
   const float scale = a->scale > 0.f ? a->scale : 1.0f / sqrtf(static_cast<float>(a->head_dim));
   p.scale_log2 = scale * 1.4426950408889634f;
+  static const int pv_wait = [] {
+    const char* e = getenv("ANIMA_ATTN_PV_WAIT");
+    return e && atoi(e) != 0 ? 1 : 0;
+  }();
+  p.pv_wait = pv_wait;
 
   const long long grid = static_cast<long long>(p.q_pairs) * a->heads * a->batch;
   ANIMA_REQUIRE(grid < (1LL << 31), "anima_attention: problem too large");
   ProfScope prof(ctx, "attn.flash", 4.0 * a->batch * a->heads * static_cast<double>(a->Lq) * a->Lk * a->head_dim, 0);
-  // share of the exponentials computed on the FMA pipes (ANIMA_ATTN_EMU = 0, 1 or 2 of 4)
-  static const int emu = [] {
-    const char* e = getenv("ANIMA_ATTN_EMU");
-    const int v = e ? atoi(e) : 0;
-    return v < 0 ? 0 : (v > 2 ? 2 : v);
-  }();
-  const bool bf16 = a->dtype == ANIMA_BF16;
   using Kfn = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const attn::Params);
-  Kfn fns[2][3] = {{attn::attention_kernel<false, 0>, attn::attention_kernel<false, 1>, attn::attention_kernel<false, 2>},
-                   {attn::attention_kernel<true, 0>, attn::attention_kernel<true, 1>, attn::attention_kernel<true, 2>}};
-  static bool set[2][3] = {};
-  Kfn fn = fns[bf16 ? 1 : 0][emu];
-  if (!set[bf16 ? 1 : 0][emu]) {
+  const int kind = a->dtype == ANIMA_BF16 ? 1 : 0;
+  const Kfn fns[2] = {attn::attention_kernel<false>, attn::attention_kernel<true>};
+  static bool set[2] = {};
+  const Kfn fn = fns[kind];
+  if (!set[kind]) {
     ANIMA_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, attn::SMEM_BYTES));
-    set[bf16 ? 1 : 0][emu] = true;
+    set[kind] = true;
   }
   fn<<<static_cast<int>(grid), attn::THREADS, attn::SMEM_BYTES, ctx->stream>>>(tq, tk, tv, p);
   return check_launch("attention_kernel");

@@ -73,15 +73,8 @@ __device__ __forceinline__ float warp_max(float v) {
 }
 
 // ------------------------------------------------------------------ packed fp32 pairs
-// sm_100 issues two fp32 adds, multiplies or FMAs per instruction on a register pair; the row
-// kernels keep their data as float2 pairs of neighbouring elements so the bulk of the arithmetic
-// uses these.
-using f2 = float2;
-__device__ __forceinline__ f2 dup2(float a) { return make_float2(a, a); }
-__device__ __forceinline__ f2 add2(f2 a, f2 b) { return __fadd2_rn(a, b); }
-__device__ __forceinline__ f2 mul2(f2 a, f2 b) { return __fmul2_rn(a, b); }
-__device__ __forceinline__ f2 fma2(f2 a, f2 b, f2 c) { return __ffma2_rn(a, b, c); }
-__device__ __forceinline__ f2 sub2(f2 a, f2 b) { return __ffma2_rn(b, dup2(-1.0f), a); }
+// The row kernels keep their data as float2 pairs of neighbouring elements so the bulk of the
+// arithmetic uses the paired fp32 instructions (f2 helpers in sm100.cuh).
 
 template <typename T>
 __device__ __forceinline__ void load16p(const T* p, f2 (&x)[8]) {
@@ -378,7 +371,7 @@ __global__ void __launch_bounds__(256, 4) rows_kernel(const TIn* __restrict__ x,
 #pragma unroll
     for (int p = 0; p < G2; ++p)
 #pragma unroll
-      for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fmaxf(fabsf(v[p][j].x), fabsf(v[p][j].y)));
+      for (int j = 0; j < 8; ++j) amax = fmax3(amax, fabsf(v[p][j].x), fabsf(v[p][j].y));
     amax = row_reduce<COLS, true>(amax, red);
     if (!valid) return;
     // a = (y / 16) * 127 / (amax / 16) = y * (127 / amax) for the unscaled y: the 1/16 is a power of
@@ -596,9 +589,13 @@ __global__ void euler_kernel(float* x, const float* __restrict__ v, const float*
 
 // ------------------------------------------------------------------ SIMT GEMM for bf16 / f32 weights
 // C[m, n] = act(alpha * sum_k A[m, k] B[n, k] (+ bias[n])), stored or accumulated (C += gate * y).
-// 64 x 64 tiles, 256 threads, 4 x 4 outputs per thread, K tiles of 16 through shared memory.
+// 256 threads compute a BM x 64 tile (BM = 64, 32 or 16, the tallest that still gives two CTAs
+// per SM). The threads form KS = 64 / BM K-slices of 4 BM threads; a slice walks every KS-th K
+// tile of 32, each thread accumulating a 4 x 4 block from two 16-byte shared-memory reads per k,
+// and the slices' partial tiles are summed through shared memory at the end. The next tile's
+// global loads are issued before the current tile's FMAs.
 // QA: A is given as quantized rows, A[m, k] = qs[m] * (qhi[m, k] + qlo[m, k] / 254).
-template <typename TB, bool QA = false>
+template <typename TB, bool QA, int BM>
 __global__ void __launch_bounds__(256) simt_gemm_kernel(int M, int N, int K, float alpha, const float* __restrict__ A,
                                                         int lda, const TB* __restrict__ B, int ldb,
                                                         const float* __restrict__ bias, int act, float* C, int ldc,
@@ -606,64 +603,138 @@ __global__ void __launch_bounds__(256) simt_gemm_kernel(int M, int N, int K, flo
                                                         const int8_t* __restrict__ qhi = nullptr,
                                                         const int8_t* __restrict__ qlo = nullptr,
                                                         const float* __restrict__ qs = nullptr) {
-  __shared__ float As[16][65];
-  __shared__ float Bs[16][65];
-  const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
-  const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
-  float acc[4][4] = {};
-  for (int k0 = 0; k0 < K; k0 += 16) {
-    for (int i = threadIdx.x; i < 64 * 16; i += 256) {
-      const int r = i / 16, kk = i % 16;
-      const int m = m0 + r, n = n0 + r, k = k0 + kk;
-      if constexpr (QA) {
-        float a = 0.f;
-        if (m < M && k < K) {
-          const size_t idx = static_cast<size_t>(m) * lda + k;
+  constexpr int BN = 64, BK = 32, KS = 64 / BM, ST = 4 * BM;
+  constexpr int AE = BM * BK / ST, BE = BN * BK / ST;
+  constexpr int AS = BM + 4, BS = BN + 4;            // padded rows, 16-byte aligned
+  constexpr int SLICE = BK * AS + BK * BS;           // floats per slice
+  static_assert(KS * SLICE >= KS * BM * BN, "reduction buffer");
+  __shared__ __align__(16) float smem[KS * SLICE];
+  const int sl = threadIdx.x / ST, lt = threadIdx.x % ST;
+  const int tx = lt % 16, ty = lt / 16;
+  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+  float* As = smem + sl * SLICE;
+  float* Bs = As + BK * AS;
+  float ra[AE], rb[BE];
+  auto fetch = [&](int k0) {
+#pragma unroll
+    for (int e = 0; e < AE; ++e) {
+      const int i = lt + e * ST, r = i / BK, k = k0 + i % BK, m = m0 + r;
+      float a = 0.f;
+      if (m < M && k < K) {
+        const size_t idx = static_cast<size_t>(m) * lda + k;
+        if constexpr (QA) {
           a = static_cast<float>(qhi[idx]);
           if (qlo) a += static_cast<float>(qlo[idx]) * (1.0f / 254.0f);
           a *= qs[m];
+        } else {
+          a = A[idx];
         }
-        As[kk][r] = a;
-      } else {
-        As[kk][r] = (m < M && k < K) ? A[static_cast<size_t>(m) * lda + k] : 0.f;
       }
-      Bs[kk][r] = (n < N && k < K) ? to_f<TB>(B[static_cast<size_t>(n) * ldb + k]) : 0.f;
+      ra[e] = a;
+    }
+#pragma unroll
+    for (int e = 0; e < BE; ++e) {
+      const int i = lt + e * ST, r = i / BK, k = k0 + i % BK, n = n0 + r;
+      rb[e] = (n < N && k < K) ? to_f<TB>(B[static_cast<size_t>(n) * ldb + k]) : 0.f;
+    }
+  };
+  float acc[4][4] = {};
+  const int nk = (K + BK - 1) / BK;
+  const int steps = (nk + KS - 1) / KS;  // the same for every slice: all threads meet every barrier
+  fetch(sl * BK);
+  for (int t = 0; t < steps; ++t) {
+#pragma unroll
+    for (int e = 0; e < AE; ++e) {
+      const int i = lt + e * ST;
+      As[(i % BK) * AS + i / BK] = ra[e];
+    }
+#pragma unroll
+    for (int e = 0; e < BE; ++e) {
+      const int i = lt + e * ST;
+      Bs[(i % BK) * BS + i / BK] = rb[e];
     }
     __syncthreads();
+    if (t + 1 < steps) fetch(((t + 1) * KS + sl) * BK);
 #pragma unroll
-    for (int kk = 0; kk < 16; ++kk) {
-      float a[4], b[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        a[i] = As[kk][ty * 4 + i];
-        b[i] = Bs[kk][tx * 4 + i];
-      }
+    for (int kk = 0; kk < BK; ++kk) {
+      const float4 a = *reinterpret_cast<const float4*>(As + kk * AS + 4 * ty);
+      const float4 b = *reinterpret_cast<const float4*>(Bs + kk * BS + 4 * tx);
+      const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
     }
     __syncthreads();
   }
+  if constexpr (KS > 1) {
+    float* red = smem + sl * BM * BN;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      *reinterpret_cast<float4*>(red + (4 * ty + i) * BN + 4 * tx) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+    __syncthreads();
+    if (sl != 0) return;
+#pragma unroll
+    for (int q = 1; q < KS; ++q)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float4 v = *reinterpret_cast<const float4*>(smem + q * BM * BN + (4 * ty + i) * BN + 4 * tx);
+        acc[i][0] += v.x; acc[i][1] += v.y; acc[i][2] += v.z; acc[i][3] += v.w;
+      }
+  }
+  // the thread's 4 columns go out as one 16-byte store when the row allows it
+  const int nb = n0 + 4 * tx;
+  const bool vec = !accumulate && nb + 4 <= N && ((reinterpret_cast<uintptr_t>(C) | (static_cast<uintptr_t>(ldc) * 4)) & 15) == 0;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const int m = m0 + ty * 4 + i;
+    const int m = m0 + 4 * ty + i;
     if (m >= M) continue;
+    float r[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const int n = n0 + tx * 4 + j;
-      if (n >= N) continue;
-      float r = acc[i][j] * alpha;
-      if (bias) r += bias[n];
-      if (act == ANIMA_ACT_GELU) r = gelu_erf(r);
-      if (act == ANIMA_ACT_SILU) r = silu_f(r);
-      float* c = C + static_cast<size_t>(m) * ldc + n;
+      r[j] = acc[i][j] * alpha;
+      if (bias && nb + j < N) r[j] += bias[nb + j];
+      if (act == ANIMA_ACT_GELU) r[j] = gelu_erf(r[j]);
+      if (act == ANIMA_ACT_SILU) r[j] = silu_f(r[j]);
+    }
+    float* c = C + static_cast<size_t>(m) * ldc + nb;
+    if (vec) {
+      *reinterpret_cast<float4*>(c) = make_float4(r[0], r[1], r[2], r[3]);
+      continue;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (nb + j >= N) continue;
       if (accumulate)
-        *c += (gate ? gate[gate_off + n] : 1.0f) * r;
+        c[j] += (gate ? gate[gate_off + nb + j] : 1.0f) * r[j];
       else
-        *c = r;
+        c[j] = r[j];
     }
   }
+}
+
+// Tile height for the SIMT GEMM: the tallest tile that still gives two CTAs per SM.
+inline int simt_bm(int M, int N, int sms) {
+  const long long nt = (N + 63) / 64;
+  for (int bm : {64, 32}) {
+    if (nt * ((M + bm - 1) / bm) >= 2LL * sms) return bm;
+  }
+  return 16;
+}
+
+template <typename TB, bool QA>
+void launch_simt(cudaStream_t st, int sms, int M, int N, int K, float alpha, const float* A, int lda, const TB* B,
+                 int ldb, const float* bias, int act, float* C, int ldc, int accumulate, const float* gate,
+                 int gate_off, const int8_t* qhi = nullptr, const int8_t* qlo = nullptr, const float* qs = nullptr) {
+  const int bm = simt_bm(M, N, sms);
+  const dim3 grid((N + 63) / 64, (M + bm - 1) / bm);
+#define SIMT(BMV)                                                                                                \
+  simt_gemm_kernel<TB, QA, BMV><<<grid, 256, 0, st>>>(M, N, K, alpha, A, lda, B, ldb, bias, act, C, ldc, accumulate, \
+                                                      gate, gate_off, qhi, qlo, qs)
+  if (bm == 64) SIMT(64);
+  else if (bm == 32) SIMT(32);
+  else SIMT(16);
+#undef SIMT
 }
 
 template <typename TIn, typename TOut, bool LN>
@@ -861,24 +932,20 @@ int anima_matmul(anima_ctx* ctx, int M, int N, int K, float alpha, const float* 
   ANIMA_REQUIRE(B->kind == ANIMA_W_BF16 || B->kind == ANIMA_W_F32, "anima_matmul: weight kind %d (bf16 or f32 only)",
                 B->kind);
   ProfScope prof(ctx, B->kind == ANIMA_W_BF16 ? "gemm.bf16" : "gemm.f32", 2.0 * M * N * K, 0);
-  dim3 grid((N + 63) / 64, (M + 63) / 64);
   if (B->kind == ANIMA_W_BF16)
-    simt_gemm_kernel<__nv_bfloat16><<<grid, 256, 0, ctx->stream>>>(M, N, K, alpha, A, lda,
-                                                                   (const __nv_bfloat16*)B->data, K, B->bias, act, C,
-                                                                   ldc, accumulate, gate, gate_off);
+    launch_simt<__nv_bfloat16, false>(ctx->stream, ctx->num_sms, M, N, K, alpha, A, lda, (const __nv_bfloat16*)B->data, K,
+                                      B->bias, act, C, ldc, accumulate, gate, gate_off);
   else
-    simt_gemm_kernel<float><<<grid, 256, 0, ctx->stream>>>(M, N, K, alpha, A, lda, (const float*)B->data, K, B->bias,
-                                                           act, C, ldc, accumulate, gate, gate_off);
+    launch_simt<float, false>(ctx->stream, ctx->num_sms, M, N, K, alpha, A, lda, (const float*)B->data, K, B->bias, act,
+                              C, ldc, accumulate, gate, gate_off);
   return check_launch("simt_gemm_kernel");
 }
 
 int anima_lora_down(anima_ctx* ctx, const anima_qact* x, const float* A, int r, float* T, int ldt) {
   ANIMA_REQUIRE(ctx && x && x->hi && x->scale && A && T && r > 0 && ldt >= r, "anima_lora_down: bad argument");
   ProfScope prof(ctx, "lora.down", 2.0 * x->rows * r * x->cols, 0);
-  dim3 grid((r + 63) / 64, (x->rows + 63) / 64);
-  simt_gemm_kernel<float, true><<<grid, 256, 0, ctx->stream>>>(x->rows, r, x->cols, 1.0f, nullptr, x->ld, A, x->cols,
-                                                                nullptr, 0, T, ldt, 0, nullptr, 0, x->hi, x->lo,
-                                                                x->scale);
+  launch_simt<float, true>(ctx->stream, ctx->num_sms, x->rows, r, x->cols, 1.0f, nullptr, x->ld, A, x->cols, nullptr, 0, T,
+                           ldt, 0, nullptr, 0, x->hi, x->lo, x->scale);
   return check_launch("simt_gemm_kernel<lora_down>");
 }
 

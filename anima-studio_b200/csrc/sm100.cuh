@@ -72,6 +72,21 @@ __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps until the phase completes or kSuspendNs
+// pass, instead of spinning and taking issue slots from the warps doing the work.
+constexpr uint32_t kSuspendNs = 100000;
+__device__ __forceinline__ bool mbar_test_sleep(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(kSuspendNs)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait for the phase with `parity` to complete. Returns false (and raises the CTA abort flag and
 // the device error bit `err`) if that takes longer than kWaitTimeoutNs or another role aborted.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
@@ -79,15 +94,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   const uint32_t a = smem_u32(bar);
   if (mbar_test(a, parity)) return true;
   const unsigned long long t0 = globaltimer();
-  for (uint32_t spin = 1;; ++spin) {
-    if (mbar_test(a, parity)) return true;
-    if ((spin & 63u) == 0) {
-      if (*abort_flag) return false;
-      if (globaltimer() - t0 > kWaitTimeoutNs) {
-        flag_error(err);
-        *abort_flag = 1;
-        return false;
-      }
+  for (;;) {
+    if (mbar_test_sleep(a, parity)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer() - t0 > kWaitTimeoutNs) {
+      flag_error(err);
+      *abort_flag = 1;
+      return false;
     }
   }
 }
@@ -255,6 +268,15 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       : "memory");
 }
 
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // tcgen05.wait::ld that also "redefines" the 32 destination registers of an earlier tcgen05.ld,
@@ -339,5 +361,20 @@ __device__ __forceinline__ float gelu_erf(float x) {
   return 0.5f * x * (1.0f + copysignf(erf_abs, z));
 }
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
+
+// ---------------------------------------------------------------- packed fp32 pairs
+// sm_100 issues two fp32 adds, multiplies or FMAs per instruction on a register pair.
+using f2 = float2;
+// three-input max (sm_100)
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+__device__ __forceinline__ f2 dup2(float a) { return make_float2(a, a); }
+__device__ __forceinline__ f2 add2(f2 a, f2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ f2 mul2(f2 a, f2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ f2 fma2(f2 a, f2 b, f2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ f2 sub2(f2 a, f2 b) { return __ffma2_rn(b, dup2(-1.0f), a); }
 
 }  // namespace anima

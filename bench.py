@@ -209,7 +209,8 @@ def kernel_case(args):
     attn  self-attention, 16 heads x 4096 tokens x d=128 (fp16 q/k/v in the qkv layout)
     ln    LayerNorm + adaLN + ConvRot + two-plane quantization of [4096, 2048]
     gelu  GELU + ConvRot + quantization of the fp16 MLP hidden [4096, 8192]
-    rotq  ConvRot + quantization of the fp16 attention output [4096, 2048]"""
+    rotq  ConvRot + quantization of the fp16 attention output [4096, 2048]
+    xembed / final  the fp32 SIMT GEMMs of the patch embedding (68 -> 2048) and the final layer (2048 -> 64)"""
     import torch
 
     syn, ditm, ops, W = pkg("synthetic"), pkg("dit"), pkg("ops"), pkg("weights")
@@ -253,6 +254,13 @@ def kernel_case(args):
         q = ops.QuantRows.empty(M, 2048, planes, "cuda")
         fn = lambda: ops.layernorm_mod_quant(x, mod, 0, 2048, 2048, out=q)  # noqa: E731
         work, unit = M * 2048 * (4 + planes) + M * 4, "GB/s"
+    elif args.kernel in ("xembed", "final"):
+        N, K = (2048, 68) if args.kernel == "xembed" else (64, 2048)
+        a = torch.randn(M, K, device="cuda")
+        w = W.Linear("bf16", N, K, (torch.randn(N, K, device="cuda") * 0.02).to(torch.bfloat16), None)
+        out = torch.empty(M, N, device="cuda")
+        fn = lambda: ops.matmul(a, w, out=out)  # noqa: E731
+        work, unit = 2.0 * M * N * K, "TFLOP/s"
     elif args.kernel in ("gelu", "rotq"):
         K = 8192 if args.kernel == "gelu" else 2048
         h = torch.randn(M, K, device="cuda").half()
@@ -285,7 +293,7 @@ def kernel_case(args):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--kernel", default=None, help="time one kernel case instead (mlp1|mlp2|qkv|oproj|attn|ln|gelu|rotq)")
+    ap.add_argument("--kernel", default=None, help="time one kernel case instead (mlp1|mlp2|qkv|oproj|attn|ln|gelu|rotq|xembed|final)")
     ap.add_argument("--reps", type=int, default=20)
     ap.add_argument("--batch", type=int, default=10, help="kernel cases: launches per timed sample")
     ap.add_argument("--act", default="gelu", help="kernel case mlp1: epilogue activation (gelu|none)")

@@ -161,7 +161,8 @@ def test_elementwise_patchify_timestep_euler(ops):
     assert rel_l2(xd.cpu().numpy(), (x - v * 0.3).numpy()) < 1e-6
 
 
-@pytest.mark.parametrize("M,N,K", [(1, 6144, 2048), (64, 2048, 68), (130, 64, 2048)])
+@pytest.mark.parametrize("M,N,K", [(1, 6144, 2048), (64, 2048, 68), (130, 64, 2048), (2000, 1000, 100),
+                                   (1000, 1000, 300), (4096, 64, 2048)])
 @pytest.mark.parametrize("kind", ["bf16", "f32"])
 def test_matmul_simt(ops, M, N, K, kind):
     W = pkg("weights")
