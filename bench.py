@@ -291,6 +291,70 @@ def kernel_case(args):
                       "ms_min": min(ts), "rate": rate, "unit": unit, "reps": args.reps}), flush=True)
 
 
+def run_tp(args, world, rank, local):
+    """One image denoised by all ranks together (head-sharded tensor parallelism): the latency
+    mode. Eager launches (the per-block all-reduces stay outside CUDA graphs)."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    syn, ditm, ops, pl, sh = pkg("synthetic"), pkg("dit"), pkg("ops"), pkg("pipeline"), pkg("sharding")
+    seed = 1234
+    tensors = syn.dit_tensors(seed, "int8", 28, device="cuda")
+    dit = ditm.AnimaDiT(tensors, "cuda", precision=args.precision,
+                        attn_dtype=torch.bfloat16 if args.attn == "bf16" else torch.float16,
+                        tp=sh.TPGroup(rank, world, None))
+    del tensors
+    torch.cuda.empty_cache()
+    ctx = torch.cat([syn.randn(seed, "ctx", (256, 1024)), torch.zeros(256, 1024)]).cuda()
+    cond = dit.prepare_context(ctx)
+    sig = pl.sigmas_simple(8, 3.0)
+    tcs = dit.time_cond_batch(sig[:-1])
+    noise = syn.randn(seed, "noise", (1, 16, 128, 128)).cuda()   # the same image on every rank
+    x = noise * sig[0]
+
+    def step(i):
+        j = i % 8
+        v = dit.forward(x, cond, tcs[j])
+        ops.euler_step(x, v, sig[j], sig[j + 1])
+        if j == 7:
+            x.copy_(noise * sig[0])
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(local)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        step(args.warmup + i)
+    e1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    ms = sh.max_over_ranks(e0.elapsed_time(e1), "cuda")
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {"metric": "DiT denoise steps/sec at 1024^2 (4096 tokens) for one image, head-sharded tensor parallel",
+            "value": args.steps / (ms * 1e-3), "unit": "steps/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": "BASELINE configs[4] latency run: one 1024x1024 image, 28 INT8 ConvRot blocks, "
+                                   "16 heads and the 8192 MLP features split over the ranks, 3 NCCL all-reduces "
+                                   "of the fp32 residual stream per block", "parallelism": f"tp{world}",
+                       "launch": "eager", "precision": args.precision, "attention": args.attn},
+            "clocks": clk}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--kernel", default=None, help="time one kernel case instead (mlp1|mlp2|qkv|oproj|attn|ln|gelu|rotq|xembed|final)")
@@ -307,12 +371,16 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch kernels from Python per step instead of CUDA graphs")
+    ap.add_argument("--tp", action="store_true",
+                    help="single-image latency: heads sharded over the --gpus ranks, NCCL all-reduce per block")
     args = ap.parse_args()
     world, rank, local = setup_dist()
     if args.kernel:
         return kernel_case(args)
     if args.impl == "reference":
         return run_reference(args, world, rank)
+    if args.tp:
+        return run_tp(args, world, rank, local)
 
     import torch
     import torch.distributed as dist
@@ -376,11 +444,7 @@ def main():
     barrier()
     clk = clocks.stop()
     launches = dev.Context.launches - launches0
-    ms = e0.elapsed_time(e1)
-    t = torch.tensor([ms], device="cuda")
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
+    ms_max = pkg("sharding").max_over_ranks(e0.elapsed_time(e1), "cuda")
     value = world * args.steps / (ms_max * 1e-3)
 
     # Per-kernel durations: an instrumented replay of the same steps (CUDA events around each
@@ -424,11 +488,9 @@ def main():
         torch.cuda.synchronize()
         wall = time.perf_counter() - t0
         barrier()
-        et = torch.tensor([max(f0.elapsed_time(f1), wall * 1e3)], device="cuda")
-        if world > 1:
-            dist.all_reduce(et, op=dist.ReduceOp.MAX)
+        et = pkg("sharding").max_over_ranks(max(f0.elapsed_time(f1), wall * 1e3), "cuda")
         nbytes = xh.numel() * 4
-        e2e = {"value": world * args.steps / (float(et.item()) * 1e-3), "unit": "steps/s",
+        e2e = {"value": world * args.steps / (et * 1e-3), "unit": "steps/s",
                "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes,
                "api": "per step: pinned host latent -> device, pipeline.GraphedSampler step (AnimaDiT.forward + "
                       "euler_step as one CUDA graph), latent -> pinned host (the reference's per-pass host round trip, "
