@@ -47,6 +47,14 @@ struct Params {
   int rope_rows;
   int n_q;
   float eps;
+  // LoRA side paths (see anima_linear_opts)
+  const float* lora_t;
+  int ld_t;
+  int lora_t_lo;
+  const float* lora_bt;
+  int ld_bt;
+  int lora_count;
+  int lora_off[4], lora_n[4], lora_r0[4], lora_r[4];
   int num_m_blocks, num_n_blocks, num_k_blocks, num_tiles;
   int group_m;
 };
@@ -63,13 +71,17 @@ __device__ __forceinline__ void tile_coords(const Params& p, int tile, int& mb, 
   nb = within / gm;
 }
 
-template <int BN, int NPLANES>
+constexpr int LORA_R = 32;  // rank held per tile by the fused LoRA epilogue
+
+template <int BN, int NPLANES, bool LORA = false>
 struct Cfg {
   static constexpr int A_BYTES = BM * BK;
   static constexpr int B_BYTES = BN * BK;
   static constexpr int STAGE_BYTES = NPLANES * A_BYTES + B_BYTES;
   static constexpr int STAGING_BYTES = 8 * 2 * 32 * 128;  // 8 epilogue warps x 2 x 4 KB
-  static constexpr int STAGES = (216 * 1024 - STAGING_BYTES) / STAGE_BYTES;
+  // LoRA: one [LORA_R, BN] fp32 slice of scale * B^T per epilogue warpgroup
+  static constexpr int LORA_BYTES = LORA ? 2 * LORA_R * BN * 4 : 0;
+  static constexpr int STAGES = (216 * 1024 - STAGING_BYTES - LORA_BYTES) / STAGE_BYTES;
   static constexpr int ACC_COLS = NPLANES * BN;
   // one accumulator buffer per epilogue warpgroup when two fit in TMEM, else one (the second
   // epilogue warpgroup then idles and the epilogue of a tile delays the next tile's MMAs)
@@ -77,7 +89,7 @@ struct Cfg {
   static_assert(ACC_BUFS * ACC_COLS <= 512, "accumulators exceed TMEM");
   static constexpr int TMEM_COLS = 512;
   static constexpr int BAR_BYTES = 256;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + STAGING_BYTES + BAR_BYTES + 1024;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + STAGING_BYTES + LORA_BYTES + BAR_BYTES + 1024;
   static_assert(STAGES >= 2, "need at least two pipeline stages");
 };
 
@@ -116,10 +128,57 @@ __device__ __forceinline__ void issue_cols(uint32_t taddr, int col, uint32_t (&r
   if constexpr (NPLANES == 2) tmem_ldc<CH>(taddr + BN + col, rl);
 }
 
-// After the loads landed: y = a_scale[m] w_scale[n] (hi + lo / 254) (+ bias) (+ add) (act).
-template <int NPLANES, int CH>
+// LoRA: v[j] += sum_i t[m, r0 + i] * bt[i, col + j], with this tile's slice of scale * B^T staged
+// in shared memory (bt_s [r][BN], read as 16-byte broadcasts: every lane of the warp works on the
+// same columns of a different row) and t = x_r A^T read from global memory (one row per lane, L1
+// resident across the tile's pieces). The products run as paired fp32 FMAs.
+struct LoraTile {
+  const float* bt_s;  // nullptr: no LoRA entry covers this tile
+  const float* t;     // row m of T at the entry's first rank
+  int t_lo;           // column offset of the second partial product of T (0: none)
+  int r;
+};
+
+template <int BN, int CH>
+__device__ __forceinline__ void lora_cols(const LoraTile& lt, int col, float (&v)[CH]) {
+  f2 acc[CH / 2];
+#pragma unroll
+  for (int j = 0; j < CH / 2; ++j) acc[j] = dup2(0.f);
+#pragma unroll 2
+  for (int i = 0; i < lt.r; i += 4) {
+    float4 t4 = __ldg(reinterpret_cast<const float4*>(lt.t + i));
+    if (lt.t_lo) {
+      const float4 l4 = __ldg(reinterpret_cast<const float4*>(lt.t + lt.t_lo + i));
+      t4.x += l4.x;
+      t4.y += l4.y;
+      t4.z += l4.z;
+      t4.w += l4.w;
+    }
+    const float tv[4] = {t4.x, t4.y, t4.z, t4.w};
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float4* row = reinterpret_cast<const float4*>(lt.bt_s + (i + u) * BN + col);
+      const f2 tt = dup2(tv[u]);
+#pragma unroll
+      for (int q = 0; q < CH / 4; ++q) {
+        const float4 b = row[q];
+        acc[2 * q] = fma2(tt, make_float2(b.x, b.y), acc[2 * q]);
+        acc[2 * q + 1] = fma2(tt, make_float2(b.z, b.w), acc[2 * q + 1]);
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < CH / 2; ++j) {
+    v[2 * j] += acc[j].x;
+    v[2 * j + 1] += acc[j].y;
+  }
+}
+
+// After the loads landed: y = a_scale[m] w_scale[n] (hi + lo / 254) (+ bias) (+ add) (+ LoRA) (act).
+template <int BN, int NPLANES, int CH, bool LORA>
 __device__ __forceinline__ void finish_cols(const Params& p, int m, int n, bool row_ok, const uint32_t (&rh)[CH],
-                                            const uint32_t (&rl)[CH], float (&v)[CH], bool apply_act) {
+                                            const uint32_t (&rl)[CH], float (&v)[CH], bool apply_act,
+                                            const LoraTile& lt, int col) {
   const float as = row_ok ? __ldg(p.a_scale + m) : 0.0f;
   float ws[CH];
   ldv<CH>(p.w_scale + n, ws);
@@ -145,6 +204,9 @@ __device__ __forceinline__ void finish_cols(const Params& p, int m, int n, bool 
 #pragma unroll
     for (int j = 0; j < CH; ++j) v[j] += av[j];
   }
+  if constexpr (LORA) {
+    if (lt.bt_s && row_ok) lora_cols<BN, CH>(lt, col, v);
+  }
   if (apply_act && p.act != ANIMA_ACT_NONE) {
 #pragma unroll
     for (int j = 0; j < CH; ++j) v[j] = act_fn(v[j], p.act);
@@ -152,14 +214,14 @@ __device__ __forceinline__ void finish_cols(const Params& p, int m, int n, bool 
 }
 
 // Load CH accumulator columns and finish them (no overlap; used by the per-head epilogues).
-template <int BN, int NPLANES, int CH = 16>
+template <int BN, int NPLANES, bool LORA, int CH = 16>
 __device__ __forceinline__ void load_cols(const Params& p, uint32_t taddr, int col, int m, int n, bool row_ok,
-                                          float (&v)[CH], bool apply_act) {
+                                          float (&v)[CH], bool apply_act, const LoraTile& lt) {
   uint32_t rh[CH], rl[CH];
   issue_cols<BN, NPLANES, CH>(taddr, col, rh, rl);
   tmem_ld_wait(rh);
   if constexpr (NPLANES == 2) tmem_ld_wait(rl);
-  finish_cols<NPLANES, CH>(p, m, n, row_ok, rh, rl, v, apply_act);
+  finish_cols<BN, NPLANES, CH, LORA>(p, m, n, row_ok, rh, rl, v, apply_act, lt, col);
 }
 
 // ------------------------------------------------------------------ staged stores
@@ -225,9 +287,9 @@ __device__ __forceinline__ void stage_acquire() {
 
 // One tile's epilogue for this warp's 32 rows (m = row of this lane) over BN columns from n0.
 // stage: this warp's two staging buffers; y0: first row of the warp's quadrant.
-template <int BN, int NPLANES>
+template <int BN, int NPLANES, bool LORA>
 __device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap* tm_out, uint8_t* stage,
-                                              uint32_t taddr, int m, int y0, int n0) {
+                                              uint32_t taddr, int m, int y0, int n0, const LoraTile& lt) {
   const bool row_ok = m < p.M;
   const int lane = threadIdx.x & 31;
   const int esz = p.out_dtype == ANIMA_F32 ? 4 : 2;
@@ -251,7 +313,7 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap
       uint8_t* buf = stage + (chunk & 1) * STAGE_BUF;
       if (q == 0) stage_acquire<1>();
       float v[CH];
-      finish_cols<NPLANES, CH>(p, m, n0 + col, row_ok, rh[cur], rl[cur], v, true);
+      finish_cols<BN, NPLANES, CH, LORA>(p, m, n0 + col, row_ok, rh[cur], rl[cur], v, true, lt, col);
       if (resid) {
         float g[CH];
         if (p.gate) {
@@ -285,7 +347,7 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap
         uint8_t* buf = stage + (chunk & 1) * STAGE_BUF;
         if (q == 0) stage_acquire<1>();
         float v[CH];
-        load_cols<BN, NPLANES, CH>(p, taddr, h0 + col, m, nh + col, row_ok, v, true);
+        load_cols<BN, NPLANES, LORA, CH>(p, taddr, h0 + col, m, nh + col, row_ok, v, true, lt);
         stage_piece(buf, lane, p.out_dtype, q, v);
         if (q == ppc - 1) stage_flush(tm_out, buf, nh + chunk * chc, y0, false);
       }
@@ -295,7 +357,7 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap
 #pragma unroll 1
     for (int c = 0; c < 128; c += CH) {
       float v[CH];
-      load_cols<BN, NPLANES, CH>(p, taddr, h0 + c, m, nh + c, row_ok, v, true);
+      load_cols<BN, NPLANES, LORA, CH>(p, taddr, h0 + c, m, nh + c, row_ok, v, true, lt);
 #pragma unroll
       for (int j = 0; j < CH; ++j) ss += v[j] * v[j];
     }
@@ -311,8 +373,8 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap
         const int q = (c % chc) / CH;
         if (q == 0) stage_acquire<0>();
         float v1[CH], v2[CH];
-        load_cols<BN, NPLANES, CH>(p, taddr, h0 + c, m, nh + c, row_ok, v1, true);
-        load_cols<BN, NPLANES, CH>(p, taddr, h0 + 64 + c, m, nh + 64 + c, row_ok, v2, true);
+        load_cols<BN, NPLANES, LORA, CH>(p, taddr, h0 + c, m, nh + c, row_ok, v1, true, lt);
+        load_cols<BN, NPLANES, LORA, CH>(p, taddr, h0 + 64 + c, m, nh + 64 + c, row_ok, v2, true, lt);
         float a[CH], b[CH];
         ldv<CH>(w + c, a);
         ldv<CH>(w + 64 + c, b);
@@ -344,7 +406,7 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap
         uint8_t* buf = stage + (chunk & 1) * STAGE_BUF;
         if (q == 0) stage_acquire<1>();
         float v[CH];
-        load_cols<BN, NPLANES, CH>(p, taddr, h0 + col, m, nh + col, row_ok, v, true);
+        load_cols<BN, NPLANES, LORA, CH>(p, taddr, h0 + col, m, nh + col, row_ok, v, true, lt);
         float wv[CH];
         ldv<CH>(w + col, wv);
 #pragma unroll
@@ -364,16 +426,34 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
   return ok != 0;
 }
 
-template <int BN, int NPLANES>
+// LORA: the build with the LoRA side path in the epilogue (kept separate so the plain build's
+// register allocation does not carry it).
+// Barrier of one epilogue warpgroup (named barrier 1 + g, 128 threads) that also returns the AND of
+// `ok` over its threads, so the four warps take the same branch after a failed wait.
+__device__ __forceinline__ bool wg_sync_and(int g, bool ok) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, 128, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}\n"
+      : "=r"(r)
+      : "r"(ok ? 1u : 0u), "r"(1 + g)
+      : "memory");
+  return r != 0;
+}
+
+template <int BN, int NPLANES, bool LORA>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tm_hi, const __grid_constant__ CUtensorMap tm_lo,
                    const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_out,
                    const Params p) {
-  using C = Cfg<BN, NPLANES>;
+  using C = Cfg<BN, NPLANES, LORA>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* staging = smem + C::STAGES * C::STAGE_BYTES;  // 1024-aligned (stage sizes are)
-  uint64_t* full = reinterpret_cast<uint64_t*>(staging + C::STAGING_BYTES);
+  float* lora_smem = reinterpret_cast<float*>(staging + C::STAGING_BYTES);
+  uint64_t* full = reinterpret_cast<uint64_t*>(staging + C::STAGING_BYTES + C::LORA_BYTES);
   uint64_t* empty = full + C::STAGES;
   uint64_t* acc_full = empty + C::STAGES;
   uint64_t* acc_empty = acc_full + 2;
@@ -511,13 +591,36 @@ __global__ void __launch_bounds__(THREADS, 1)
          tile += C::ACC_BUFS * gridDim.x, t += C::ACC_BUFS) {
       const int buf = g;
       const uint32_t acc_phase = (t / C::ACC_BUFS) & 1;
-      if (!warp_wait(&acc_full[buf], acc_phase, abort_flag, kErrTimeoutAcc)) break;
+      bool ok = warp_wait(&acc_full[buf], acc_phase, abort_flag, kErrTimeoutAcc);
+      if constexpr (LORA) ok = wg_sync_and(g, ok);  // also: the previous tile's LoRA slice is read
+      if (!ok) break;
       tc_fence_after();
       int mb, nb;
       tile_coords(p, tile, mb, nb);
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + buf * C::ACC_COLS;
-      epilogue_tile<BN, NPLANES>(p, &tm_out, staging + warp * 2 * STAGE_BUF, taddr, mb * BM + row,
-                                 mb * BM + quad * 32, nb * BN);
+      LoraTile lt{nullptr, nullptr, 0, 0};
+      if constexpr (LORA) {
+        // the entry covering this tile (entries are BN-aligned): stage its slice of scale * B^T
+        const int n0 = nb * BN;
+        int e = -1;
+        for (int i = 0; i < p.lora_count; ++i)
+          if (n0 >= p.lora_off[i] && n0 < p.lora_off[i] + p.lora_n[i]) e = i;
+        if (e >= 0) {
+          float* bt_s = lora_smem + g * LORA_R * BN;
+          const int r = p.lora_r[e];
+          const int tid = threadIdx.x - g * 128;
+          for (int k = tid; k < r * BN / 4; k += 128) {
+            const int i = k / (BN / 4), c4 = k % (BN / 4);
+            reinterpret_cast<float4*>(bt_s)[k] =
+                __ldg(reinterpret_cast<const float4*>(p.lora_bt + static_cast<size_t>(p.lora_r0[e] + i) * p.ld_bt + n0) + c4);
+          }
+          wg_sync_and(g, true);
+          const int m = mb * BM + row;
+          lt = LoraTile{bt_s, p.lora_t + static_cast<size_t>(m < p.M ? m : 0) * p.ld_t + p.lora_r0[e], p.lora_t_lo, r};
+        }
+      }
+      epilogue_tile<BN, NPLANES, LORA>(p, &tm_out, staging + warp * 2 * STAGE_BUF, taddr, mb * BM + row,
+                                 mb * BM + quad * 32, nb * BN, lt);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
@@ -534,9 +637,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 }
 
-template <int BN, int NPLANES>
+template <int BN, int NPLANES, bool LORA>
 int launch(anima_ctx* ctx, const anima_qact* x, const anima_weight* W, const anima_linear_opts* o) {
-  using C = Cfg<BN, NPLANES>;
+  using C = Cfg<BN, NPLANES, LORA>;
   const int M = x->rows, N = W->N, K = W->K;
   CUtensorMap tm_hi, tm_lo, tm_w;
   uint64_t adims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M)};
@@ -591,6 +694,18 @@ int launch(anima_ctx* ctx, const anima_qact* x, const anima_weight* W, const ani
   p.rope_rows = o->rope_rows;
   p.n_q = o->n_q;
   p.eps = o->eps > 0 ? o->eps : 1e-6f;
+  p.lora_t = o->lora_t;
+  p.ld_t = o->ld_t;
+  p.lora_t_lo = o->lora_t_lo;
+  p.lora_bt = o->lora_bt;
+  p.ld_bt = o->ld_bt;
+  p.lora_count = o->lora_t ? o->lora_count : 0;
+  for (int e = 0; e < 4; ++e) {
+    p.lora_off[e] = o->lora_off[e];
+    p.lora_n[e] = o->lora_n[e];
+    p.lora_r0[e] = o->lora_r0[e];
+    p.lora_r[e] = o->lora_r[e];
+  }
   p.num_m_blocks = (M + BM - 1) / BM;
   p.num_n_blocks = N / BN;
   p.num_k_blocks = K / BK;
@@ -603,14 +718,14 @@ int launch(anima_ctx* ctx, const anima_qact* x, const anima_weight* W, const ani
 
   static bool attr_set = false;
   if (!attr_set) {
-    ANIMA_CUDA(cudaFuncSetAttribute(gemm_i8_kernel<BN, NPLANES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    ANIMA_CUDA(cudaFuncSetAttribute(gemm_i8_kernel<BN, NPLANES, LORA>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     C::SMEM_BYTES));
     attr_set = true;
   }
   const int grid = p.num_tiles < ctx->num_sms ? p.num_tiles : ctx->num_sms;
   ProfScope prof(ctx, NPLANES == 2 ? "linear.i8x2" : "linear.i8", 2.0 * M * N * K,
                  static_cast<double>(M) * K * NPLANES + static_cast<double>(N) * K);
-  gemm_i8_kernel<BN, NPLANES><<<grid, THREADS, C::SMEM_BYTES, ctx->stream>>>(tm_hi, tm_lo, tm_w, tm_out, p);
+  gemm_i8_kernel<BN, NPLANES, LORA><<<grid, THREADS, C::SMEM_BYTES, ctx->stream>>>(tm_hi, tm_lo, tm_w, tm_out, p);
   return check_launch("gemm_i8_kernel");
 }
 
@@ -652,6 +767,22 @@ extern "C" int anima_linear(anima_ctx* ctx, const anima_qact* x, const anima_wei
     ANIMA_REQUIRE(o->n_q % 128 == 0 && 2 * o->n_q <= W->N, "anima_linear: bad n_q %d", o->n_q);
   }
   if (o->out_mode == ANIMA_OUT_HEAD_NORM) ANIMA_REQUIRE(o->norm_q, "anima_linear: head-norm epilogue needs norm_q");
+  if (o->lora_t) {
+    ANIMA_REQUIRE(o->lora_bt && o->lora_count >= 1 && o->lora_count <= 4, "anima_linear: LoRA needs t, bt and 1-4 entries");
+    ANIMA_REQUIRE(aligned16(o->lora_t) && aligned16(o->lora_bt) && o->ld_t % 4 == 0 && o->ld_bt % 4 == 0 &&
+                      o->lora_t_lo >= 0 && o->lora_t_lo % 4 == 0 &&
+                      o->ld_bt >= W->N,
+                  "anima_linear: LoRA t/bt must be 16-byte aligned with ld_t, ld_bt multiples of 4 (ld_bt >= N)");
+    for (int e = 0; e < o->lora_count; ++e) {
+      ANIMA_REQUIRE(o->lora_off[e] >= 0 && o->lora_n[e] > 0 && o->lora_off[e] % 128 == 0 && o->lora_n[e] % 128 == 0 &&
+                        o->lora_off[e] + o->lora_n[e] <= W->N && o->lora_r[e] > 0 && o->lora_r[e] % 4 == 0 &&
+                        o->lora_r[e] <= gemm::LORA_R &&
+                        o->lora_r0[e] >= 0 && o->lora_r0[e] % 4 == 0 &&
+                        o->lora_t_lo + o->lora_r0[e] + o->lora_r[e] <= o->ld_t,
+                    "anima_linear: LoRA entry %d (off %d, n %d, r0 %d, r %d) invalid", e, o->lora_off[e],
+                    o->lora_n[e], o->lora_r0[e], o->lora_r[e]);
+    }
+  }
   // the epilogue reads per-column vectors 16 bytes at a time
   ANIMA_REQUIRE(aligned16(W->scale) && (!W->bias || aligned16(W->bias)) && (!o->norm_q || aligned16(o->norm_q)) &&
                     (!o->norm_k || aligned16(o->norm_k)) && (!o->rope || aligned16(o->rope)) &&
@@ -661,11 +792,14 @@ extern "C" int anima_linear(anima_ctx* ctx, const anima_qact* x, const anima_wei
   // epilogue overlaps the next tile's MMAs; for long K (>= 4096) the MMA time per tile dwarfs the
   // epilogue and 256-column tiles (one buffer) read 25% fewer shared-memory bytes per MMA.
   // One plane: 256-column tiles, double-buffered.
+  // LoRA side paths: 128-column tiles (each inside one entry), with the entry's B slice staged
+  // in shared memory in place of one pipeline stage.
   const bool two = x->lo != nullptr;
+  if (o->lora_t) return two ? gemm::launch<128, 2, true>(ctx, x, W, o) : gemm::launch<128, 1, true>(ctx, x, W, o);
   if (two) {
-    if (W->N % 256 == 0 && W->K >= 4096) return gemm::launch<256, 2>(ctx, x, W, o);
-    return gemm::launch<128, 2>(ctx, x, W, o);
+    if (W->N % 256 == 0 && W->K >= 4096) return gemm::launch<256, 2, false>(ctx, x, W, o);
+    return gemm::launch<128, 2, false>(ctx, x, W, o);
   }
-  if (W->N % 256 == 0) return gemm::launch<256, 1>(ctx, x, W, o);
-  return gemm::launch<128, 1>(ctx, x, W, o);
+  if (W->N % 256 == 0) return gemm::launch<256, 1, false>(ctx, x, W, o);
+  return gemm::launch<128, 1, false>(ctx, x, W, o);
 }

@@ -58,7 +58,10 @@ class LinearOpts(C.Structure):
     _fields_ = [("act", C.c_int), ("add", C.c_void_p), ("ld_add", C.c_int), ("out_mode", C.c_int),
                 ("out_dtype", C.c_int), ("out", C.c_void_p), ("ldo", C.c_int), ("gate", C.c_void_p),
                 ("gate_off", C.c_int), ("norm_q", C.c_void_p), ("norm_k", C.c_void_p), ("rope", C.c_void_p),
-                ("rope_rows", C.c_int), ("n_q", C.c_int), ("eps", C.c_float)]
+                ("rope_rows", C.c_int), ("n_q", C.c_int), ("eps", C.c_float),
+                ("lora_t", C.c_void_p), ("ld_t", C.c_int), ("lora_t_lo", C.c_int), ("lora_bt", C.c_void_p), ("ld_bt", C.c_int),
+                ("lora_count", C.c_int), ("lora_off", C.c_int * 4), ("lora_n", C.c_int * 4),
+                ("lora_r0", C.c_int * 4), ("lora_r", C.c_int * 4)]
 
 
 class AttentionArgs(C.Structure):

@@ -161,6 +161,8 @@ def attach_loras(registries, active):
         if reg:
             for (W, _, _) in reg.values():
                 W._lora_cat = None
+                W._lora_bt = None
+                W._lora_down = None
 
 
 def _cat_A(W):
@@ -194,3 +196,76 @@ def lora_delta(x, W) -> torch.Tensor:
                  C.c_void_p(0), 0)
         r0 += e["r"]
     return D
+
+
+def _fusable(W) -> bool:
+    """The fused epilogue takes up to 4 entries with 128-aligned column ranges and ranks that are
+    multiples of 4 up to 32; anything else goes through the [M, N] delta (lora_delta)."""
+    return (0 < len(W.lora) <= 4 and all(e["off"] % 128 == 0 and e["n"] % 128 == 0 and e["r"] % 4 == 0
+                                         and e["r"] <= 32 for e in W.lora))
+
+
+def _cat_Bt(W):
+    """scale_e * B_e^T of every entry in its rows and columns of one [sum r, N] matrix (cached per
+    attach; only each entry's own columns are read)."""
+    bt = getattr(W, "_lora_bt", None)
+    if bt is None:
+        R = sum(e["r"] for e in W.lora)
+        bt = torch.zeros(R, W.N, dtype=torch.float32, device=W.lora[0]["B"].device)
+        r0 = 0
+        for e in W.lora:
+            bt[r0:r0 + e["r"], e["off"]:e["off"] + e["n"]] = (e["B"].float() * e["scale"]).t()
+            r0 += e["r"]
+        W._lora_bt = bt
+    return bt
+
+
+def _down_linear(W):
+    """All entries' A (rotated, fp32 [R, K]) as an int8 linear for the tensor-core GEMM, in two
+    planes so that x_r A^T keeps ~16 bits: A ~= s (hi + lo / 254) per row, hi in rows [0, R) with
+    scale s, lo in rows [R, 2R) with scale s / 254, zero rows up to a multiple of 128 (cached per
+    attach). T = x_r A^T is then the sum of the two column halves of one GEMM's output."""
+    from .weights import Linear
+
+    lin = getattr(W, "_lora_down", None)
+    if lin is None:
+        A = _cat_A(W).float()
+        R, K = A.shape
+        s = A.abs().amax(1).clamp(min=1e-30) / 127.0
+        a = A / s[:, None]
+        hi = torch.round(a)
+        lo = torch.round((a - hi) * 254.0)
+        n2 = ((2 * R + 127) // 128) * 128
+        q = torch.zeros(n2, K, dtype=torch.int8, device=A.device)
+        q[:R] = hi.to(torch.int8)
+        q[R:2 * R] = lo.to(torch.int8)
+        sc = torch.ones(n2, dtype=torch.float32, device=A.device)
+        sc[:R] = s
+        sc[R:2 * R] = s / 254.0
+        lin = Linear("i8", n2, K, q.contiguous(), sc.contiguous(), name=W.name + ".lora_down")
+        W._lora_down = lin
+    return lin
+
+
+def lora_epilogue(x, W, opts) -> list:
+    """Fill the LoRA fields of anima_linear_opts for the fused epilogue: T = x_r A^T of all entries
+    (one int8 tensor-core GEMM, `_down_linear`), then the GEMM adds T B^T per entry before its
+    activation. Returns the tensors that must stay alive until the GEMM is enqueued, or None when
+    W's entries do not fit the fused form."""
+    from .ops import linear
+
+    if not _fusable(W) or W.K % 128:
+        return None
+    A = _cat_A(W)
+    R = A.shape[0]
+    down = _down_linear(W)
+    T = linear(x, down)                      # [M, 2R (+ padding)]: hi and lo partial products
+    bt = _cat_Bt(W)
+    opts.lora_t, opts.ld_t, opts.lora_t_lo = T.data_ptr(), down.N, R
+    opts.lora_bt, opts.ld_bt = bt.data_ptr(), W.N
+    opts.lora_count = len(W.lora)
+    r0 = 0
+    for i, e in enumerate(W.lora):
+        opts.lora_off[i], opts.lora_n[i], opts.lora_r0[i], opts.lora_r[i] = e["off"], e["n"], r0, e["r"]
+        r0 += e["r"]
+    return [T, bt]

@@ -172,21 +172,24 @@ def linear(x, W, *, out: torch.Tensor | None = None, resid: bool = False, gate: 
     mode: "store" | "qkv" (per-head RMSNorm + RoPE on q/k heads, qk = (qn, kn)) |
           "head_norm" (per-head RMSNorm with qk[0]).
     """
-    from .lora import lora_delta
+    from .lora import lora_delta, lora_epilogue
 
     if W.kind in ("bf16", "f32"):
         return matmul(x, W, act=act, out=out, resid=resid, gate=gate, g_off=g_off)
     if not isinstance(x, QuantRows):
         x = rotate_quant(x.reshape(-1, W.K).contiguous(), planes)
     M = x.rows
+    o = dev.LinearOpts()
+    keep = None
     if W.lora:
-        delta = lora_delta(x, W)
-        add = delta if add is None else add + delta
+        keep = lora_epilogue(x, W, o)   # fused into the GEMM epilogue
+        if keep is None:                 # entries the fused form does not take: an added delta
+            delta = lora_delta(x, W)
+            add = delta if add is None else add + delta
     if out is None:
         if resid:
             raise dev.AnimaError(1, "resid=True needs out")
         out = torch.empty(M, W.N, dtype=out_dtype, device=x.hi.device)
-    o = dev.LinearOpts()
     o.act = dev.ACT[act]
     o.add = add.data_ptr() if add is not None else 0
     o.ld_add = add.stride(0) if add is not None else 0
@@ -208,6 +211,7 @@ def linear(x, W, *, out: torch.Tensor | None = None, resid: bool = False, gate: 
     qa = x.c()
     w = W.c()
     ctx_for(x.hi).call("anima_linear", C.byref(qa), C.byref(w), C.byref(o), tag=name, work=2.0 * M * W.N * W.K)
+    del keep
     return out
 
 

@@ -88,6 +88,21 @@ typedef struct {
   int rope_rows;
   int n_q;             /* QKV: columns [0, n_q) q heads, [n_q, 2 n_q) k heads, the rest v */
   float eps;
+  /* LoRA side paths added in the epilogue before the activation (ops.js:55-57, 70-87):
+     y[m, n] += sum_{i < r_e} t[m, r0_e + i] * lora_bt[r0_e + i, n] for the entry e whose
+     columns [off_e, off_e + n_e) hold n, where t[m, j] = lora_t[m, j] (+ lora_t[m, lora_t_lo + j]
+     when lora_t_lo > 0: x_r A^T computed as two partial products, e.g. by anima_linear with A in two
+     int8 planes). lora_t [M, ld_t] holds x_r A^T of all entries stacked (or anima_lora_down's
+     result); lora_bt [R, ld_bt] holds scale_e * B_e^T in the entry's columns (only those are read).
+     Entries: off and n multiples of 128, r a multiple of 4 and at most 32, at most 4 entries;
+     lora_t NULL = none. */
+  const float* lora_t;
+  int ld_t;
+  int lora_t_lo;
+  const float* lora_bt;
+  int ld_bt;
+  int lora_count;
+  int lora_off[4], lora_n[4], lora_r0[4], lora_r[4];
 } anima_linear_opts;
 
 typedef struct {

@@ -256,6 +256,63 @@ def test_linear_qkv_norm_rope_epilogue(ops):
     assert rel_l2(h, ref.reshape(M, -1)) < 2e-6
 
 
+def _lora_entries(K, spec, seed):
+    """LoRA entries [(off, n, r, scale)] with A [r, K], B [n, r] on the device + numpy copies."""
+    out = []
+    for i, (off, n, r, scale) in enumerate(spec):
+        A = randn((r, K), seed + 2 * i, 0.01)
+        B = randn((n, r), seed + 2 * i + 1, 0.01)
+        out.append({"A": A.to(DEV), "B": B.to(DEV), "r": r, "scale": scale, "off": off, "n": n,
+                    "A_np": A.numpy(), "B_np": B.numpy()})
+    return out
+
+
+def _lora_ref(qa, entries, N):
+    x = qa.dequant().cpu().double().numpy()
+    d = np.zeros((x.shape[0], N))
+    for e in entries:
+        d[:, e["off"]:e["off"] + e["n"]] += e["scale"] * (x @ e["A_np"].T.astype(np.float64)) @ e["B_np"].T
+    return d
+
+
+# fused (ranks multiple of 4, 16-aligned ranges) and the [M, N] delta fallback (rank 6)
+@pytest.mark.parametrize("spec,mode", [([(0, 2048, 32, 1.0), (2048, 2048, 32, 0.5), (4096, 2048, 16, 2.0)], "store"),
+                                       ([(128, 1024, 8, 1.5)], "resid"),
+                                       ([(0, 2048, 32, 1.0), (2048, 2048, 32, 1.0)], "qkv"),
+                                       ([(0, 6144, 6, 1.0)], "store")])
+def test_linear_lora_epilogue(ops, spec, mode):
+    M, K = 260, 2048
+    N = 6144 if mode in ("store", "qkv") else 2048
+    lin, wq, ws = make_linear(N, K, 8)
+    lin.lora = [{k: v for k, v in e.items() if not k.endswith("_np")} for e in _lora_entries(K, spec, 50)]
+    ents = _lora_entries(K, spec, 50)
+    qa = ops.rotate_quant((randn((M, K), 33)).to(DEV))
+    y = gemm_ref(qa, wq, ws) + _lora_ref(qa, ents, N)
+    if mode == "store":
+        out = ops.linear(qa, lin, act="gelu").cpu().numpy()
+        assert rel_l2(out, oracle.gelu(y.astype(np.float32))) < 2e-6
+    elif mode == "resid":
+        x0 = randn((M, N), 34)
+        mod = randn((6144,), 35, 0.5)
+        out = x0.clone().to(DEV)
+        ops.linear(qa, lin, out=out, resid=True, gate=mod.to(DEV), g_off=4096)
+        assert rel_l2(out.cpu().numpy(), x0.numpy() + mod[4096:].numpy() * y) < 1e-6
+    else:
+        Hp, Wp = 10, 26
+        qn, kn = 1 + randn((128,), 36, 0.1), 1 + randn((128,), 37, 0.1)
+        cs = torch.from_numpy(pkg("dit").rope_table(Hp, Wp)).to(DEV)
+        out = ops.linear(qa, lin, mode="qkv", qk=(qn.to(DEV), kn.to(DEV)), rope_cs=cs, n_q=2048,
+                         out_dtype=torch.float32).cpu().numpy()
+        yf = y.astype(np.float32)
+        cos, sin = oracle.dit_rope(Hp, Wp)
+        cos = np.concatenate([cos, cos], -1)[:, None]
+        sin = np.concatenate([sin, sin], -1)[:, None]
+        q = oracle.rms_norm(yf[:, :2048].reshape(M, 16, 128), qn.numpy())
+        q = q * cos + oracle.rotate_half(q) * sin
+        assert rel_l2(out[:, :2048], q.reshape(M, -1)) < 2e-6
+        assert rel_l2(out[:, 4096:], yf[:, 4096:]) < 1e-6
+
+
 def test_linear_rejects_bad_shapes(ops):
     dev = pkg("device")
     lin, _, _ = make_linear(2048, 2048, 7)
