@@ -789,15 +789,21 @@ extern "C" int anima_linear(anima_ctx* ctx, const anima_qact* x, const anima_wei
                     (!o->gate || (aligned16(o->gate) && o->gate_off % 4 == 0)),
                 "anima_linear: scale/bias/gate/norm/rope vectors must be 16-byte aligned (gate_off a multiple of 4)");
   // Two planes: 128-column tiles double-buffer both accumulators (2 x 2 x 128 TMEM columns) so the
-  // epilogue overlaps the next tile's MMAs; for long K (>= 4096) the MMA time per tile dwarfs the
-  // epilogue and 256-column tiles (one buffer) read 25% fewer shared-memory bytes per MMA.
-  // One plane: 256-column tiles, double-buffered.
+  // epilogue overlaps the next tile's MMAs. One plane: 256-column tiles, double-buffered.
   // LoRA side paths: 128-column tiles (each inside one entry), with the entry's B slice staged
   // in shared memory in place of one pipeline stage.
   const bool two = x->lo != nullptr;
   if (o->lora_t) return two ? gemm::launch<128, 2, true>(ctx, x, W, o) : gemm::launch<128, 1, true>(ctx, x, W, o);
   if (two) {
-    if (W->N % 256 == 0 && W->K >= 4096) return gemm::launch<256, 2, false>(ctx, x, W, o);
+    // 128-column tiles: double-buffered accumulators and three pipeline stages measured faster than
+    // 256-column tiles at every block shape, K = 8192 included (135 vs 169 us for the 8192 -> 2048
+    // linear at 4096 tokens). ANIMA_GEMM_BN2=256 selects the wide tile for experiments.
+    static const int bn2 = [] {
+      const char* e = getenv("ANIMA_GEMM_BN2");
+      return e ? atoi(e) : 0;
+    }();
+    const bool wide = bn2 == 256;
+    if (W->N % 256 == 0 && wide) return gemm::launch<256, 2, false>(ctx, x, W, o);
     return gemm::launch<128, 2, false>(ctx, x, W, o);
   }
   if (W->N % 256 == 0) return gemm::launch<256, 1, false>(ctx, x, W, o);
