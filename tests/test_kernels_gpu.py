@@ -313,6 +313,42 @@ def test_linear_lora_epilogue(ops, spec, mode):
         assert rel_l2(out[:, 4096:], yf[:, 4096:]) < 1e-6
 
 
+# block-sized shapes whose tile counts leave a partial last wave on 148 SMs
+@pytest.mark.parametrize("M,N,mode", [(4096, 2048, "resid"), (2560, 2048, "store"), (2560, 6144, "qkv")])
+def test_linear_partial_last_wave(ops, M, N, mode):
+    K = 2048
+    lin, wq, ws = make_linear(N, K, 9)
+    qa = ops.rotate_quant((randn((M, K), 38)).to(DEV))
+    y = gemm_ref(qa, wq, ws)
+    if mode == "resid":
+        x0 = randn((M, N), 39)
+        mod = randn((6144,), 40, 0.5)
+        out = x0.clone().to(DEV)
+        ops.linear(qa, lin, out=out, resid=True, gate=mod.to(DEV), g_off=4096)
+        assert rel_l2(out.cpu().numpy(), x0.numpy() + mod[4096:].numpy() * y) < 1e-6
+    elif mode == "store":
+        assert rel_l2(ops.linear(qa, lin).cpu().numpy(), y) < 1e-6
+    else:
+        Hp, Wp = 40, 64
+        qn, kn = 1 + randn((128,), 41, 0.1), 1 + randn((128,), 42, 0.1)
+        cs = torch.from_numpy(pkg("dit").rope_table(Hp, Wp)).to(DEV)
+        out = ops.linear(qa, lin, mode="qkv", qk=(qn.to(DEV), kn.to(DEV)), rope_cs=cs, n_q=2048,
+                         out_dtype=torch.float32).cpu().numpy()
+        yf = y.astype(np.float32)
+        cos, sin = oracle.dit_rope(Hp, Wp)
+        cos = np.concatenate([cos, cos], -1)[:, None]
+        sin = np.concatenate([sin, sin], -1)[:, None]
+        k = oracle.rms_norm(yf[:, 2048:4096].reshape(M, 16, 128), kn.numpy())
+        k = k * cos + oracle.rotate_half(k) * sin
+        assert rel_l2(out[:, 2048:4096], k.reshape(M, -1)) < 2e-6
+        assert rel_l2(out[:, 4096:], yf[:, 4096:]) < 1e-6
+    # the same call twice gives the same bits
+    if mode == "store":
+        a = ops.linear(qa, lin).cpu()
+        b = ops.linear(qa, lin).cpu()
+        assert torch.equal(a, b)
+
+
 def test_linear_rejects_bad_shapes(ops):
     dev = pkg("device")
     lin, _, _ = make_linear(2048, 2048, 7)
