@@ -490,6 +490,36 @@ __global__ void rope_kernel(T* x, int L, int H, int D, int row_stride, int col_o
 }
 
 // ------------------------------------------------------------------ elementwise
+// y = c0 x0 + c1 x1 + c2 x2 + c3 x3 (NULL terms dropped), 4 elements per thread when aligned.
+__global__ void lincomb_kernel(float* y, long long n, const float* x0, const float* x1, const float* x2,
+                               const float* x3, float c0, float c1, float c2, float c3) {
+  const long long i = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
+  if (i >= n) return;
+  const float* xs[4] = {x0, x1, x2, x3};
+  const float cs[4] = {c0, c1, c2, c3};
+  if (i + 4 <= n) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      if (!xs[k]) continue;
+      const float4 v = *reinterpret_cast<const float4*>(xs[k] + i);
+      acc.x = fmaf(cs[k], v.x, acc.x);
+      acc.y = fmaf(cs[k], v.y, acc.y);
+      acc.z = fmaf(cs[k], v.z, acc.z);
+      acc.w = fmaf(cs[k], v.w, acc.w);
+    }
+    *reinterpret_cast<float4*>(y + i) = acc;
+  } else {
+    for (long long e = i; e < n; ++e) {
+      float acc = 0.f;
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        if (xs[k]) acc = fmaf(cs[k], xs[k][e], acc);
+      y[e] = acc;
+    }
+  }
+}
+
 __global__ void elementwise_kernel(int op, const float* __restrict__ a, const float* __restrict__ b, float* y,
                                    long long n) {
   const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -905,6 +935,17 @@ int anima_rope(anima_ctx* ctx, void* x, int dtype, int L, int H, int D, int row_
   else if (dtype == ANIMA_F16) rope_kernel<__half><<<grid1(n, 256), 256, 0, ctx->stream>>>((__half*)x, L, H, D, row_stride, col_off, rope, rope_rows);
   else return set_error(ANIMA_ERR_ARG, "anima_rope: dtype %d", dtype);
   return check_launch("rope_kernel");
+}
+
+int anima_lincomb(anima_ctx* ctx, float* y, long long n, const float* x0, const float* x1, const float* x2,
+                  const float* x3, const float* c) {
+  ANIMA_REQUIRE(ctx && y && c && n > 0, "anima_lincomb: bad argument");
+  const float* xs[4] = {x0, x1, x2, x3};
+  ANIMA_REQUIRE(al16(y), "anima_lincomb: y must be 16-byte aligned");
+  for (int k = 0; k < 4; ++k) ANIMA_REQUIRE(!xs[k] || al16(xs[k]), "anima_lincomb: x%d must be 16-byte aligned", k);
+  lincomb_kernel<<<static_cast<int>((n + 1023) / 1024), 256, 0, ctx->stream>>>(y, n, x0, x1, x2, x3, c[0], c[1], c[2],
+                                                                              c[3]);
+  return check_launch("lincomb_kernel");
 }
 
 int anima_elementwise(anima_ctx* ctx, int op, const float* a, const float* b, float* y, long long n) {

@@ -32,7 +32,7 @@ EXPORTS = [
     "anima_unpack_w4", "anima_linear", "anima_matmul", "anima_lora_down", "anima_layernorm_mod", "anima_layernorm_mod_quant",
     "anima_rotate", "anima_rotate_quant", "anima_act_rotate_quant", "anima_quant_rows", "anima_rmsnorm", "anima_qk_norm_rope", "anima_rope",
     "anima_attention", "anima_elementwise", "anima_zero", "anima_patchify", "anima_unpatchify",
-    "anima_timestep_embedding", "anima_euler_step",
+    "anima_timestep_embedding", "anima_euler_step", "anima_lincomb",
 ]
 
 

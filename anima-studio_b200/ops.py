@@ -293,6 +293,22 @@ def euler_step(x: torch.Tensor, v: torch.Tensor, sigma: float, sigma_next: float
     return x
 
 
+def lincomb(out: torch.Tensor, *terms) -> torch.Tensor:
+    """out = sum of c * t over up to four (c, t) pairs of fp32 tensors with out's element count; out
+    may be one of the t (the samplers' axpby, samplers.js:97-101)."""
+    if not 1 <= len(terms) <= 4:
+        raise ValueError("lincomb takes one to four (coefficient, tensor) terms")
+    xs = [C.c_void_p(0)] * 4
+    cs = (C.c_float * 4)(0.0, 0.0, 0.0, 0.0)
+    for k, (c, t) in enumerate(terms):
+        if t.dtype != torch.float32 or t.numel() != out.numel() or not t.is_contiguous():
+            raise dev.AnimaError(1, "lincomb: terms must be contiguous fp32 tensors of out's size")
+        xs[k] = ptr(t)
+        cs[k] = float(c)
+    ctx_for(out).call("anima_lincomb", ptr(out), out.numel(), *xs, cs)
+    return out
+
+
 def unpack_w4(packed: torch.Tensor, s_rel: torch.Tensor, codebook: torch.Tensor, N: int, K: int) -> torch.Tensor:
     """4-bit codes -> int8-grid values [N, K], bit-exact with tools/quant.py:179-180."""
     out = torch.empty(N, K, dtype=torch.int8, device=packed.device)

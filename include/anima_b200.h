@@ -207,6 +207,12 @@ int anima_timestep_embedding(anima_ctx* ctx, const float* sigmas, int B, float* 
  * den_out may be NULL. */
 int anima_euler_step(anima_ctx* ctx, float* x, const float* v, const float* v_uncond, float cfg, float sigma,
                      float sigma_next, long long n, float* den_out);
+/* The samplers' latent updates (samplers.js:104-218: axpby and the noise/derivative terms of
+ * euler_a, dpmpp_2m and er_sde, and den = x - sigma v with CFG in pipeline.js:260-269):
+ *   y[i] = c[0] x0[i] + c[1] x1[i] + c[2] x2[i] + c[3] x3[i] over n fp32 elements.
+ * A NULL x_k drops its term; y may be any of the x_k (elementwise, in place). */
+int anima_lincomb(anima_ctx* ctx, float* y, long long n, const float* x0, const float* x1, const float* x2,
+                  const float* x3, const float* c);
 
 #ifdef __cplusplus
 }

@@ -114,3 +114,14 @@ def test_full_forward_and_euler_match_reference(fmt):
     if steps == 2:
         assert rel_l2(lat, g["latent_final"]) < 1e-4
     print(f"oracle forward {fmt}: {time.time() - t0:.1f}s")
+
+
+def test_beta_scheduler_matches_reference_algorithm():
+    """pipeline.sigmas_beta (scipy's Beta quantile) against the reference's own bisection of its
+    continued-fraction Beta CDF (app/samplers.js:24-93, restated in oracle/samplers_np.py)."""
+    from oracle import samplers_np
+    from tests.conftest import pkg
+    pl = pkg("pipeline")
+    for steps in (1, 3, 4, 8, 12, 20, 30, 50):
+        for shift in (1.0, 3.0, 6.0):
+            assert pl.sigmas_beta(steps, shift) == samplers_np.sigmas_beta(steps, shift)
