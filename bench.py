@@ -355,6 +355,76 @@ def run_tp(args, world, rank, local):
     print(json.dumps(line), flush=True)
 
 
+def run_cfg(args, world, rank, local):
+    """the base model with classifier-free guidance (cond + negative context
+    as one batch of 2 per image), Euler, 30 steps per image at 1024^2 or 1536^2; images (seeds) are
+    split over the ranks with no collective on the data path (weak scaling)."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    syn, ditm, pl, sh = pkg("synthetic"), pkg("dit"), pkg("pipeline"), pkg("sharding")
+    seed, steps_per_image = 1234, 30
+    lat = args.res // 8
+    tensors = syn.dit_tensors(seed, "int8", 28, device="cuda")
+    dit = ditm.AnimaDiT(tensors, "cuda", precision=args.precision,
+                        attn_dtype=torch.bfloat16 if args.attn == "bf16" else torch.float16)
+    del tensors
+    torch.cuda.empty_cache()
+    pad = torch.zeros(256, 1024)
+    cond = dit.prepare_context(torch.cat([syn.randn(seed, "ctx", (256, 1024)), pad]).cuda())
+    uncond = dit.prepare_context(torch.cat([syn.randn(seed, "ctx_neg", (256, 1024)), pad]).cuda())
+    image = sh.seed_shard(64, rank, world)[0] if world <= 64 else rank  # this rank's first seed of the 64
+    noise = syn.randn(seed + image, "noise", (1, 16, lat, lat)).cuda()
+    graphed = pl.GraphedSampler(dit, cond, steps_per_image, 1, lat, lat, cfg=args.cfg, uncond=uncond)
+    graphed.start(noise)
+
+    def step(i):
+        j = i % steps_per_image
+        graphed.replay(j)
+        if j == steps_per_image - 1:
+            graphed.start(noise)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(local)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        step(args.warmup + i)
+    e1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    ms = sh.max_over_ranks(e0.elapsed_time(e1), "cuda")
+    del graphed
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    value = world * args.steps / (ms * 1e-3)
+    tokens = (lat // 2) ** 2
+    line = {"metric": f"DiT denoise steps/sec with CFG (batch 2 per image) at {args.res}^2 ({tokens} tokens)",
+            "value": value, "unit": "steps/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8", "data": "synthetic",
+            "config": {"workload": f"BASELINE configs[4]: base model, INT8 ConvRot, cfg {args.cfg} with a negative "
+                                   f"context (cond and uncond as one batch of 2), Euler {steps_per_image} steps per "
+                                   f"image, {args.res}x{args.res}, one image per GPU at a time (seeds split over "
+                                   "the ranks)", "tokens": tokens, "rows_per_gemm": 2 * tokens,
+                       "images_per_s": value / steps_per_image, "launch": "CUDA graph per step",
+                       "parallelism": f"dp{world}", "precision": args.precision, "attention": args.attn},
+            "clocks": clk}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--kernel", default=None, help="time one kernel case instead (mlp1|mlp2|qkv|oproj|attn|ln|gelu|rotq|xembed|final)")
@@ -371,6 +441,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch kernels from Python per step instead of CUDA graphs")
+    ap.add_argument("--cfg", type=float, default=None,
+                    help="BASELINE configs[4]: guidance scale with a negative context (batch 2 per image), 30 steps")
+    ap.add_argument("--res", type=int, default=1024, help="with --cfg: image side (1024 or 1536)")
     ap.add_argument("--tp", action="store_true",
                     help="single-image latency: heads sharded over the --gpus ranks, NCCL all-reduce per block")
     args = ap.parse_args()
@@ -381,6 +454,8 @@ def main():
         return run_reference(args, world, rank)
     if args.tp:
         return run_tp(args, world, rank, local)
+    if args.cfg is not None:
+        return run_cfg(args, world, rank, local)
 
     import torch
     import torch.distributed as dist
