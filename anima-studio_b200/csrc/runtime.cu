@@ -192,6 +192,41 @@ int anima_sync(anima_ctx* ctx) {
   return ANIMA_OK;
 }
 
+// Failure-path self test: one warp waits, with the pipelines' bounded wait, on an mbarrier phase
+// that nothing completes. After timeout_ns the wait raises kErrTimeoutFull in the device error
+// word and the CTA abort flag and returns; out = {wait succeeded, abort flag}.
+__global__ void selftest_wait_kernel(unsigned long long timeout_ns, int* out) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncwarp();
+  int ok = 1;
+  if (threadIdx.x == 0) ok = mbar_wait_for(&bar, 0, &abort_flag, kErrTimeoutFull, timeout_ns) ? 1 : 0;
+  __syncwarp();
+  if (threadIdx.x == 0) {
+    out[0] = ok;
+    out[1] = abort_flag;
+  }
+}
+
+int anima_selftest_wait_timeout(anima_ctx* ctx, unsigned timeout_us, int* result) {
+  ANIMA_REQUIRE(ctx && result && timeout_us > 0 && timeout_us <= 2000000u,
+                "anima_selftest_wait_timeout: bad argument (timeout 1 us .. 2 s)");
+  int* d = nullptr;
+  ANIMA_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&d), 2 * sizeof(int), ctx->stream));
+  selftest_wait_kernel<<<1, 32, 0, ctx->stream>>>(1000ull * timeout_us, d);
+  int st = check_launch("selftest_wait_kernel");
+  if (!st) st = check_cuda(cudaMemcpyAsync(result, d, 2 * sizeof(int), cudaMemcpyDeviceToHost, ctx->stream),
+                           "anima_selftest_wait_timeout: copy");
+  cudaFreeAsync(d, ctx->stream);
+  if (!st) st = check_cuda(cudaStreamSynchronize(ctx->stream), "anima_selftest_wait_timeout: synchronize");
+  return st;
+}
+
 int anima_alloc(anima_ctx* ctx, size_t bytes, void** out) {
   ANIMA_REQUIRE(ctx && out, "anima_alloc: NULL argument");
   ANIMA_CUDA(cudaMallocAsync(out, bytes ? bytes : 16, ctx->stream));

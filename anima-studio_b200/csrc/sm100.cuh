@@ -88,21 +88,25 @@ __device__ __forceinline__ bool mbar_test_sleep(uint32_t bar, uint32_t parity) {
 }
 
 // Wait for the phase with `parity` to complete. Returns false (and raises the CTA abort flag and
-// the device error bit `err`) if that takes longer than kWaitTimeoutNs or another role aborted.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          unsigned err) {
+// the device error bit `err`) if that takes longer than timeout_ns or another role aborted.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, volatile int* abort_flag, unsigned err,
+                                              unsigned long long timeout_ns) {
   const uint32_t a = smem_u32(bar);
   if (mbar_test(a, parity)) return true;
   const unsigned long long t0 = globaltimer();
   for (;;) {
     if (mbar_test_sleep(a, parity)) return true;
     if (*abort_flag) return false;
-    if (globaltimer() - t0 > kWaitTimeoutNs) {
+    if (globaltimer() - t0 > timeout_ns) {
       flag_error(err);
       *abort_flag = 1;
       return false;
     }
   }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, unsigned err) {
+  return mbar_wait_for(bar, parity, abort_flag, err, kWaitTimeoutNs);
 }
 
 // ------------------------------------------------------------------ TMA (no multicast anywhere)

@@ -32,7 +32,7 @@ EXPORTS = [
     "anima_unpack_w4", "anima_linear", "anima_matmul", "anima_lora_down", "anima_layernorm_mod", "anima_layernorm_mod_quant",
     "anima_rotate", "anima_rotate_quant", "anima_act_rotate_quant", "anima_quant_rows", "anima_rmsnorm", "anima_qk_norm_rope", "anima_rope",
     "anima_attention", "anima_elementwise", "anima_zero", "anima_patchify", "anima_unpatchify",
-    "anima_timestep_embedding", "anima_euler_step", "anima_lincomb",
+    "anima_timestep_embedding", "anima_euler_step", "anima_lincomb", "anima_selftest_wait_timeout",
 ]
 
 
@@ -138,7 +138,7 @@ def check(status: int):
 # Entry points that enqueue one of this library's kernels (anima_zero is a memset).
 LAUNCHING = set(EXPORTS) - {"anima_ctx_create", "anima_ctx_destroy", "anima_ctx_set_stream", "anima_sync",
                             "anima_last_error", "anima_alloc", "anima_free", "anima_upload", "anima_download",
-                            "anima_profile_report", "anima_version", "anima_zero"}
+                            "anima_profile_report", "anima_version", "anima_zero", "anima_selftest_wait_timeout"}
 
 
 class KernelTimer:

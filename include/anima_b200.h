@@ -207,6 +207,13 @@ int anima_timestep_embedding(anima_ctx* ctx, const float* sigmas, int B, float* 
  * den_out may be NULL. */
 int anima_euler_step(anima_ctx* ctx, float* x, const float* v, const float* v_uncond, float cfg, float sigma,
                      float sigma_next, long long n, float* den_out);
+/* Diagnostic with no counterpart in the reference: runs one bounded wait (the same as the
+ * kernels' pipeline waits) on a barrier that is never released, so it gives up after timeout_us
+ * (1 us .. 2 s), records "data wait timed out" in the device error word and returns; the next
+ * anima_sync reports that error (ANIMA_ERR_DEVICE) and clears it, and the context stays usable.
+ * result[0] = 1 if the wait completed (it should not), result[1] = the kernel's abort flag.
+ * Exercises the failure path without a GPU fault. Synchronous. */
+int anima_selftest_wait_timeout(anima_ctx* ctx, unsigned timeout_us, int* result);
 /* The samplers' latent updates (samplers.js:104-218: axpby and the noise/derivative terms of
  * euler_a, dpmpp_2m and er_sde, and den = x - sigma v with CFG in pipeline.js:260-269):
  *   y[i] = c[0] x0[i] + c[1] x1[i] + c[2] x2[i] + c[3] x3[i] over n fp32 elements.
