@@ -433,7 +433,7 @@ def main():
     ap.add_argument("--act", default="gelu", help="kernel case mlp1: epilogue activation (gelu|none)")
     ap.add_argument("--out", default="f16", help="kernel case mlp1: output dtype (f16|f32)")
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=16)
+    ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="anima", choices=["anima", "reference"])
     ap.add_argument("--precision", default="a16", choices=["a16", "a8"])
