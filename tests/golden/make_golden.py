@@ -1,10 +1,10 @@
 """Generate the golden fixtures of tests/golden/ from the reference's own Python code.
 
 Runs only where the reference checkout exists (it imports tools/quant.py and tools/reference.py
-from REF, default /root/reference). Inputs come from the package's seeded synthetic generator, so
-the tests can rebuild identical inputs without the reference. Usage:
+from REF: --ref, or the ANIMA_REFERENCE environment variable). Inputs come from the package's
+seeded synthetic generator, so the tests can rebuild identical inputs without the reference. Usage:
 
-    python tests/golden/make_golden.py [--ref /path/to/anima-studio]
+    python tests/golden/make_golden.py --ref /path/to/anima-studio
 """
 
 from __future__ import annotations
@@ -74,8 +74,10 @@ class RefWeights:
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("ANIMA_REFERENCE"))
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("give the reference checkout with --ref or ANIMA_REFERENCE")
     quant, R = load_ref(args.ref)
     sys.path.insert(0, ROOT)
     syn = importlib.import_module("anima-studio_b200.synthetic")
