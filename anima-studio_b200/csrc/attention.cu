@@ -2,12 +2,13 @@
 // (Lq = Lk = 4096 at 1024^2) and cross-attention against cached text keys (Lk = 256..512). The
 // reference's counterpart is the fp32 WGSL flash kernel of app/gpu/kernels.js:147-299.
 //
-// One CTA = one (batch, head) and two 128-query tiles A and B; 576 threads:
+// A unit = one (batch, head) and two 128-query tiles A and B. A CTA runs one unit, or, under
+// stream-K (below), an equal share of all units' key blocks. 576 threads:
 //   warps 0-7   softmax for tile A, warps 8-15 for tile B. Warp w serves the 32 query rows of
 //               lane quadrant w % 4 (the tensor-memory lanes it may access) and the key columns
 //               [64 h, 64 h + 64) with h = (w / 4) % 2, so two warps on the same SM sub-partition
 //               share each row; they exchange the row maximum through shared memory.
-//   warp 16     TMA producer: Q_A, Q_B once, then K_j / V_j (128 keys) into two stages each
+//   warp 16     TMA producer: Q_A, Q_B per unit, then K_j / V_j (128 keys) into two stages each
 //   warp 17     TMEM allocator + single-thread UMMA issuer
 // Tensor memory (512 columns): S_A [0,128) S_B [128,256) O_A [256,384) O_B [384,512).
 // Per key block j the tensor core runs S_X = Q_X K_j^T (smem x smem), the softmax threads read S_X,
@@ -39,7 +40,9 @@ constexpr int OFF_V = OFF_K + 2 * TILE_BYTES;
 constexpr int OFF_BAR = OFF_V + 2 * TILE_BYTES;
 constexpr int OFF_RED = OFF_BAR + 256;                 // row max exchange [2 parity][2 tiles][2 halves][128]
 constexpr int OFF_RED_L = OFF_RED + 2 * 2 * 2 * 128 * 4;  // row sum exchange [2 tiles][2 halves][128]
-constexpr int SMEM_BYTES = OFF_RED_L + 2 * 2 * 128 * 4 + 1024;
+constexpr int OFF_SEG = OFF_RED_L + 2 * 2 * 128 * 4;   // this CTA's segments (int4 each)
+constexpr int MAX_SEGS = 64;
+constexpr int SMEM_BYTES = OFF_SEG + MAX_SEGS * 16 + 1024;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O when the max grows by > 2^8
 
 struct Params {
@@ -51,7 +54,10 @@ struct Params {
   const int* key_len;
   int kv_bcast;      // one K/V (and key_len) shared by every batch item
   float scale_log2;  // softmax scale * log2(e)
-  int pv_wait;       // issue S_x(j+1) only after PV_x(j) has completed
+  // stream-K: the units' key blocks split evenly over the CTAs (no key mask; every unit has ublk)
+  int stream_k, units, ublk;
+  float* ws;         // [units][PART_FLOATS] partial softmax states of split units
+  unsigned* flags;   // [units] tail part written (cleared by the head part)
 };
 
 __device__ __forceinline__ float ex2(float x) {
@@ -77,6 +83,77 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
+// A CTA's work is a list of segments: (unit, first key block, end key block), a unit being one
+// (batch, head, pair of query tiles). Without stream-K each CTA runs one whole unit. With stream-K
+// (long self-attention without a key mask) the units' key blocks are laid end to end and cut into
+// one equal range per CTA, so every SM gets the same number of key blocks instead of whole units
+// in ceil(units / SMs) waves. The range of CTA c reads: [tail of unit u] whole units... [head of
+// unit u']. A cut unit has exactly two parts (a range is at least one unit long): CTA c runs its
+// head part and writes the unnormalised O, running max and row sum to workspace slot c, then
+// raises one flag per softmax warp; CTA c + 1 runs the tail part LAST in its own range, waits for
+// those flags (CTA c, dispatched earlier, has finished its head part by then), merges the two
+// softmax states and writes the output. The roles of a CTA pass from one segment to the next
+// without a block-wide barrier: the producer reloads Q once the last QK^T of the previous segment
+// has completed (q_empty), and the first PV of a segment, issued after its P, finds O already read.
+struct Seg {
+  int unit, kb0, kb1, kind;
+};
+constexpr int kWhole = 0, kHeadPart = 1, kTailPart = 2;
+// workspace slot: O of both tiles as float4 [tile][half][16 column quads][128 rows], then the max
+// and the row sum [tile][half][128 rows] each
+constexpr int PART_FLOATS = 2 * TILE * HD + 2 * 2 * 2 * TILE;
+constexpr int PART_M = 2 * TILE * HD;
+constexpr int PART_L = PART_M + 2 * 2 * TILE;
+
+__device__ __forceinline__ Seg segment_at(const Params& p, long long g, long long end) {
+  Seg s;
+  s.unit = static_cast<int>(g / p.ublk);
+  const long long u0 = static_cast<long long>(s.unit) * p.ublk;
+  s.kb0 = static_cast<int>(g - u0);
+  s.kb1 = static_cast<int>((end < u0 + p.ublk ? end : u0 + p.ublk) - u0);
+  s.kind = s.kb0 > 0 ? kTailPart : (s.kb1 < p.ublk ? kHeadPart : kWhole);
+  return s;
+}
+
+// The segments of this CTA in the order it runs them (a leading tail part moved to the end),
+// written to shared memory by one thread; returns their count (at most MAX_SEGS, which the host
+// guarantees for stream-K launches). A whole unit's key blocks end at key_len (blocks entirely past
+// it are skipped).
+__device__ __forceinline__ int build_segments(const Params& p, int4* out) {
+  if (!p.stream_k) {
+    const int unit = blockIdx.x;
+    const int b = unit / p.q_pairs / p.heads;
+    const int kv_len = p.key_len ? min(p.Lk, p.key_len[p.kv_bcast ? 0 : b]) : p.Lk;
+    out[0] = make_int4(unit, 0, kv_len > 0 ? (kv_len + TILE - 1) / TILE : 0, kWhole);
+    return 1;
+  }
+  const long long total = static_cast<long long>(p.units) * p.ublk;
+  long long g = total * blockIdx.x / gridDim.x;
+  const long long end = total * (blockIdx.x + 1) / gridDim.x;
+  int n = 0;
+  const Seg first = segment_at(p, g, end);
+  const bool defer = first.kind == kTailPart;
+  if (defer) g = static_cast<long long>(first.unit) * p.ublk + first.kb1;
+  while (g < end && n < MAX_SEGS - 1) {
+    const Seg sg = segment_at(p, g, end);
+    out[n++] = make_int4(sg.unit, sg.kb0, sg.kb1, sg.kind);
+    g = static_cast<long long>(sg.unit) * p.ublk + sg.kb1;
+  }
+  if (g < end) flag_error(kErrBadArgs);  // more segments than MAX_SEGS: the host prevents this
+  if (defer) out[n++] = make_int4(first.unit, first.kb0, first.kb1, first.kind);
+  return n;
+}
+
+__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* q) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(q) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_u32(unsigned* q, unsigned v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(q), "r"(v) : "memory");
+}
+
 // 18 warps are allocated registers as 20: 96 x 32 x 20 = 61440 of the SM's 65536
 template <bool BF16>
 __global__ void __launch_bounds__(THREADS, 1)
@@ -94,22 +171,17 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* p_full = bars + 11;  // [2] per tile: P_X(j) written (8 warp arrivals)
   uint64_t* o_done = bars + 13;  // [2] per tile: PV_X(j) complete
   uint64_t* drain = bars + 15;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* q_empty = bars + 16;  // the segment's last QK^T has completed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* nseg_slot = reinterpret_cast<int*>(tmem_slot + 2);
+  int4* segs = reinterpret_cast<int4*>(smem + OFF_SEG);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qp = blockIdx.x % p.q_pairs;
-  const int bh = blockIdx.x / p.q_pairs;
-  const int h = bh % p.heads;
-  const int b = bh / p.heads;
-  const int q0 = qp * 2 * TILE;
-  const int kvb = p.kv_bcast ? 0 : b;
-  int kv_len = p.Lk;
-  if (p.key_len) kv_len = min(kv_len, p.key_len[kvb]);
-  const int nblk = kv_len > 0 ? (kv_len + TILE - 1) / TILE : 0;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&k_empty[i], 1);
@@ -121,6 +193,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
+    *nseg_slot = build_segments(p, segs);
     fence_mbar_init();
   }
   constexpr int kProducerWarp = SOFTMAX_WARPS, kMmaWarp = SOFTMAX_WARPS + 1;
@@ -132,40 +205,59 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  const int nseg = *nseg_slot;
 
   if (warp == kProducerWarp) {
-    if (lane == 0 && nblk > 0) {
+    if (lane == 0) {
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
-      const int qc = p.q_col + h * HD, kc = p.k_col + h * HD, vc = p.v_col + h * HD;
-      int armed[5] = {-1, -1, -1, -1, -1};  // parity of the last arm: q, k0, k1, v0, v1
-      mbar_arrive_expect_tx(q_full, 2 * TILE_BYTES);
-      tma_load_3d(smem + OFF_Q, &tm_q, q_full, qc, q0, b);
-      tma_load_3d(smem + OFF_Q + ATOM, &tm_q, q_full, qc + 64, q0, b);
-      tma_load_3d(smem + OFF_Q + TILE_BYTES, &tm_q, q_full, qc, q0 + TILE, b);
-      tma_load_3d(smem + OFF_Q + TILE_BYTES + ATOM, &tm_q, q_full, qc + 64, q0 + TILE, b);
-      armed[0] = 0;
-      for (int j = 0; j < nblk; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(&k_empty[st], ph ^ 1, abort_flag, kErrTimeoutEmpty)) break;
-        mbar_arrive_expect_tx(&k_full[st], TILE_BYTES);
-        tma_load_3d(smem + OFF_K + st * TILE_BYTES, &tm_k, &k_full[st], kc, j * TILE, kvb);
-        tma_load_3d(smem + OFF_K + st * TILE_BYTES + ATOM, &tm_k, &k_full[st], kc + 64, j * TILE, kvb);
-        armed[1 + st] = static_cast<int>(ph);
-        if (!mbar_wait(&v_empty[st], ph ^ 1, abort_flag, kErrTimeoutEmpty)) break;
-        mbar_arrive_expect_tx(&v_full[st], TILE_BYTES);
-        tma_load_3d(smem + OFF_V + st * TILE_BYTES, &tm_v, &v_full[st], vc, j * TILE, kvb);
-        tma_load_3d(smem + OFF_V + st * TILE_BYTES + ATOM, &tm_v, &v_full[st], vc + 64, j * TILE, kvb);
-        armed[3 + st] = static_cast<int>(ph);
+      // the last arm of q_full, k_full[0], k_full[1], v_full[0], v_full[1]: 2 bits each (armed, parity)
+      uint32_t armed = 0;
+      auto arm = [&](int i, uint32_t ph) { armed = (armed & ~(3u << (2 * i))) | ((2u | ph) << (2 * i)); };
+      int gb = 0, qn = 0;                   // key blocks and Q loads so far
+      for (int si = 0; si < nseg && !*abort_flag; ++si) {
+        const int4 sg = segs[si];  // unit, kb0, kb1, kind
+        const int qp = sg.x % p.q_pairs, bh = sg.x / p.q_pairs;
+        const int h = bh % p.heads, b = bh / p.heads;
+        const int kvb = p.kv_bcast ? 0 : b;
+        const int nb = sg.z - sg.y;
+        if (nb <= 0) continue;
+        const int q0 = qp * 2 * TILE;
+        const int qc = p.q_col + h * HD, kc = p.k_col + h * HD, vc = p.v_col + h * HD;
+        if (qn > 0 && !mbar_wait(q_empty, (qn - 1) & 1, abort_flag, kErrTimeoutEmpty)) break;
+        mbar_arrive_expect_tx(q_full, 2 * TILE_BYTES);
+        tma_load_3d(smem + OFF_Q, &tm_q, q_full, qc, q0, b);
+        tma_load_3d(smem + OFF_Q + ATOM, &tm_q, q_full, qc + 64, q0, b);
+        tma_load_3d(smem + OFF_Q + TILE_BYTES, &tm_q, q_full, qc, q0 + TILE, b);
+        tma_load_3d(smem + OFF_Q + TILE_BYTES + ATOM, &tm_q, q_full, qc + 64, q0 + TILE, b);
+        arm(0, qn & 1);
+        ++qn;
+        for (int j = 0; j < nb; ++j) {
+          const int G = gb + j, kb = sg.y + j;
+          const int st = G & 1;
+          const uint32_t ph = (G >> 1) & 1;
+          if (!mbar_wait(&k_empty[st], ph ^ 1, abort_flag, kErrTimeoutEmpty)) break;
+          mbar_arrive_expect_tx(&k_full[st], TILE_BYTES);
+          tma_load_3d(smem + OFF_K + st * TILE_BYTES, &tm_k, &k_full[st], kc, kb * TILE, kvb);
+          tma_load_3d(smem + OFF_K + st * TILE_BYTES + ATOM, &tm_k, &k_full[st], kc + 64, kb * TILE, kvb);
+          arm(1 + st, ph);
+          if (!mbar_wait(&v_empty[st], ph ^ 1, abort_flag, kErrTimeoutEmpty)) break;
+          mbar_arrive_expect_tx(&v_full[st], TILE_BYTES);
+          tma_load_3d(smem + OFF_V + st * TILE_BYTES, &tm_v, &v_full[st], vc, kb * TILE, kvb);
+          tma_load_3d(smem + OFF_V + st * TILE_BYTES + ATOM, &tm_v, &v_full[st], vc + 64, kb * TILE, kvb);
+          arm(3 + st, ph);
+        }
+        gb += nb;
       }
       if (*abort_flag) {
-        uint64_t* fb[5] = {q_full, &k_full[0], &k_full[1], &v_full[0], &v_full[1]};
+        // let every copy this thread started land before the CTA exits
         for (int i = 0; i < 5; ++i) {
-          if (armed[i] < 0) continue;
+          const uint32_t a = (armed >> (2 * i)) & 3u;
+          if (!(a & 2u)) continue;
+          uint64_t* fb = bars + (i < 3 ? i : i + 2);  // q_full, k_full[0..1], v_full[0..1]
           const unsigned long long t0 = globaltimer();
-          while (!mbar_test(smem_u32(fb[i]), static_cast<uint32_t>(armed[i]))) {
+          while (!mbar_test(smem_u32(fb), a & 1u)) {
             if (globaltimer() - t0 > kWaitTimeoutNs) {
               flag_error(kErrTimeoutDrain);
               break;
@@ -175,12 +267,12 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
     }
   } else if (warp == kMmaWarp) {
-    if (lane == 0 && nblk > 0) {
+    if (lane == 0) {
       const uint32_t id_qk = idesc_f16(TILE, TILE, BF16, false);
       const uint32_t id_pv = idesc_f16(TILE, HD, BF16, true);
       const uint32_t sq = smem_u32(smem + OFF_Q);
-      auto issue_s = [&](int x, int j) {  // S_x(j) = Q_x K_j^T
-        const uint32_t sk = smem_u32(smem + OFF_K + (j & 1) * TILE_BYTES);
+      auto issue_s = [&](int x, int G) {  // S_x = Q_x K^T for the block in stage G & 1
+        const uint32_t sk = smem_u32(smem + OFF_K + (G & 1) * TILE_BYTES);
         const uint32_t qx = sq + x * TILE_BYTES;
 #pragma unroll
         for (int k = 0; k < HD / 16; ++k) {
@@ -190,55 +282,65 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         umma_commit(&s_full[x]);
       };
-      auto issue_pv = [&](int x, int j) {  // O_x (+)= P_x(j) V_j, P from tensor memory
-        const uint32_t sv = smem_u32(smem + OFF_V + (j & 1) * TILE_BYTES);
+      auto issue_pv = [&](int x, int G, bool first) {  // O_x (+)= P_x V, P from tensor memory
+        const uint32_t sv = smem_u32(smem + OFF_V + (G & 1) * TILE_BYTES);
 #pragma unroll
         for (int k = 0; k < TILE / 16; ++k) {
           const uint64_t bd = sdesc_sw128(sv + k * 16 * 128, ATOM, 1024);
-          umma_f16_ts(tmem + 256 + x * 128, tmem + x * 128 + k * 8, bd, id_pv, (j > 0 || k > 0) ? 1u : 0u);
+          umma_f16_ts(tmem + 256 + x * 128, tmem + x * 128 + k * 8, bd, id_pv, (!first || k > 0) ? 1u : 0u);
         }
         umma_commit(&o_done[x]);
       };
-      bool ok = mbar_wait(q_full, 0, abort_flag, kErrTimeoutFull) &&
-                mbar_wait(&k_full[0], 0, abort_flag, kErrTimeoutFull);
-      if (ok) {
+      int gb = 0, qn = 0;
+      bool ok = true;
+      for (int si = 0; ok && si < nseg; ++si) {
+        const int nb = segs[si].z - segs[si].y;
+        if (nb <= 0) continue;
+        ok = mbar_wait(q_full, qn & 1, abort_flag, kErrTimeoutFull) &&
+             mbar_wait(&k_full[gb & 1], (gb >> 1) & 1, abort_flag, kErrTimeoutFull);
+        if (!ok) break;
+        ++qn;
+        // S(0) of this segment queues behind the previous segment's last PV on the tensor core
         tc_fence_after();
-        issue_s(0, 0);
-        issue_s(1, 0);
-        umma_commit(&k_empty[0]);
-      }
-      // Per tile: PV_x(j) as soon as P_x(j) is written, then (once PV_x(j) has read P_x(j), which
-      // lives in S_x's columns) S_x(j+1). The two tiles are serviced alternately, so one tile's
-      // softmax runs while the tensor core works on the other tile.
-      for (int j = 0; ok && j < nblk; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        const uint32_t jp = j & 1;
-        if (!mbar_wait(&v_full[st], ph, abort_flag, kErrTimeoutFull)) { ok = false; break; }
-        const bool more = j + 1 < nblk;
-        const int st1 = (j + 1) & 1;
-        for (int x = 0; x < 2; ++x) {
-          if (!mbar_wait(&p_full[x], jp, abort_flag, kErrTimeoutFull)) { ok = false; break; }
-          tc_fence_after();
-          issue_pv(x, j);
-          if (x == 1) umma_commit(&v_empty[st]);
-          if (more) {
-            if (x == 0 && !mbar_wait(&k_full[st1], ((j + 1) >> 1) & 1, abort_flag, kErrTimeoutFull)) {
-              ok = false;
-              break;
+        issue_s(0, gb);
+        issue_s(1, gb);
+        umma_commit(&k_empty[gb & 1]);
+        if (nb == 1) umma_commit(q_empty);
+        // Per tile: PV_x(j) as soon as P_x(j) is written, then S_x(j+1) into the same columns (the
+        // tensor core runs this thread's MMAs in issue order, so PV_x(j) has read P_x(j) first).
+        // The two tiles are serviced alternately: one tile's softmax overlaps the other's MMAs.
+        // P_x(0) is written after the softmax warps have read the previous segment's O_x, so the
+        // first PV (which overwrites O_x) comes after that read.
+        for (int j = 0; ok && j < nb; ++j) {
+          const int G = gb + j;
+          const int st = G & 1;
+          const uint32_t ph = (G >> 1) & 1;
+          const uint32_t jp = G & 1;
+          if (!mbar_wait(&v_full[st], ph, abort_flag, kErrTimeoutFull)) { ok = false; break; }
+          const bool more = j + 1 < nb;
+          const int st1 = (G + 1) & 1;
+          for (int x = 0; x < 2; ++x) {
+            if (!mbar_wait(&p_full[x], jp, abort_flag, kErrTimeoutFull)) { ok = false; break; }
+            tc_fence_after();
+            issue_pv(x, G, j == 0);
+            if (x == 1) umma_commit(&v_empty[st]);
+            if (more) {
+              if (x == 0 && !mbar_wait(&k_full[st1], ((G + 1) >> 1) & 1, abort_flag, kErrTimeoutFull)) {
+                ok = false;
+                break;
+              }
+              issue_s(x, G + 1);
+              if (x == 1) {
+                umma_commit(&k_empty[st1]);
+                if (j + 2 == nb) umma_commit(q_empty);
+              }
             }
-            // S_x(j+1) overwrites P_x(j): the tensor core runs this thread's MMAs in issue order,
-            // so PV_x(j) has read P_x(j) by then (pv_wait: wait for PV_x(j) explicitly instead)
-            if (p.pv_wait) {
-              if (!mbar_wait(&o_done[x], jp, abort_flag, kErrTimeoutAcc)) { ok = false; break; }
-              tc_fence_after();
-            }
-            issue_s(x, j + 1);
-            if (x == 1) umma_commit(&k_empty[st1]);
           }
         }
+        gb += nb;
       }
-      if (*abort_flag) {
+      if (!ok) {
+        // every MMA this thread issued completes before the CTA frees tensor memory
         umma_commit(drain);
         const unsigned long long t0 = globaltimer();
         while (!mbar_test(smem_u32(drain), 0)) {
@@ -259,165 +361,248 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t s_addr = tmem + lane_addr + x * 128 + 64 * hf;  // fp32 scores of this half
     const uint32_t p_addr = tmem + lane_addr + x * 128 + 32 * hf;  // its 64 probabilities, 2 per column
     const uint32_t o_addr = tmem + lane_addr + 256 + x * 128 + 64 * hf;
-    float* red = reinterpret_cast<float*>(smem + OFF_RED);  // [parity][tile][half][row]
-    const int bar_id = 1 + x * 4 + quad;                      // named barrier of the two warps of a row
+    float* red = reinterpret_cast<float*>(smem + OFF_RED);      // [parity][tile][half][row]
+    float* red_l = reinterpret_cast<float*>(smem + OFF_RED_L);  // [tile][half][row]
+    const int bar_id = 1 + x * 4 + quad;                        // named barrier of the two warps of a row
     auto pair_sync = [&]() { asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory"); };
-    float m_used = -INFINITY;  // max the probabilities (and O, l) are relative to
-    float l = 0.f;             // this half's share of the row sum
     bool ok = true;
-    // Every iteration meets pair_sync exactly once, also after a failed wait (the warp then skips
-    // the work), so the two warps of a row always agree on the barrier count.
-    for (int j = 0; j < nblk; ++j) {
-      const uint32_t jp = j & 1;
-      if (ok && !warp_wait(&s_full[x], jp, abort_flag, kErrTimeoutFull)) ok = false;
-      if (!ok) {
-        pair_sync();
+    int gb = 0;
+    for (int si = 0; si < nseg; ++si) {
+      const int kb0 = segs[si].y;
+      const int nb = segs[si].z - kb0;
+      // keys past kv_len get probability 0; only the last block of a unit can hold such keys
+      int kv_len = p.Lk;
+      if (p.key_len) kv_len = min(kv_len, p.key_len[p.kv_bcast ? 0 : segs[si].x / p.q_pairs / p.heads]);
+      // where this warp's output rows go (read again from shared memory after the key loop)
+      auto out_base = [&](int& qrow) {
+        const int unit = segs[si].x;
+        const int qp = unit % p.q_pairs, bh = unit / p.q_pairs;
+        const int h = bh % p.heads, b = bh / p.heads;
+        qrow = qp * 2 * TILE + x * TILE + row;
+        return static_cast<size_t>(b) * p.o_bstride + static_cast<size_t>(qrow) * p.ldo + static_cast<size_t>(h) * HD +
+               64 * hf;
+      };
+      if (nb <= 0) {
+        int qrow;
+        const size_t obase = out_base(qrow);
+        // no keys: zero rows (the softmax of an empty set is taken as 0)
+        if (qrow < p.Lq) {
+          const int esz = p.out_dtype == ANIMA_F32 ? 4 : 2;
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.out) + obase * esz);
+          for (int t = 0; t < 64 * esz / 16; ++t) dst[t] = make_uint4(0, 0, 0, 0);
+        }
         continue;
       }
-      tc_fence_after();
-      uint32_t sr[2][32];
-#pragma unroll
-      for (int c = 0; c < 2; ++c) tmem_ld32(s_addr + 32 * c, sr[c]);
-#pragma unroll
-      for (int c = 0; c < 2; ++c) tmem_ld_wait(sr[c]);
-      const int kbase = j * TILE + 64 * hf;
-      const bool masked = j * TILE + TILE > kv_len;  // only the last block can hold keys past kv_len
-      if (masked) {
-#pragma unroll
-        for (int c = 0; c < 2; ++c)
-#pragma unroll
-          for (int t = 0; t < 32; ++t)
-            if (kbase + 32 * c + t >= kv_len) sr[c][t] = __float_as_uint(-INFINITY);
-      }
-      float mx;
-      {  // four independent partial maxima, two new values per max
-        float pm[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) pm[i] = -INFINITY;
-#pragma unroll
-        for (int c = 0; c < 2; ++c)
-#pragma unroll
-          for (int t = 0; t < 32; t += 2)
-            pm[(t >> 1) & 3] = fmax3(pm[(t >> 1) & 3], __uint_as_float(sr[c][t]), __uint_as_float(sr[c][t + 1]));
-        mx = fmax3(fmaxf(pm[0], pm[1]), pm[2], pm[3]);
-      }
-      // the row maximum over both halves (double-buffered by block parity: the partner reads this
-      // block's value before it can reach the next block's barrier). The barrier also orders both
-      // warps' reads of S before either overwrites S's first 64 columns with P.
-      red[((jp * 2 + x) * 2 + hf) * 128 + row] = mx;
-      tc_fence_before();
-      pair_sync();
-      tc_fence_after();
-      mx = fmaxf(mx, red[((jp * 2 + x) * 2 + (hf ^ 1)) * 128 + row]) * p.scale_log2;
-      // lazy rescale: keep the old max unless the new one is more than 2^8 larger (both halves
-      // see the same maximum and take the same decision)
-      float alpha = 1.f;
-      bool rescale = false;
-      if (mx > m_used + kRescaleThreshold) {
-        rescale = j > 0;
-        alpha = (m_used == -INFINITY) ? 0.f : ex2(m_used - mx);
-        m_used = mx;
-      }
-      f2 rsp[2] = {dup2(0.f), dup2(0.f)};  // partial row sums
-      const f2 sc2 = dup2(p.scale_log2), nm2 = dup2(-m_used);
-      // P over the first 64 columns of S (two 16-bit probabilities per column), 32 keys at a time
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int t = 0; t < 32; t += 2) {
-          const f2 a = fma2(make_float2(__uint_as_float(sr[c][t]), __uint_as_float(sr[c][t + 1])), sc2, nm2);
-          float e0 = ex2(a.x), e1 = ex2(a.y);
-          if (masked) {  // -inf scores: exactly zero probability
-            if (kbase + 32 * c + t >= kv_len) e0 = 0.f;
-            if (kbase + 32 * c + t + 1 >= kv_len) e1 = 0.f;
-          }
-          rsp[(t >> 1) & 1] = add2(rsp[(t >> 1) & 1], make_float2(e0, e1));
-          pk[t / 2] = pack2<BF16>(e0, e1);
-        }
-        tmem_st16(p_addr + 16 * c, pk);
-      }
-      l = l * alpha + ((rsp[0].x + rsp[0].y) + (rsp[1].x + rsp[1].y));
-      if (rescale) {
-        // O holds sum_{i<j} P_i V_i relative to the old max: wait for PV(j-1), then scale in place
-        if (!warp_wait(&o_done[x], jp ^ 1, abort_flag, kErrTimeoutAcc)) {
-          ok = false;
+      float m_used = -INFINITY;  // max the probabilities (and O, l) are relative to
+      float l = 0.f;             // this half's share of the row sum
+      // Every iteration meets pair_sync exactly once, also after a failed wait (the warp then skips
+      // the work), so the two warps of a row always agree on the barrier count.
+      for (int j = 0; j < nb; ++j) {
+        const int G = gb + j;
+        const uint32_t jp = G & 1;
+        if (ok && !warp_wait(&s_full[x], jp, abort_flag, kErrTimeoutFull)) ok = false;
+        if (!ok) {
+          pair_sync();
           continue;
         }
         tc_fence_after();
+        uint32_t sr[2][32];
+#pragma unroll
+        for (int c = 0; c < 2; ++c) tmem_ld32(s_addr + 32 * c, sr[c]);
+#pragma unroll
+        for (int c = 0; c < 2; ++c) tmem_ld_wait(sr[c]);
+        const int kbase = (kb0 + j) * TILE + 64 * hf;
+        const bool masked = (kb0 + j) * TILE + TILE > kv_len;
+        if (masked) {
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+#pragma unroll
+            for (int t = 0; t < 32; ++t)
+              if (kbase + 32 * c + t >= kv_len) sr[c][t] = __float_as_uint(-INFINITY);
+        }
+        float mx;
+        {  // four independent partial maxima, two new values per max
+          float pm[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) pm[i] = -INFINITY;
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+#pragma unroll
+            for (int t = 0; t < 32; t += 2)
+              pm[(t >> 1) & 3] = fmax3(pm[(t >> 1) & 3], __uint_as_float(sr[c][t]), __uint_as_float(sr[c][t + 1]));
+          mx = fmax3(fmaxf(pm[0], pm[1]), pm[2], pm[3]);
+        }
+        // the row maximum over both halves (double-buffered by block parity: the partner reads this
+        // block's value before it can reach the next block's barrier). The barrier also orders both
+        // warps' reads of S before either overwrites S's first 64 columns with P.
+        red[((jp * 2 + x) * 2 + hf) * 128 + row] = mx;
+        tc_fence_before();
+        pair_sync();
+        tc_fence_after();
+        mx = fmaxf(mx, red[((jp * 2 + x) * 2 + (hf ^ 1)) * 128 + row]) * p.scale_log2;
+        // lazy rescale: keep the old max unless the new one is more than 2^8 larger (both halves
+        // see the same maximum and take the same decision)
+        float alpha = 1.f;
+        bool rescale = false;
+        if (mx > m_used + kRescaleThreshold) {
+          rescale = j > 0;
+          alpha = (m_used == -INFINITY) ? 0.f : ex2(m_used - mx);
+          m_used = mx;
+        }
+        f2 rsp[2] = {dup2(0.f), dup2(0.f)};  // partial row sums
+        const f2 sc2 = dup2(p.scale_log2), nm2 = dup2(-m_used);
+        // P over the first 64 columns of S (two 16-bit probabilities per column), 32 keys at a time
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int t = 0; t < 32; t += 2) {
+            const f2 a = fma2(make_float2(__uint_as_float(sr[c][t]), __uint_as_float(sr[c][t + 1])), sc2, nm2);
+            float e0 = ex2(a.x), e1 = ex2(a.y);
+            if (masked) {  // -inf scores: exactly zero probability
+              if (kbase + 32 * c + t >= kv_len) e0 = 0.f;
+              if (kbase + 32 * c + t + 1 >= kv_len) e1 = 0.f;
+            }
+            rsp[(t >> 1) & 1] = add2(rsp[(t >> 1) & 1], make_float2(e0, e1));
+            pk[t / 2] = pack2<BF16>(e0, e1);
+          }
+          tmem_st16(p_addr + 16 * c, pk);
+        }
+        l = l * alpha + ((rsp[0].x + rsp[0].y) + (rsp[1].x + rsp[1].y));
+        if (rescale) {
+          // O holds sum_{i<j} P_i V_i relative to the old max: wait for PV(j-1), then scale in place
+          if (!warp_wait(&o_done[x], jp ^ 1, abort_flag, kErrTimeoutAcc)) {
+            ok = false;
+            continue;
+          }
+          tc_fence_after();
+#pragma unroll 1
+          for (int c = 0; c < 2; ++c) {
+            uint32_t orr[32];
+            tmem_ld32(o_addr + 32 * c, orr);
+            tmem_ld_wait(orr);
+#pragma unroll
+            for (int t = 0; t < 32; ++t) orr[t] = __float_as_uint(__uint_as_float(orr[t]) * alpha);
+            tmem_st32(o_addr + 32 * c, orr);
+          }
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[x]);
+      }
+      gb += nb;
+      // the row sum over both halves (a warp that failed still takes part, releasing its partner).
+      // red_l is reused by the next segment only after both warps passed that segment's first
+      // pair_sync, which each reaches after reading red_l here.
+      red_l[(x * 2 + hf) * 128 + row] = l;
+      pair_sync();
+      const float l_row = l + red_l[(x * 2 + (hf ^ 1)) * 128 + row];
+      // the finished O (this half's 64 columns) once the last PV has landed
+      if (!ok || !warp_wait(&o_done[x], (gb - 1) & 1, abort_flag, kErrTimeoutAcc)) {
+        ok = false;
+        continue;
+      }
+      tc_fence_after();
+      const int kind = segs[si].w;
+      if (kind == kHeadPart) {
+        // unnormalised partial for the CTA that runs the unit's tail part
+        float* slot = p.ws + static_cast<size_t>(blockIdx.x) * PART_FLOATS;
+        float4* po = reinterpret_cast<float4*>(slot) + (x * 2 + hf) * 16 * TILE + row;
 #pragma unroll 1
         for (int c = 0; c < 2; ++c) {
           uint32_t orr[32];
           tmem_ld32(o_addr + 32 * c, orr);
           tmem_ld_wait(orr);
 #pragma unroll
-          for (int t = 0; t < 32; ++t) orr[t] = __float_as_uint(__uint_as_float(orr[t]) * alpha);
-          tmem_st32(o_addr + 32 * c, orr);
+          for (int t = 0; t < 8; ++t)
+            __stcg(po + (c * 8 + t) * TILE, make_float4(__uint_as_float(orr[4 * t]), __uint_as_float(orr[4 * t + 1]),
+                                                       __uint_as_float(orr[4 * t + 2]), __uint_as_float(orr[4 * t + 3])));
         }
+        __stcg(slot + PART_M + (x * 2 + hf) * TILE + row, m_used);
+        __stcg(slot + PART_L + (x * 2 + hf) * TILE + row, l_row);
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) st_release_u32(p.flags + blockIdx.x * SOFTMAX_WARPS + warp, 1u);
+        continue;
       }
-      tmem_st_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[x]);
-    }
-    // the row sum over both halves; a warp that failed still takes part so its partner is released
-    float* red_l = reinterpret_cast<float*>(smem + OFF_RED_L);
-    red_l[(x * 2 + hf) * 128 + row] = l;
-    pair_sync();
-    const float l_row = l + red_l[(x * 2 + (hf ^ 1)) * 128 + row];
-    // normalised output (this half's 64 columns) once the last PV has landed
-    if (ok && nblk > 0 && warp_wait(&o_done[x], (nblk - 1) & 1, abort_flag, kErrTimeoutAcc)) {
-      tc_fence_after();
-      const int qrow = q0 + x * TILE + row;
-      const float inv = l_row > 0.f ? 1.0f / l_row : 0.f;
-      const size_t base = static_cast<size_t>(b) * p.o_bstride + static_cast<size_t>(qrow) * p.ldo +
-                          static_cast<size_t>(h) * HD + 64 * hf;
+      float fa = 1.f, fb = 0.f, inv = l_row > 0.f ? 1.0f / l_row : 0.f;
+      const float4* pb = nullptr;
+      if (kind == kTailPart) {
+        // wait (bounded) for the head part's partial from the previous CTA, then merge
+        const float* slot = p.ws + static_cast<size_t>(blockIdx.x - 1) * PART_FLOATS;
+        unsigned* flag = p.flags + (blockIdx.x - 1) * SOFTMAX_WARPS + warp;
+        int got = 1;
+        if (lane == 0) {
+          const unsigned long long t0 = globaltimer();
+          while (ld_acquire_u32(flag) != 1u) {
+            if (*abort_flag) {
+              got = 0;
+              break;
+            }
+            if (globaltimer() - t0 > kWaitTimeoutNs) {
+              flag_error(kErrTimeoutAcc);
+              *abort_flag = 1;
+              got = 0;
+              break;
+            }
+            __nanosleep(256);
+          }
+          if (got) *reinterpret_cast<volatile unsigned*>(flag) = 0u;  // consumed: clear for the next launch
+        }
+        __syncwarp();
+        if (!__shfl_sync(0xffffffffu, got, 0)) {
+          ok = false;
+          continue;
+        }
+        const float mb = __ldcg(slot + PART_M + (x * 2 + hf) * TILE + row);
+        const float lb = __ldcg(slot + PART_L + (x * 2 + hf) * TILE + row);
+        const float m = fmaxf(m_used, mb);
+        fa = ex2(m_used - m);
+        fb = ex2(mb - m);
+        const float lt = l_row * fa + lb * fb;
+        inv = lt > 0.f ? 1.0f / lt : 0.f;
+        pb = reinterpret_cast<const float4*>(slot) + (x * 2 + hf) * 16 * TILE + row;
+      }
+      int qrow;
+      const size_t obase = out_base(qrow);
 #pragma unroll 1
       for (int c = 0; c < 2; ++c) {
         uint32_t orr[32];
         tmem_ld32(o_addr + 32 * c, orr);
         tmem_ld_wait(orr);
-        if (qrow < p.Lq) {
-          if (p.out_dtype == ANIMA_F32) {
-            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + base + 32 * c);
+        if (qrow >= p.Lq) continue;
+        float v[32];
 #pragma unroll
-            for (int t = 0; t < 8; ++t)
-              dst[t] = make_float4(__uint_as_float(orr[4 * t]) * inv, __uint_as_float(orr[4 * t + 1]) * inv,
-                                   __uint_as_float(orr[4 * t + 2]) * inv, __uint_as_float(orr[4 * t + 3]) * inv);
-          } else {
-            uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + base + 32 * c);
-            const bool obf = p.out_dtype == ANIMA_BF16;
+        for (int t = 0; t < 32; ++t) v[t] = __uint_as_float(orr[t]) * fa;
+        if (pb) {
 #pragma unroll
-            for (int t = 0; t < 4; ++t) {
-              float v[8];
-#pragma unroll
-              for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(orr[8 * t + e]) * inv;
-              uint4 u;
-              if (obf) {
-                u.x = pack2<true>(v[0], v[1]);
-                u.y = pack2<true>(v[2], v[3]);
-                u.z = pack2<true>(v[4], v[5]);
-                u.w = pack2<true>(v[6], v[7]);
-              } else {
-                u.x = pack2<false>(v[0], v[1]);
-                u.y = pack2<false>(v[2], v[3]);
-                u.z = pack2<false>(v[4], v[5]);
-                u.w = pack2<false>(v[6], v[7]);
-              }
-              dst[t] = u;
-            }
+          for (int t = 0; t < 8; ++t) {
+            const float4 o = __ldcg(pb + (c * 8 + t) * TILE);
+            v[4 * t] = fmaf(o.x, fb, v[4 * t]);
+            v[4 * t + 1] = fmaf(o.y, fb, v[4 * t + 1]);
+            v[4 * t + 2] = fmaf(o.z, fb, v[4 * t + 2]);
+            v[4 * t + 3] = fmaf(o.w, fb, v[4 * t + 3]);
           }
         }
-      }
-    } else if (nblk == 0) {
-      // no keys: zero rows (the softmax of an empty set is taken as 0)
-      const int qrow = q0 + x * TILE + row;
-      if (qrow < p.Lq) {
-        const size_t base = static_cast<size_t>(b) * p.o_bstride + static_cast<size_t>(qrow) * p.ldo +
-                            static_cast<size_t>(h) * HD + 64 * hf;
-        const int esz = p.out_dtype == ANIMA_F32 ? 4 : 2;
-        uint4* dst = reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.out) + base * esz);
-        for (int t = 0; t < 64 * esz / 16; ++t) dst[t] = make_uint4(0, 0, 0, 0);
+        if (p.out_dtype == ANIMA_F32) {
+          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + obase + 32 * c);
+#pragma unroll
+          for (int t = 0; t < 8; ++t)
+            dst[t] = make_float4(v[4 * t] * inv, v[4 * t + 1] * inv, v[4 * t + 2] * inv, v[4 * t + 3] * inv);
+        } else {
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + obase + 32 * c);
+          const bool obf = p.out_dtype == ANIMA_BF16;
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            uint32_t w[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              w[e] = obf ? pack2<true>(v[8 * t + 2 * e] * inv, v[8 * t + 2 * e + 1] * inv)
+                         : pack2<false>(v[8 * t + 2 * e] * inv, v[8 * t + 2 * e + 1] * inv);
+            dst[t] = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+        }
       }
     }
   }
@@ -427,6 +612,42 @@ __global__ void __launch_bounds__(THREADS, 1)
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
+}
+
+
+// Stream-K pays when whole units leave the last wave of CTAs far from full. Legal without a key
+// mask (every unit has the same key blocks) and with at least one unit per SM (a unit is then cut
+// into two parts at most); chosen (mode -1) when the last wave would leave more than 5% of the
+// SMs idle and units are long enough (>= 16 key blocks) to hide the cost of a cut: each segment
+// reloads Q and refills the pipeline, and a cut unit writes and reads back a 130 KB partial.
+// (Cross-attention over 512 keys, 4 blocks per unit, measured slower with it.)
+bool use_stream_k(const anima_ctx* ctx, const anima_attention_args* a, long long units, int ublk) {
+  const int mode = ctx->attn_split;
+  const int sms = ctx->num_sms;
+  // a CTA then runs at most units / sms + 3 segments
+  if (mode == 0 || a->key_len || units < sms || units > static_cast<long long>(MAX_SEGS - 4) * sms || ublk < 1)
+    return false;
+  if (mode == 1) return true;
+  const long long waves = (units + sms - 1) / sms;
+  return ublk >= 16 && units % sms != 0 && static_cast<double>(units) / static_cast<double>(waves * sms) < 0.95;
+}
+
+// One workspace slot per CTA (a CTA writes at most one partial) and one flag per softmax warp of
+// each slot, allocated once per context (its size depends only on the SM count) and zeroed; the
+// kernel leaves every flag at zero again. Allocation happens outside stream capture only: a graph
+// captured later keeps these pointers, which live as long as the context.
+int stream_k_scratch(anima_ctx* ctx) {
+  if (ctx->attn_ws) return ANIMA_OK;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  ANIMA_CUDA(cudaStreamIsCapturing(ctx->stream, &cap));
+  ANIMA_REQUIRE(cap == cudaStreamCaptureStatusNone,
+                "anima_attention: first stream-K call inside stream capture (run once before capturing)");
+  const size_t ws_bytes = static_cast<size_t>(ctx->num_sms) * PART_FLOATS * sizeof(float);
+  const size_t flag_bytes = static_cast<size_t>(ctx->num_sms) * SOFTMAX_WARPS * sizeof(unsigned);
+  ANIMA_CUDA(cudaMalloc(&ctx->attn_ws, ws_bytes));
+  ANIMA_CUDA(cudaMalloc(&ctx->attn_flags, flag_bytes));
+  ANIMA_CUDA(cudaMemset(ctx->attn_flags, 0, flag_bytes));
+  return ANIMA_OK;
 }
 
 }  // namespace attn
@@ -500,14 +721,20 @@ extern "C" int anima_attention(anima_ctx* ctx, const anima_attention_args* a) {
   p.kv_bcast = kv_bcast ? 1 : 0;
   const float scale = a->scale > 0.f ? a->scale : 1.0f / sqrtf(static_cast<float>(a->head_dim));
   p.scale_log2 = scale * 1.4426950408889634f;
-  static const int pv_wait = [] {
-    const char* e = getenv("ANIMA_ATTN_PV_WAIT");
-    return e && atoi(e) != 0 ? 1 : 0;
-  }();
-  p.pv_wait = pv_wait;
 
-  const long long grid = static_cast<long long>(p.q_pairs) * a->heads * a->batch;
-  ANIMA_REQUIRE(grid < (1LL << 31), "anima_attention: problem too large");
+  const long long units = static_cast<long long>(p.q_pairs) * a->heads * a->batch;
+  ANIMA_REQUIRE(units < (1LL << 31), "anima_attention: problem too large");
+  p.units = static_cast<int>(units);
+  p.ublk = (a->Lk + attn::TILE - 1) / attn::TILE;
+  long long grid = units;
+  if (attn::use_stream_k(ctx, a, units, p.ublk)) {
+    int st = attn::stream_k_scratch(ctx);
+    if (st) return st;
+    p.stream_k = 1;
+    p.ws = ctx->attn_ws;
+    p.flags = ctx->attn_flags;
+    grid = ctx->num_sms;
+  }
   ProfScope prof(ctx, "attn.flash", 4.0 * a->batch * a->heads * static_cast<double>(a->Lq) * a->Lk * a->head_dim, 0);
   using Kfn = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const attn::Params);
   const int kind = a->dtype == ANIMA_BF16 ? 1 : 0;

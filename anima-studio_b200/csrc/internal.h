@@ -16,6 +16,9 @@ struct anima_ctx {
   int num_sms = 148;
   bool profile = false;
   void* prof = nullptr;  // ProfileState* (runtime.cu)
+  float* attn_ws = nullptr;         // stream-K attention partials (attention.cu)
+  unsigned* attn_flags = nullptr;   // their ready flags, zero between launches
+  int attn_split = -1;              // anima_ctx_set_attention_split mode
 };
 
 namespace anima {

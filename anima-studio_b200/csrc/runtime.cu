@@ -151,6 +151,8 @@ int anima_ctx_create(int device, anima_ctx** out) {
   auto* c = new anima_ctx();
   c->device = device;
   c->num_sms = prop.multiProcessorCount;
+  const char* split = getenv("ANIMA_ATTN_STREAMK");
+  if (split && split[0]) c->attn_split = atoi(split) != 0 ? 1 : 0;
   const char* p = getenv("ANIMA_PROFILE");
   c->profile = p && p[0] == '1';
   if (c->profile) c->prof = new ProfileState();
@@ -164,6 +166,8 @@ int anima_ctx_destroy(anima_ctx* ctx) {
     prof_collect(ctx);
     delete static_cast<ProfileState*>(ctx->prof);
   }
+  if (ctx->attn_ws) cudaFree(ctx->attn_ws);
+  if (ctx->attn_flags) cudaFree(ctx->attn_flags);
   delete ctx;
   return ANIMA_OK;
 }
@@ -174,6 +178,13 @@ int anima_ctx_set_stream(anima_ctx* ctx, void* stream) {
   return ANIMA_OK;
 }
 
+int anima_ctx_set_attention_split(anima_ctx* ctx, int mode) {
+  ANIMA_REQUIRE(ctx, "anima_ctx_set_attention_split: ctx is NULL");
+  ANIMA_REQUIRE(mode >= -1 && mode <= 1, "anima_ctx_set_attention_split: mode %d (-1, 0 or 1)", mode);
+  ctx->attn_split = mode;
+  return ANIMA_OK;
+}
+
 int anima_sync(anima_ctx* ctx) {
   ANIMA_REQUIRE(ctx, "anima_sync: ctx is NULL");
   ANIMA_CUDA(cudaStreamSynchronize(ctx->stream));
@@ -181,6 +192,9 @@ int anima_sync(anima_ctx* ctx) {
   ANIMA_CUDA(cudaMemcpyFromSymbol(&err, g_device_error, sizeof(err)));
   if (err) {
     ANIMA_CUDA(cudaMemcpyToSymbol(g_device_error, &zero, sizeof(zero)));
+    // an aborted stream-K attention can leave a partial's ready flag raised
+    if (ctx->attn_flags)
+      ANIMA_CUDA(cudaMemset(ctx->attn_flags, 0, static_cast<size_t>(ctx->num_sms) * 16 * sizeof(unsigned)));
     return set_error(ANIMA_ERR_DEVICE, "device error flags 0x%x (%s%s%s%s%s)", err,
                      (err & kErrTimeoutFull) ? "data wait timed out; " : "",
                      (err & kErrTimeoutEmpty) ? "stage wait timed out; " : "",

@@ -33,6 +33,7 @@ EXPORTS = [
     "anima_rotate", "anima_rotate_quant", "anima_act_rotate_quant", "anima_quant_rows", "anima_rmsnorm", "anima_qk_norm_rope", "anima_rope",
     "anima_attention", "anima_elementwise", "anima_zero", "anima_patchify", "anima_unpatchify",
     "anima_timestep_embedding", "anima_euler_step", "anima_lincomb", "anima_selftest_wait_timeout",
+    "anima_ctx_set_attention_split",
 ]
 
 
@@ -91,7 +92,7 @@ def load_library(path: str = LIB_PATH):
         vp, i, f, ll, sz = C.c_void_p, C.c_int, C.c_float, C.c_longlong, C.c_size_t
         sig = {
             "anima_ctx_create": [i, C.POINTER(vp)], "anima_ctx_destroy": [vp], "anima_ctx_set_stream": [vp, vp],
-            "anima_sync": [vp], "anima_alloc": [vp, sz, C.POINTER(vp)], "anima_free": [vp, vp],
+            "anima_sync": [vp], "anima_ctx_set_attention_split": [vp, i], "anima_alloc": [vp, sz, C.POINTER(vp)], "anima_free": [vp, vp],
             "anima_upload": [vp, vp, vp, sz], "anima_download": [vp, vp, vp, sz],
             "anima_profile_report": [vp, C.c_char_p, sz], "anima_version": [],
             "anima_unpack_w4": [vp, vp, vp, vp, i, i, vp],
@@ -138,7 +139,8 @@ def check(status: int):
 # Entry points that enqueue one of this library's kernels (anima_zero is a memset).
 LAUNCHING = set(EXPORTS) - {"anima_ctx_create", "anima_ctx_destroy", "anima_ctx_set_stream", "anima_sync",
                             "anima_last_error", "anima_alloc", "anima_free", "anima_upload", "anima_download",
-                            "anima_profile_report", "anima_version", "anima_zero", "anima_selftest_wait_timeout"}
+                            "anima_profile_report", "anima_version", "anima_zero", "anima_selftest_wait_timeout",
+                            "anima_ctx_set_attention_split"}
 
 
 class KernelTimer:
@@ -194,6 +196,10 @@ class Context:
         if ctx is None:
             ctx = cls._per_device[device] = Context(device)
         return ctx
+
+    def set_attention_split(self, mode: int):
+        """-1 automatic stream-K for attention, 0 whole units only, 1 stream-K wherever legal."""
+        check(self.lib.anima_ctx_set_attention_split(self.h, int(mode)))
 
     def bind_stream(self):
         check(self.lib.anima_ctx_set_stream(self.h, C.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)))

@@ -123,6 +123,12 @@ int anima_ctx_create(int device, anima_ctx** out);
 int anima_ctx_destroy(anima_ctx* ctx);
 /* Run subsequent calls on this CUDA stream (cudaStream_t; NULL = legacy default stream). */
 int anima_ctx_set_stream(anima_ctx* ctx, void* stream);
+/* How anima_attention spreads work over the SMs (no reference counterpart: the reference's WGSL
+ * dispatch has no such choice). -1 (default, or the ANIMA_ATTN_STREAMK environment variable at
+ * context creation): stream-K split of the key blocks when the last wave of whole units would leave
+ * more than 5% of the SMs idle; 0: whole units only; 1: stream-K wherever legal (no key_len, at
+ * least one unit per SM). Results of the two schedules differ by fp32 rounding only. */
+int anima_ctx_set_attention_split(anima_ctx* ctx, int mode);
 /* gpu.sync (device.js:218-232): wait for the stream, then report device-side errors. */
 int anima_sync(anima_ctx* ctx);
 const char* anima_last_error(void);

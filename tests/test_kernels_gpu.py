@@ -419,3 +419,76 @@ def test_device_errors_surface_at_sync(ops):
     x = randn((4, 2048), 46).to(DEV)
     ops.rotate(x)
     ctx.sync()
+
+
+# ----------------------------------------------------------------------------- stream-K attention
+
+def _self_attn(ops, qkv, L, H, batch=1, bstride=None):
+    return ops.attention(qkv, qkv, qkv, Lq=L, Lk=L, H=H, ldq=3 * H * 128, ldk=3 * H * 128, ldv=3 * H * 128,
+                         q_off=0, k_off=H * 128, v_off=2 * H * 128, batch=batch, q_bstride=bstride or 0,
+                         k_bstride=bstride or 0, v_bstride=bstride or 0, out_dtype=torch.float32)
+
+
+def _split(mode):
+    pkg("device").Context.get(0).set_attention_split(mode)
+
+
+@pytest.fixture
+def split_mode():
+    yield _split
+    _split(-1)
+
+
+@pytest.mark.parametrize("L,H,batch", [(4096, 16, 1), (4000, 16, 1), (2048, 24, 2), (1536, 64, 1)])
+def test_stream_k_attention_matches_whole_units(ops, split_mode, L, H, batch):
+    """The key blocks of all units split evenly over the SMs (a unit cut into a head part and a tail
+    part, merged through the workspace) give the whole-unit result up to rounding: each part keeps
+    its own running max, so its 16-bit probabilities round differently. Checked against the oracle
+    on two heads."""
+    D = 3 * H * 128
+    qkv = randn((batch * L, D), 60 + L + H).to(torch.bfloat16).to(DEV)
+    split_mode(0)
+    whole = _self_attn(ops, qkv, L, H, batch, L * D if batch > 1 else None).cpu().numpy()
+    split_mode(1)
+    sk = _self_attn(ops, qkv, L, H, batch, L * D if batch > 1 else None).cpu().numpy()
+    assert rel_l2(sk, whole) < 2e-3
+    c = qkv[:L].cpu()
+    for h in (0, H - 1):
+        q = c[:, h * 128:(h + 1) * 128][None]
+        k = c[:, H * 128 + h * 128:H * 128 + (h + 1) * 128][None]
+        v = c[:, 2 * H * 128 + h * 128:2 * H * 128 + (h + 1) * 128][None]
+        ref = attn_ref(q, k, v)[0]
+        assert rel_l2(sk[:L, h * 128:(h + 1) * 128], ref) < 6e-3, h
+
+
+def test_stream_k_attention_consecutive_calls(ops, split_mode):
+    """Two stream-K calls on different inputs: the second must not merge partials or flags left by the
+    first (every flag is cleared by the CTA that consumes it), and repeating a call is bit-exact."""
+    L, H = 4096, 16
+    a = randn((L, 6144), 70).to(torch.bfloat16).to(DEV)
+    b = randn((L, 6144), 71).to(torch.bfloat16).to(DEV)
+    split_mode(0)
+    ref_b = _self_attn(ops, b, L, H).cpu().numpy()
+    split_mode(1)
+    _self_attn(ops, a, L, H)
+    out_b1 = _self_attn(ops, b, L, H).cpu().numpy()
+    out_b2 = _self_attn(ops, b, L, H).cpu().numpy()
+    assert np.array_equal(out_b1, out_b2)
+    assert rel_l2(out_b1, ref_b) < 2e-3  # a merge with the first call's partials would be O(1) off
+
+
+def test_stream_k_not_used_with_key_mask(ops, split_mode):
+    """With key_len the units differ in length: the whole-unit schedule runs even when forced."""
+    B, H, Lq, Lk = 1, 16, 4096, 512
+    q = randn((Lq, 2048), 72).to(torch.bfloat16)
+    k = randn((Lk, 2048), 73).to(torch.bfloat16)
+    v = randn((Lk, 2048), 74).to(torch.bfloat16)
+    kl = torch.tensor([300], dtype=torch.int32)
+    split_mode(1)
+    out = ops.attention(q.to(DEV), k.to(DEV), v.to(DEV), Lq=Lq, Lk=Lk, H=H, key_len=kl.to(DEV),
+                        out_dtype=torch.float32).cpu().numpy()
+    qb = q.reshape(Lq, H, 128).transpose(0, 1)[:2]
+    kb = k.reshape(Lk, H, 128).transpose(0, 1)[:2]
+    vb = v.reshape(Lk, H, 128).transpose(0, 1)[:2]
+    ref = attn_ref(qb, kb, vb, 300).transpose(1, 0, 2).reshape(Lq, 256)
+    assert rel_l2(out[:, :256], ref) < 6e-3
