@@ -650,12 +650,43 @@ int stream_k_scratch(anima_ctx* ctx) {
   return ANIMA_OK;
 }
 
+// Static workspace of anima_attention_noalloc: the flags of up to kStaticMaxSms CTAs, then one
+// partial slot per CTA (21.6 MB in the module's device data). Calls that use it must not overlap
+// (same device, any context or stream): they would share flags and slots.
+constexpr int kStaticMaxSms = 160;
+constexpr size_t kStaticFlagBytes = static_cast<size_t>(kStaticMaxSms) * SOFTMAX_WARPS * sizeof(unsigned);
+constexpr size_t kStaticScratchBytes =
+    kStaticFlagBytes + static_cast<size_t>(kStaticMaxSms) * PART_FLOATS * sizeof(float);
+static_assert(kStaticFlagBytes % 256 == 0, "partial slots stay 256-byte aligned");
+static __device__ __align__(256) unsigned char g_attn_static_ws[kStaticScratchBytes];
+
+// The static workspace's address (cudaGetSymbolAddress, once per context). The flags must start at
+// zero: the first call clears them with a memset on the context's stream (nothing is allocated);
+// every launch leaves them at zero again, and anima_sync clears them after a device error.
+int static_scratch(anima_ctx* ctx) {
+  ANIMA_REQUIRE(ctx->num_sms <= kStaticMaxSms,
+                "anima_attention_noalloc: stream-K needs %d workspace slots (one per SM), the static workspace "
+                "holds %d",
+                ctx->num_sms, kStaticMaxSms);
+  if (ctx->attn_static_ws) return ANIMA_OK;
+  void* base = nullptr;
+  ANIMA_CUDA(cudaGetSymbolAddress(&base, g_attn_static_ws));
+  ANIMA_REQUIRE(base != nullptr, "anima_attention_noalloc: no address for the static workspace");
+  ANIMA_CUDA(cudaMemsetAsync(base, 0, kStaticFlagBytes, ctx->stream));
+  ctx->attn_static_ws = base;
+  return ANIMA_OK;
+}
+
 }  // namespace attn
 }  // namespace anima
 
 using namespace anima;
 
-extern "C" int anima_attention(anima_ctx* ctx, const anima_attention_args* a) {
+namespace {
+
+// static_ws: the stream-K workspace comes from the module's static device array (no allocation)
+// instead of the context's lazily allocated one.
+int attention_launch(anima_ctx* ctx, const anima_attention_args* a, bool static_ws) {
   ANIMA_REQUIRE(ctx && a, "anima_attention: NULL argument");
   ANIMA_REQUIRE(a->head_dim == attn::HD, "anima_attention: head_dim %d (only 128)", a->head_dim);
   ANIMA_REQUIRE(a->dtype == ANIMA_BF16 || a->dtype == ANIMA_F16, "anima_attention: q/k/v dtype must be bf16 or f16");
@@ -728,14 +759,23 @@ extern "C" int anima_attention(anima_ctx* ctx, const anima_attention_args* a) {
   p.ublk = (a->Lk + attn::TILE - 1) / attn::TILE;
   long long grid = units;
   if (attn::use_stream_k(ctx, a, units, p.ublk)) {
-    int st = attn::stream_k_scratch(ctx);
-    if (st) return st;
+    if (static_ws) {
+      int st = attn::static_scratch(ctx);
+      if (st) return st;
+      p.flags = static_cast<unsigned*>(ctx->attn_static_ws);
+      p.ws = reinterpret_cast<float*>(static_cast<unsigned char*>(ctx->attn_static_ws) + attn::kStaticFlagBytes);
+    } else {
+      int st = attn::stream_k_scratch(ctx);
+      if (st) return st;
+      p.ws = ctx->attn_ws;
+      p.flags = ctx->attn_flags;
+    }
     p.stream_k = 1;
-    p.ws = ctx->attn_ws;
-    p.flags = ctx->attn_flags;
     grid = ctx->num_sms;
   }
-  ProfScope prof(ctx, "attn.flash", 4.0 * a->batch * a->heads * static_cast<double>(a->Lq) * a->Lk * a->head_dim, 0);
+  // (profiling events are created only on the allocating entry point)
+  ProfScope prof(static_ws ? nullptr : ctx, "attn.flash",
+                 4.0 * a->batch * a->heads * static_cast<double>(a->Lq) * a->Lk * a->head_dim, 0);
   using Kfn = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const attn::Params);
   const int kind = a->dtype == ANIMA_BF16 ? 1 : 0;
   const Kfn fns[2] = {attn::attention_kernel<false>, attn::attention_kernel<true>};
@@ -747,4 +787,14 @@ extern "C" int anima_attention(anima_ctx* ctx, const anima_attention_args* a) {
   }
   fn<<<static_cast<int>(grid), attn::THREADS, attn::SMEM_BYTES, ctx->stream>>>(tq, tk, tv, p);
   return check_launch("attention_kernel");
+}
+
+}  // namespace
+
+extern "C" int anima_attention(anima_ctx* ctx, const anima_attention_args* a) {
+  return attention_launch(ctx, a, false);
+}
+
+extern "C" int anima_attention_noalloc(anima_ctx* ctx, const anima_attention_args* a) {
+  return attention_launch(ctx, a, true);
 }

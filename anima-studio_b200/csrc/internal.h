@@ -19,6 +19,7 @@ struct anima_ctx {
   float* attn_ws = nullptr;         // stream-K attention partials (attention.cu)
   unsigned* attn_flags = nullptr;   // their ready flags, zero between launches
   int attn_split = -1;              // anima_ctx_set_attention_split mode
+  void* attn_static_ws = nullptr;   // static workspace of anima_attention_noalloc (flags first)
 };
 
 namespace anima {

@@ -195,6 +195,8 @@ int anima_sync(anima_ctx* ctx) {
     // an aborted stream-K attention can leave a partial's ready flag raised
     if (ctx->attn_flags)
       ANIMA_CUDA(cudaMemset(ctx->attn_flags, 0, static_cast<size_t>(ctx->num_sms) * 16 * sizeof(unsigned)));
+    if (ctx->attn_static_ws)
+      ANIMA_CUDA(cudaMemset(ctx->attn_static_ws, 0, static_cast<size_t>(ctx->num_sms) * 16 * sizeof(unsigned)));
     return set_error(ANIMA_ERR_DEVICE, "device error flags 0x%x (%s%s%s%s%s)", err,
                      (err & kErrTimeoutFull) ? "data wait timed out; " : "",
                      (err & kErrTimeoutEmpty) ? "stage wait timed out; " : "",

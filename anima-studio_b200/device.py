@@ -31,7 +31,7 @@ EXPORTS = [
     "anima_alloc", "anima_free", "anima_upload", "anima_download", "anima_profile_report", "anima_version",
     "anima_unpack_w4", "anima_linear", "anima_matmul", "anima_lora_down", "anima_layernorm_mod", "anima_layernorm_mod_quant",
     "anima_rotate", "anima_rotate_quant", "anima_act_rotate_quant", "anima_quant_rows", "anima_rmsnorm", "anima_qk_norm_rope", "anima_rope",
-    "anima_attention", "anima_elementwise", "anima_zero", "anima_patchify", "anima_unpatchify",
+    "anima_attention", "anima_attention_noalloc", "anima_elementwise", "anima_zero", "anima_patchify", "anima_unpatchify",
     "anima_timestep_embedding", "anima_euler_step", "anima_lincomb", "anima_selftest_wait_timeout",
     "anima_ctx_set_attention_split",
 ]
@@ -109,6 +109,7 @@ def load_library(path: str = LIB_PATH):
             "anima_qk_norm_rope": [vp, vp, i, i, i, i, i, vp, vp, vp, i, f],
             "anima_rope": [vp, vp, i, i, i, i, i, i, vp, i],
             "anima_attention": [vp, C.POINTER(AttentionArgs)],
+            "anima_attention_noalloc": [vp, C.POINTER(AttentionArgs)],
             "anima_elementwise": [vp, i, vp, vp, vp, ll], "anima_zero": [vp, vp, sz],
             "anima_patchify": [vp, vp, i, i, i, vp], "anima_unpatchify": [vp, vp, i, i, i, vp],
             "anima_timestep_embedding": [vp, vp, i, vp],

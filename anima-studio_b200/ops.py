@@ -237,10 +237,11 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, Lq: int, Lk:
               k_off: int = 0, v_off: int = 0, batch: int = 1, q_bstride: int = 0, k_bstride: int = 0,
               v_bstride: int = 0, key_len: torch.Tensor | None = None, out: torch.Tensor | None = None,
               out_dtype=None, o_bstride: int | None = None, scale: float | None = None,
-              name: str | None = None) -> torch.Tensor:
+              name: str | None = None, noalloc: bool = False) -> torch.Tensor:
     """Non-causal multi-head attention (ops.js:166-208): q [.., ldq] with head h at q_off + h D,
     k/v likewise; output [batch * Lq, H D]. q/k/v are bf16 or fp16; key_len (int32 [batch]) masks
-    keys past each item's text length."""
+    keys past each item's text length. noalloc: the entry point whose stream-K workspace is the
+    library's static device array (no allocation; calls must not overlap)."""
     ldq = ldq or H * D
     ldk = ldk or H * D
     ldv = ldv or H * D
@@ -257,7 +258,8 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, Lq: int, Lk:
     a.out_dtype = _dt(out)
     a.key_len = key_len.data_ptr() if key_len is not None else 0
     a.scale = scale if scale is not None else 1.0 / math.sqrt(D)
-    ctx_for(q).call("anima_attention", C.byref(a), tag=name, work=4.0 * batch * Lq * Lk * D * H)
+    ctx_for(q).call("anima_attention_noalloc" if noalloc else "anima_attention", C.byref(a), tag=name,
+                    work=4.0 * batch * Lq * Lk * D * H)
     return out
 
 
