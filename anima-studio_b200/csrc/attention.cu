@@ -77,10 +77,36 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
   }
 }
 
+// One arrival for the warp, from one elected lane (predicated, no branch).
+__device__ __forceinline__ void arrive_one_lane(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "@p mbarrier.arrive.shared::cta.b64 _, [%0];\n\t}\n" ::"r"(smem_u32(bar))
+      : "memory");
+}
+
+// Warp-wide bounded wait: every lane polls, so the common case (phase already complete) has no
+// divergent branch; the result is the AND over the lanes.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, unsigned err) {
-  int ok = 1;
-  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort_flag, err) ? 1 : 0;
-  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+  const uint32_t a = smem_u32(bar);
+  if (__all_sync(0xffffffffu, mbar_test(a, parity))) return true;
+  // spin without the suspend hint: the wait is on the critical path
+  bool ok = true;
+  const unsigned long long t0 = globaltimer();
+  while (!mbar_test(a, parity)) {
+    if (*abort_flag) {
+      ok = false;
+      break;
+    }
+    if (globaltimer() - t0 > kWaitTimeoutNs) {
+      flag_error(err);
+      *abort_flag = 1;
+      ok = false;
+      break;
+    }
+  }
+  return __all_sync(0xffffffffu, ok);
 }
 
 // A CTA's work is a list of segments: (unit, first key block, end key block), a unit being one
@@ -440,14 +466,16 @@ __global__ void __launch_bounds__(THREADS, 1)
         pair_sync();
         tc_fence_after();
         mx = fmaxf(mx, red[((jp * 2 + x) * 2 + (hf ^ 1)) * 128 + row]) * p.scale_log2;
-        // lazy rescale: keep the old max unless the new one is more than 2^8 larger (both halves
-        // see the same maximum and take the same decision)
+        // lazy rescale: keep the old max unless the new one is more than 2^8 larger for some row of
+        // the warp; then every row of the warp moves to its larger maximum (a warp-uniform decision,
+        // identical in the two warps of a row, which see the same maxima)
         float alpha = 1.f;
         bool rescale = false;
-        if (mx > m_used + kRescaleThreshold) {
+        if (__any_sync(0xffffffffu, mx > m_used + kRescaleThreshold)) {
+          const float m_new = fmaxf(m_used, mx);
           rescale = j > 0;
-          alpha = (m_used == -INFINITY) ? 0.f : ex2(m_used - mx);
-          m_used = mx;
+          alpha = (m_used == -INFINITY) ? 0.f : ex2(m_used - m_new);
+          m_used = m_new;
         }
         f2 rsp[2] = {dup2(0.f), dup2(0.f)};  // partial row sums
         const f2 sc2 = dup2(p.scale_log2), nm2 = dup2(-m_used);
@@ -489,7 +517,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&p_full[x]);
+        arrive_one_lane(&p_full[x]);
       }
       gb += nb;
       // the row sum over both halves (a warp that failed still takes part, releasing its partner).
