@@ -21,6 +21,8 @@
 // (lazy rescaling), and l is kept consistent with the max actually used. Keys >= key_len[b] (and
 // >= Lk) get probability 0; key blocks entirely past key_len are skipped.
 
+#include <mutex>
+
 #include "internal.h"
 #include "sm100.cuh"
 
@@ -688,20 +690,37 @@ constexpr size_t kStaticScratchBytes =
 static_assert(kStaticFlagBytes % 256 == 0, "partial slots stay 256-byte aligned");
 static __device__ __align__(256) unsigned char g_attn_static_ws[kStaticScratchBytes];
 
-// The static workspace's address (cudaGetSymbolAddress, once per context). The flags must start at
-// zero: the first call clears them with a memset on the context's stream (nothing is allocated);
-// every launch leaves them at zero again, and anima_sync clears them after a device error.
+// The static workspace's device address. In host code g_attn_static_ws names a host-side stand-in,
+// not device memory, so the address comes from cudaGetSymbolAddress: once per device, with that
+// device made current, on the first call that needs the workspace there. That first call also
+// clears the flags, which must start at zero, with a memset on the context's stream (nothing is
+// allocated); every launch leaves them at zero again, and anima_sync clears them after a device
+// error. The first call on a device should therefore come before any stream capture.
+constexpr int kStaticMaxDevices = 64;
 int static_scratch(anima_ctx* ctx) {
   ANIMA_REQUIRE(ctx->num_sms <= kStaticMaxSms,
                 "anima_attention_noalloc: stream-K needs %d workspace slots (one per SM), the static workspace "
                 "holds %d",
                 ctx->num_sms, kStaticMaxSms);
-  if (ctx->attn_static_ws) return ANIMA_OK;
-  void* base = nullptr;
-  ANIMA_CUDA(cudaGetSymbolAddress(&base, g_attn_static_ws));
-  ANIMA_REQUIRE(base != nullptr, "anima_attention_noalloc: no address for the static workspace");
-  ANIMA_CUDA(cudaMemsetAsync(base, 0, kStaticFlagBytes, ctx->stream));
-  ctx->attn_static_ws = base;
+  ANIMA_REQUIRE(ctx->device >= 0 && ctx->device < kStaticMaxDevices, "anima_attention_noalloc: device %d",
+                ctx->device);
+  static std::mutex mu;
+  static void* addr[kStaticMaxDevices] = {};
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[ctx->device]) {
+    int cur = 0;
+    ANIMA_CUDA(cudaGetDevice(&cur));
+    if (cur != ctx->device) ANIMA_CUDA(cudaSetDevice(ctx->device));
+    void* base = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&base, g_attn_static_ws);
+    const cudaError_t z = e == cudaSuccess ? cudaMemsetAsync(base, 0, kStaticFlagBytes, ctx->stream) : cudaSuccess;
+    if (cur != ctx->device) ANIMA_CUDA(cudaSetDevice(cur));
+    ANIMA_CUDA(e);
+    ANIMA_CUDA(z);
+    ANIMA_REQUIRE(base != nullptr, "anima_attention_noalloc: no device address for the static workspace");
+    addr[ctx->device] = base;
+  }
+  ctx->attn_static_ws = addr[ctx->device];  // also lets anima_sync clear the flags after an error
   return ANIMA_OK;
 }
 

@@ -195,13 +195,17 @@ int anima_rope(anima_ctx* ctx, void* x, int dtype, int L, int H, int D, int row_
 /* ops.attention (ops.js:166-208, kernels.js:147-299): non-causal multi-head attention, tcgen05
  * flash kernel, fp32 softmax. head_dim must be 128. */
 int anima_attention(anima_ctx* ctx, const anima_attention_args* a);
-/* anima_attention without any device allocation (no reference counterpart): the stream-K
- * workspace is a static device array in the library (21.6 MB: ready flags for up to 160 SMs, then
- * one 135 KB partial slot per SM) found with cudaGetSymbolAddress on the first call, which also
- * clears the flags with a memset on the context's stream; every launch leaves them at zero. Same
- * arguments, schedule and results as anima_attention. Fails with ANIMA_ERR_ARG when the device
- * has more SMs than the workspace has slots. Calls on the same device must not overlap (any
- * context or stream): they share the workspace and would race. */
+/* anima_attention for callers that cannot call cudaMalloc (no reference counterpart): hosts whose
+ * device memory belongs to another allocator or pool, or that must not allocate once running.
+ * anima_attention allocates its stream-K workspace (20 MB) on first use; this entry point instead
+ * uses a static device array in the library (21.6 MB: ready flags for up to 160 SMs, then one
+ * 135 KB partial slot per SM), held by every GPU that loads the library until exit. Its first call
+ * on a device looks up the array's address (cudaGetSymbolAddress, with that device current) and
+ * clears the flags with a memset on the context's stream; make that first call before any stream
+ * capture. Every launch leaves the flags at zero again. Same arguments, schedule and results as
+ * anima_attention. Fails with ANIMA_ERR_ARG when the device has more SMs than the array has slots.
+ * All calls share the array: calls on one device that overlap on the GPU (any context or stream)
+ * race. */
 int anima_attention_noalloc(anima_ctx* ctx, const anima_attention_args* a);
 /* ops.elementwise (ops.js:154-160): op 0 copy, 1 add, 2 silu, 3 silu_mul; n fp32 elements. */
 int anima_elementwise(anima_ctx* ctx, int op, const float* a, const float* b, float* y, long long n);

@@ -1,7 +1,9 @@
-"""anima_attention_noalloc, the attention entry point whose stream-K workspace is the library's
-static device array: on two consecutive calls with different inputs it must give exactly what
-anima_attention (context-owned workspace) gives. Collected last, so it also runs after every other
-GPU test has used the library; it passes alone as well."""
+"""anima_attention_noalloc, the attention entry point for hosts that cannot call cudaMalloc (their
+device memory belongs to another allocator, or they must not allocate once running): its stream-K
+workspace is a static device array in the library instead of an allocation. On two calls in a row
+with different inputs it must give exactly what anima_attention (context-owned workspace) gives.
+Collected last, so it also runs after every other GPU test has used the library; it passes alone
+as well."""
 
 import numpy as np
 import pytest
