@@ -58,6 +58,7 @@ struct Params {
   float scale_log2;  // softmax scale * log2(e)
   // stream-K: the units' key blocks split evenly over the CTAs (no key mask; every unit has ublk)
   int stream_k, units, ublk;
+  int persist;       // whole units, CTA c taking units c, c + grid, ... (grid = SM count)
   float* ws;         // [units][PART_FLOATS] partial softmax states of split units
   unsigned* flags;   // [units] tail part written (cleared by the head part)
 };
@@ -149,11 +150,16 @@ __device__ __forceinline__ Seg segment_at(const Params& p, long long g, long lon
 // it are skipped).
 __device__ __forceinline__ int build_segments(const Params& p, int4* out) {
   if (!p.stream_k) {
-    const int unit = blockIdx.x;
-    const int b = unit / p.q_pairs / p.heads;
-    const int kv_len = p.key_len ? min(p.Lk, p.key_len[p.kv_bcast ? 0 : b]) : p.Lk;
-    out[0] = make_int4(unit, 0, kv_len > 0 ? (kv_len + TILE - 1) / TILE : 0, kWhole);
-    return 1;
+    // whole units: this CTA's one unit, or (persistent grid) every grid-th unit, so a CTA's next
+    // unit loads its Q and starts its first QK^T while the previous unit's output is written
+    const int step = p.persist ? static_cast<int>(gridDim.x) : p.units;
+    int n = 0;
+    for (int unit = blockIdx.x; unit < p.units && n < MAX_SEGS; unit += step) {
+      const int b = unit / p.q_pairs / p.heads;
+      const int kv_len = p.key_len ? min(p.Lk, p.key_len[p.kv_bcast ? 0 : b]) : p.Lk;
+      out[n++] = make_int4(unit, 0, kv_len > 0 ? (kv_len + TILE - 1) / TILE : 0, kWhole);
+    }
+    return n;
   }
   const long long total = static_cast<long long>(p.units) * p.ublk;
   long long g = total * blockIdx.x / gridDim.x;
@@ -818,6 +824,10 @@ int attention_launch(anima_ctx* ctx, const anima_attention_args* a, bool static_
       p.flags = ctx->attn_flags;
     }
     p.stream_k = 1;
+    grid = ctx->num_sms;
+  } else if (units > ctx->num_sms && (units + ctx->num_sms - 1) / ctx->num_sms <= attn::MAX_SEGS) {
+    // more than one wave of whole units: a persistent grid, one CTA per SM
+    p.persist = 1;
     grid = ctx->num_sms;
   }
   // (profiling events are created only on the allocating entry point)

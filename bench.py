@@ -213,6 +213,7 @@ def kernel_case(args):
     mlp2  the 8192->2048 block linear with the gated residual
     qkv   the 2048->6144 qkv linear with the per-head RMSNorm + RoPE epilogue
     attn  self-attention, 16 heads x 4096 tokens x d=128 (fp16 q/k/v in the qkv layout)
+    xattn cross-attention, 4096 queries x 512 context rows (k|v stacked per row), 16 heads
     ln    LayerNorm + adaLN + ConvRot + two-plane quantization of [4096, 2048]
     gelu  GELU + ConvRot + quantization of the fp16 MLP hidden [4096, 8192]
     rotq  ConvRot + quantization of the fp16 attention output [4096, 2048]
@@ -254,6 +255,15 @@ def kernel_case(args):
         fn = lambda: ops.attention(qkv, qkv, qkv, Lq=M, Lk=M, H=16, ldq=6144, ldk=6144, ldv=6144, q_off=0,  # noqa: E731
                                    k_off=2048, v_off=4096, out=out)
         work, unit = 4.0 * M * M * 128 * 16, "TFLOP/s"
+    elif args.kernel == "xattn":
+        # cross-attention of one DiT block: 4096 queries against the 512-row (zero-padded) context
+        dt = torch.float16 if args.attn == "f16" else torch.bfloat16
+        q = torch.randn(M, 2048, device="cuda").to(dt)
+        kv = torch.randn(512, 4096, device="cuda").to(dt)
+        out = torch.empty(M, 2048, dtype=dt, device="cuda")
+        fn = lambda: ops.attention(q, kv, kv, Lq=M, Lk=512, H=16, ldk=4096, ldv=4096, k_off=0, v_off=2048,  # noqa: E731
+                                   out=out)
+        work, unit = 4.0 * M * 512 * 128 * 16, "TFLOP/s"
     elif args.kernel == "ln":
         x = torch.randn(M, 2048, device="cuda")
         mod = torch.randn(6144, device="cuda") * 0.5
@@ -433,7 +443,7 @@ def run_cfg(args, world, rank, local):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--kernel", default=None, help="time one kernel case instead (mlp1|mlp2|qkv|oproj|attn|ln|gelu|rotq|xembed|final)")
+    ap.add_argument("--kernel", default=None, help="time one kernel case instead (mlp1|mlp2|qkv|oproj|attn|xattn|ln|gelu|rotq|xembed|final)")
     ap.add_argument("--reps", type=int, default=20)
     ap.add_argument("--batch", type=int, default=10, help="kernel cases: launches per timed sample")
     ap.add_argument("--act", default="gelu", help="kernel case mlp1: epilogue activation (gelu|none)")

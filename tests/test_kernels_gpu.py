@@ -492,3 +492,19 @@ def test_stream_k_not_used_with_key_mask(ops, split_mode):
     vb = v.reshape(Lk, H, 128).transpose(0, 1)[:2]
     ref = attn_ref(qb, kb, vb, 300).transpose(1, 0, 2).reshape(Lq, 256)
     assert rel_l2(out[:, :256], ref) < 6e-3
+
+
+def test_cross_attention_persistent_grid(ops):
+    """4096 queries x 512 keys x 16 heads: 256 whole units on a persistent grid (one CTA per SM, each
+    taking every grid-th unit); checked against the oracle on two heads."""
+    Lq, Lk, H = 4096, 512, 16
+    q = randn((Lq, 2048), 80).to(torch.bfloat16)
+    kv = randn((Lk, 4096), 81).to(torch.bfloat16)
+    out = ops.attention(q.to(DEV), kv.to(DEV), kv.to(DEV), Lq=Lq, Lk=Lk, H=H, ldk=4096, ldv=4096, k_off=0,
+                        v_off=2048, out_dtype=torch.float32).cpu().numpy()
+    for h in (0, H - 1):
+        qh = q[:, h * 128:(h + 1) * 128][None]
+        kh = kv[:, h * 128:(h + 1) * 128][None]
+        vh = kv[:, 2048 + h * 128:2048 + (h + 1) * 128][None]
+        ref = attn_ref(qh, kh, vh)[0]
+        assert rel_l2(out[:, h * 128:(h + 1) * 128], ref) < 6e-3, h
