@@ -508,3 +508,43 @@ def test_cross_attention_persistent_grid(ops):
         vh = kv[:, 2048 + h * 128:2048 + (h + 1) * 128][None]
         ref = attn_ref(qh, kh, vh)[0]
         assert rel_l2(out[:, h * 128:(h + 1) * 128], ref) < 6e-3, h
+
+
+def test_stream_k_shared_kv_batch(ops, split_mode):
+    """Stream-K forced on a batch of 2 sharing one K/V (the CFG cross-attention layout): matches the
+    whole-unit schedule and the oracle."""
+    B, H, Lq, Lk = 2, 16, 2048, 1024
+    q = randn((B * Lq, 2048), 82).to(torch.bfloat16).to(DEV)
+    kv = randn((Lk, 4096), 83).to(torch.bfloat16).to(DEV)
+    args = dict(Lq=Lq, Lk=Lk, H=H, ldk=4096, ldv=4096, k_off=0, v_off=2048, batch=B, q_bstride=Lq * 2048,
+                k_bstride=0, v_bstride=0, out_dtype=torch.float32)
+    split_mode(0)
+    whole = ops.attention(q, kv, kv, **args).cpu().numpy()
+    split_mode(1)
+    sk = ops.attention(q, kv, kv, **args).cpu().numpy()
+    assert rel_l2(sk, whole) < 2e-3
+    kh = kv[:, :128].cpu()[None]
+    vh = kv[:, 2048:2048 + 128].cpu()[None]
+    for b in range(B):
+        qh = q[b * Lq:(b + 1) * Lq, :128].cpu()[None]
+        assert rel_l2(sk[b * Lq:(b + 1) * Lq, :128], attn_ref(qh, kh, vh)[0]) < 6e-3, b
+
+
+def test_persistent_grid_batched_key_len(ops):
+    """More than one wave of whole units with a different key_len per batch item (each unit looks up
+    its own item's length on the persistent grid)."""
+    B, H, Lq, Lk = 2, 16, 2048, 384
+    q = randn((B * Lq, 2048), 84).to(torch.bfloat16)
+    k = randn((B * Lk, 2048), 85).to(torch.bfloat16)
+    v = randn((B * Lk, 2048), 86).to(torch.bfloat16)
+    kl = torch.tensor([130, 384], dtype=torch.int32)
+    out = ops.attention(q.to(DEV), k.to(DEV), v.to(DEV), Lq=Lq, Lk=Lk, H=H, batch=B, q_bstride=Lq * 2048,
+                        k_bstride=Lk * 2048, v_bstride=Lk * 2048, key_len=kl.to(DEV),
+                        out_dtype=torch.float32).cpu().numpy()
+    for b in range(B):
+        qb = q[b * Lq:(b + 1) * Lq].reshape(Lq, H, 128).transpose(0, 1)[[0, H - 1]]
+        kb = k[b * Lk:(b + 1) * Lk].reshape(Lk, H, 128).transpose(0, 1)[[0, H - 1]]
+        vb = v[b * Lk:(b + 1) * Lk].reshape(Lk, H, 128).transpose(0, 1)[[0, H - 1]]
+        ref = attn_ref(qb, kb, vb, int(kl[b]))
+        got = out[b * Lq:(b + 1) * Lq].reshape(Lq, H, 128)[:, [0, H - 1]].transpose(1, 0, 2)
+        assert rel_l2(got, ref) < 6e-3, b
