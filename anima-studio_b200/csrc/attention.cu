@@ -2,8 +2,9 @@
 // (Lq = Lk = 4096 at 1024^2) and cross-attention against cached text keys (Lk = 256..512). The
 // reference's counterpart is the fp32 WGSL flash kernel of app/gpu/kernels.js:147-299.
 //
-// A unit = one (batch, head) and two 128-query tiles A and B. A CTA runs one unit, or, under
-// stream-K (below), an equal share of all units' key blocks. 576 threads:
+// A unit = one (batch, head) and two 128-query tiles A and B. A CTA runs one unit; with more than
+// one wave of units, every grid-th unit (one CTA per SM); or, under stream-K (below), an equal
+// share of all units' key blocks. 576 threads:
 //   warps 0-7   softmax for tile A, warps 8-15 for tile B. Warp w serves the 32 query rows of
 //               lane quadrant w % 4 (the tensor-memory lanes it may access) and the key columns
 //               [64 h, 64 h + 64) with h = (w / 4) % 2, so two warps on the same SM sub-partition
@@ -113,7 +114,8 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
 }
 
 // A CTA's work is a list of segments: (unit, first key block, end key block), a unit being one
-// (batch, head, pair of query tiles). Without stream-K each CTA runs one whole unit. With stream-K
+// (batch, head, pair of query tiles). Without stream-K each CTA runs whole units (one, or every
+// grid-th on a persistent grid). With stream-K
 // (long self-attention without a key mask) the units' key blocks are laid end to end and cut into
 // one equal range per CTA, so every SM gets the same number of key blocks instead of whole units
 // in ceil(units / SMs) waves. The range of CTA c reads: [tail of unit u] whole units... [head of
