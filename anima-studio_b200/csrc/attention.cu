@@ -712,19 +712,14 @@ int static_scratch(anima_ctx* ctx) {
                 ctx->num_sms, kStaticMaxSms);
   ANIMA_REQUIRE(ctx->device >= 0 && ctx->device < kStaticMaxDevices, "anima_attention_noalloc: device %d",
                 ctx->device);
+  // the entry point has made ctx->device current (ANIMA_ON_DEVICE), so the symbol resolves there
   static std::mutex mu;
   static void* addr[kStaticMaxDevices] = {};
   std::lock_guard<std::mutex> lock(mu);
   if (!addr[ctx->device]) {
-    int cur = 0;
-    ANIMA_CUDA(cudaGetDevice(&cur));
-    if (cur != ctx->device) ANIMA_CUDA(cudaSetDevice(ctx->device));
     void* base = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&base, g_attn_static_ws);
-    const cudaError_t z = e == cudaSuccess ? cudaMemsetAsync(base, 0, kStaticFlagBytes, ctx->stream) : cudaSuccess;
-    if (cur != ctx->device) ANIMA_CUDA(cudaSetDevice(cur));
-    ANIMA_CUDA(e);
-    ANIMA_CUDA(z);
+    ANIMA_CUDA(cudaGetSymbolAddress(&base, g_attn_static_ws));
+    ANIMA_CUDA(cudaMemsetAsync(base, 0, kStaticFlagBytes, ctx->stream));
     ANIMA_REQUIRE(base != nullptr, "anima_attention_noalloc: no device address for the static workspace");
     addr[ctx->device] = base;
   }
@@ -743,6 +738,7 @@ namespace {
 // instead of the context's lazily allocated one.
 int attention_launch(anima_ctx* ctx, const anima_attention_args* a, bool static_ws) {
   ANIMA_REQUIRE(ctx && a, "anima_attention: NULL argument");
+  ANIMA_ON_DEVICE(ctx);
   ANIMA_REQUIRE(a->head_dim == attn::HD, "anima_attention: head_dim %d (only 128)", a->head_dim);
   ANIMA_REQUIRE(a->dtype == ANIMA_BF16 || a->dtype == ANIMA_F16, "anima_attention: q/k/v dtype must be bf16 or f16");
   ANIMA_REQUIRE(a->out_dtype == ANIMA_F32 || a->out_dtype == ANIMA_BF16 || a->out_dtype == ANIMA_F16,
@@ -838,11 +834,10 @@ int attention_launch(anima_ctx* ctx, const anima_attention_args* a, bool static_
   using Kfn = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const attn::Params);
   const int kind = a->dtype == ANIMA_BF16 ? 1 : 0;
   const Kfn fns[2] = {attn::attention_kernel<false>, attn::attention_kernel<true>};
-  static bool set[2] = {};
   const Kfn fn = fns[kind];
-  if (!set[kind]) {
-    ANIMA_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, attn::SMEM_BYTES));
-    set[kind] = true;
+  {
+    int st = set_max_dynamic_smem(reinterpret_cast<const void*>(fn), attn::SMEM_BYTES);
+    if (st) return st;
   }
   fn<<<static_cast<int>(grid), attn::THREADS, attn::SMEM_BYTES, ctx->stream>>>(tq, tk, tv, p);
   return check_launch("attention_kernel");

@@ -716,12 +716,8 @@ int launch(anima_ctx* ctx, const anima_qact* x, const anima_weight* W, const ani
   }();
   p.group_m = group_m_env > 0 ? group_m_env : 8;
 
-  static bool attr_set = false;
-  if (!attr_set) {
-    ANIMA_CUDA(cudaFuncSetAttribute(gemm_i8_kernel<BN, NPLANES, LORA>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    C::SMEM_BYTES));
-    attr_set = true;
-  }
+  st = set_max_dynamic_smem(reinterpret_cast<const void*>(gemm_i8_kernel<BN, NPLANES, LORA>), C::SMEM_BYTES);
+  if (st) return st;
   const int grid = p.num_tiles < ctx->num_sms ? p.num_tiles : ctx->num_sms;
   ProfScope prof(ctx, NPLANES == 2 ? "linear.i8x2" : "linear.i8", 2.0 * M * N * K,
                  static_cast<double>(M) * K * NPLANES + static_cast<double>(N) * K);
@@ -736,12 +732,37 @@ using namespace anima;
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+// W4 weights run as their int8 grid: anima_linear decodes the layer into this context-owned buffer
+// right before the GEMM (the same stream, so the GEMM sees the whole grid and the next W4 call
+// cannot overwrite it early). The buffer holds at least the DiT's largest linear (8192 x 2048) and
+// grows, outside stream capture only, when a larger weight comes.
+static int w4_scratch(anima_ctx* ctx, size_t bytes) {
+  if (ctx->w4_ws_bytes >= bytes) return ANIMA_OK;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  ANIMA_CUDA(cudaStreamIsCapturing(ctx->stream, &cap));
+  ANIMA_REQUIRE(cap == cudaStreamCaptureStatusNone,
+                "anima_linear: the W4 decode buffer would grow to %zu bytes inside stream capture (run the largest "
+                "W4 linear once before capturing)",
+                bytes);
+  if (ctx->w4_ws) {  // kernels of earlier calls may still read the old buffer
+    ANIMA_CUDA(cudaDeviceSynchronize());
+    ANIMA_CUDA(cudaFree(ctx->w4_ws));
+    ctx->w4_ws = nullptr;
+    ctx->w4_ws_bytes = 0;
+  }
+  const size_t want = bytes > size_t(8192) * 2048 ? bytes : size_t(8192) * 2048;
+  ANIMA_CUDA(cudaMalloc(reinterpret_cast<void**>(&ctx->w4_ws), want));
+  ctx->w4_ws_bytes = want;
+  return ANIMA_OK;
+}
+
 extern "C" int anima_linear(anima_ctx* ctx, const anima_qact* x, const anima_weight* W, const anima_linear_opts* o) {
   ANIMA_REQUIRE(ctx && x && W && o, "anima_linear: NULL argument");
+  ANIMA_ON_DEVICE(ctx);
+  ANIMA_REQUIRE(W->kind == ANIMA_W_I8 || W->kind == ANIMA_W_W4,
+                "anima_linear: weight kind %d is not a ConvRot int8 or W4A8 weight", W->kind);
   if (W->kind == ANIMA_W_W4)
-    return set_error(ANIMA_ERR_UNSUPPORTED,
-                     "anima_linear: W4 weights are decoded once with anima_unpack_w4 and passed as kind I8");
-  ANIMA_REQUIRE(W->kind == ANIMA_W_I8, "anima_linear: weight kind %d is not a ConvRot int8 weight", W->kind);
+    ANIMA_REQUIRE(W->s_rel && W->codebook, "anima_linear: a W4 weight needs s_rel and the codebook");
   ANIMA_REQUIRE(x->cols == W->K, "anima_linear: activation has %d columns, weight K is %d", x->cols, W->K);
   ANIMA_REQUIRE(x->rows > 0 && W->N > 0, "anima_linear: empty problem (M=%d, N=%d)", x->rows, W->N);
   ANIMA_REQUIRE(W->K % gemm::BK == 0, "anima_linear: K=%d must be a multiple of %d", W->K, gemm::BK);
@@ -788,6 +809,17 @@ extern "C" int anima_linear(anima_ctx* ctx, const anima_qact* x, const anima_wei
                     (!o->norm_k || aligned16(o->norm_k)) && (!o->rope || aligned16(o->rope)) &&
                     (!o->gate || (aligned16(o->gate) && o->gate_off % 4 == 0)),
                 "anima_linear: scale/bias/gate/norm/rope vectors must be 16-byte aligned (gate_off a multiple of 4)");
+  anima_weight grid;
+  if (W->kind == ANIMA_W_W4) {
+    int st = w4_scratch(ctx, static_cast<size_t>(W->N) * W->K);
+    if (st) return st;
+    st = launch_w4_decode(ctx, static_cast<const uint8_t*>(W->data), W->s_rel, W->codebook, W->N, W->K, ctx->w4_ws);
+    if (st) return st;
+    grid = *W;
+    grid.kind = ANIMA_W_I8;
+    grid.data = ctx->w4_ws;
+    W = &grid;
+  }
   // Two planes: 128-column tiles double-buffer both accumulators (2 x 2 x 128 TMEM columns) so the
   // epilogue overlaps the next tile's MMAs. One plane: 256-column tiles, double-buffered.
   // LoRA side paths: 128-column tiles (each inside one entry), with the entry's B slice staged

@@ -20,6 +20,8 @@ struct anima_ctx {
   unsigned* attn_flags = nullptr;   // their ready flags, zero between launches
   int attn_split = -1;              // anima_ctx_set_attention_split mode
   void* attn_static_ws = nullptr;   // static workspace of anima_attention_noalloc (flags first)
+  int8_t* w4_ws = nullptr;          // int8 grid of the W4 weight anima_linear is running (gemm_i8.cu)
+  size_t w4_ws_bytes = 0;
 };
 
 namespace anima {
@@ -32,6 +34,27 @@ int check_launch(const char* what);
 // dims/strides: dims[0] is the contiguous dimension; strides are in bytes for dims 1..rank-1.
 int make_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base, const uint64_t* dims,
               const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swizzle);
+
+// Makes the context's device current for the length of one entry point and puts the caller's
+// device back afterwards, so one host thread can drive contexts on several GPUs in turn (kernel
+// launches, symbol reads and allocations all act on the current device).
+struct DeviceScope {
+  int prev = -1;
+  int status = ANIMA_OK;
+  explicit DeviceScope(const anima_ctx* ctx);
+  ~DeviceScope();
+  DeviceScope(const DeviceScope&) = delete;
+  DeviceScope& operator=(const DeviceScope&) = delete;
+};
+
+// cudaFuncAttributeMaxDynamicSharedMemorySize = bytes for kernel fn on the current device. The
+// attribute belongs to the device, so it is set once per (kernel, device) pair, under a lock.
+int set_max_dynamic_smem(const void* fn, int bytes);
+
+// Decode 4-bit weights to their int8 grid values (rowops.cu; the arithmetic of anima_unpack_w4):
+// out int8 [N, K] from packed nibbles [N, K/2] and fp8 group scales [N, K/16].
+int launch_w4_decode(anima_ctx* ctx, const uint8_t* packed, const uint8_t* s_rel, const float* codebook, int N, int K,
+                     int8_t* out);
 
 // Profiling scope: records CUDA events around a launch when ANIMA_PROFILE=1.
 struct ProfScope {
@@ -55,3 +78,8 @@ struct ProfScope {
     int _st = ::anima::check_cuda((call), #call);                  \
     if (_st) return _st;                                           \
   } while (0)
+
+// First statement after an entry point's NULL check of ctx: run the rest on ctx->device.
+#define ANIMA_ON_DEVICE(ctx)                                       \
+  ::anima::DeviceScope _anima_device_scope(ctx);                   \
+  if (_anima_device_scope.status) return _anima_device_scope.status

@@ -566,6 +566,43 @@ __global__ void unpack_w4_kernel(const uint8_t* __restrict__ packed, const uint8
   out[k0 + 1] = static_cast<int8_t>(fminf(fmaxf(rintf(p1), -127.f), 127.f));
 }
 
+// 32 codes per thread (16 packed bytes = two fp8 groups), the arithmetic of unpack_w4_kernel,
+// written as two 16-byte stores. Nibble e of packed word j holds code 8j + e (the low nibble of a
+// byte is the even k). The codebook sits in shared memory: 16 distinct words in 16 banks, so the
+// data-dependent lookups never conflict.
+__global__ void __launch_bounds__(256) w4_decode_kernel(const uint8_t* __restrict__ packed,
+                                                        const uint8_t* __restrict__ s_rel, const float* __restrict__ cb,
+                                                        long long n_chunks, int K, int8_t* __restrict__ out) {
+  __shared__ float lut[16];
+  if (threadIdx.x < 16) lut[threadIdx.x] = cb[threadIdx.x];
+  __syncthreads();
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n_chunks) return;
+  const long long k0 = 32 * i;  // flat index of the chunk's first code
+  const long long row = k0 / K;
+  const int kk = static_cast<int>(k0 - row * K);
+  const uint4 p = __ldg(reinterpret_cast<const uint4*>(packed) + i);
+  const uint8_t* sr = s_rel + row * (K / 16) + kk / 16;
+  const float sg[2] = {fp8_e4m3fn(__ldg(sr)), fp8_e4m3fn(__ldg(sr + 1))};
+  const uint32_t w[4] = {p.x, p.y, p.z, p.w};
+  uint32_t o[8];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float s = sg[j >> 1];
+    uint32_t half[2] = {0u, 0u};
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float v = fminf(fmaxf(rintf(__fmul_rn(lut[(w[j] >> (4 * e)) & 15u], s)), -127.f), 127.f);
+      half[e >> 2] |= (static_cast<uint32_t>(static_cast<int>(v)) & 0xFFu) << (8 * (e & 3));
+    }
+    o[2 * j] = half[0];
+    o[2 * j + 1] = half[1];
+  }
+  uint4* dst = reinterpret_cast<uint4*>(out + k0);
+  dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+  dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+}
+
 // ------------------------------------------------------------------ model glue
 __global__ void patchify_kernel(const float* __restrict__ lat, int B, int h, int w, float* patches) {
   const int Hp = h / 2, Wp = w / 2;
@@ -810,6 +847,18 @@ int launch_rot(anima_ctx* ctx, const TIn* x, int rows, int cols, int ldx, int ro
 inline bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 }  // namespace rowops
+
+int launch_w4_decode(anima_ctx* ctx, const uint8_t* packed, const uint8_t* s_rel, const float* codebook, int N, int K,
+                     int8_t* out) {
+  if (K % 32 != 0 || !rowops::al16(packed) || !rowops::al16(out))
+    return set_error(ANIMA_ERR_ARG, "W4 decode: K=%d must be a multiple of 32, packed/out 16-byte aligned", K);
+  const long long chunks = static_cast<long long>(N) * K / 32;
+  ProfScope prof(ctx, "w4.decode", 0, static_cast<double>(N) * K * 1.5 + static_cast<double>(N) * K / 16);
+  rowops::w4_decode_kernel<<<static_cast<int>((chunks + 255) / 256), 256, 0, ctx->stream>>>(packed, s_rel, codebook,
+                                                                                            chunks, K, out);
+  return check_launch("w4_decode_kernel");
+}
+
 }  // namespace anima
 
 using namespace anima;
@@ -831,6 +880,7 @@ extern "C" {
 int anima_layernorm_mod(anima_ctx* ctx, const float* x, int rows, int cols, const float* mod, int shift_off,
                         int scale_off, float eps, int rotate, void* out, int out_dtype) {
   ANIMA_REQUIRE(ctx && x && mod && out, "anima_layernorm_mod: NULL argument");
+  ANIMA_ON_DEVICE(ctx);
   ANIMA_REQUIRE(rows > 0, "anima_layernorm_mod: rows=%d", rows);
   ANIMA_REQUIRE(al16(x) && al16(out) && shift_off % 4 == 0 && scale_off % 4 == 0 && al16(mod),
                 "anima_layernorm_mod: pointers/offsets must be 16-byte aligned");
@@ -846,6 +896,7 @@ int anima_layernorm_mod(anima_ctx* ctx, const float* x, int rows, int cols, cons
 int anima_layernorm_mod_quant(anima_ctx* ctx, const float* x, int rows, int cols, const float* mod, int shift_off,
                               int scale_off, float eps, const anima_qact* out) {
   ANIMA_REQUIRE(ctx && x && mod, "anima_layernorm_mod_quant: NULL argument");
+  ANIMA_ON_DEVICE(ctx);
   ANIMA_REQUIRE(rows > 0, "anima_layernorm_mod_quant: rows=%d", rows);
   int st = check_qact(out, rows, cols, "anima_layernorm_mod_quant");
   if (st) return st;
@@ -857,6 +908,7 @@ int anima_layernorm_mod_quant(anima_ctx* ctx, const float* x, int rows, int cols
 
 int anima_rotate(anima_ctx* ctx, const void* x, int in_dtype, int rows, int cols, int ldx, void* y, int out_dtype) {
   ANIMA_REQUIRE(ctx && x && y, "anima_rotate: NULL argument");
+  ANIMA_ON_DEVICE(ctx);
   ANIMA_REQUIRE(rows > 0 && ldx >= cols && al16(x) && al16(y), "anima_rotate: bad shape or alignment");
   ANIMA_REQUIRE(in_dtype == ANIMA_F32 && out_dtype == ANIMA_F32, "anima_rotate: only fp32 in/out (use anima_rotate_quant)");
   ProfScope prof(ctx, "hadamard", 0, rows * (double)cols * 8);
@@ -866,6 +918,7 @@ int anima_rotate(anima_ctx* ctx, const void* x, int in_dtype, int rows, int cols
 static int rot_quant(anima_ctx* ctx, const void* x, int in_dtype, int rows, int cols, int ldx, const anima_qact* out,
                      int rotate, const char* who, int act = ANIMA_ACT_NONE) {
   ANIMA_REQUIRE(ctx && x, "%s: NULL argument", who);
+  ANIMA_ON_DEVICE(ctx);
   ANIMA_REQUIRE(rows > 0 && ldx >= cols && al16(x), "%s: bad shape or alignment", who);
   int st = check_qact(out, rows, cols, who);
   if (st) return st;
@@ -898,6 +951,7 @@ int anima_quant_rows(anima_ctx* ctx, const void* x, int in_dtype, int rows, int 
 int anima_rmsnorm(anima_ctx* ctx, const void* x, int in_dtype, int rows, int cols, const float* w, float eps, void* y,
                   int out_dtype) {
   ANIMA_REQUIRE(ctx && x && w && y && rows > 0 && cols > 0, "anima_rmsnorm: bad argument");
+  ANIMA_ON_DEVICE(ctx);
   ProfScope prof(ctx, "rmsnorm", 0, 8.0 * rows * cols);
   const int grid = grid1(rows, 8);
 #define RMS(TI, TO) rmsnorm_kernel<TI, TO><<<grid, 256, 0, ctx->stream>>>((const TI*)x, rows, cols, w, eps, (TO*)y)
@@ -914,6 +968,7 @@ int anima_rmsnorm(anima_ctx* ctx, const void* x, int in_dtype, int rows, int col
 int anima_qk_norm_rope(anima_ctx* ctx, void* qkv, int dtype, int L, int H, int D, int ld, const float* qn,
                        const float* kn, const float* rope, int rope_rows, float eps) {
   ANIMA_REQUIRE(ctx && qkv && qn && kn && rope && L > 0 && H > 0 && rope_rows > 0, "anima_qk_norm_rope: bad argument");
+  ANIMA_ON_DEVICE(ctx);
   ANIMA_REQUIRE(D == 128, "anima_qk_norm_rope: head dim %d (only 128)", D);
   ProfScope prof(ctx, "qk_norm_rope", 0, 2.0 * L * 2 * H * D * (dtype == ANIMA_F32 ? 4 : 2));
   const long long n = static_cast<long long>(L) * 2 * H;
@@ -928,6 +983,7 @@ int anima_qk_norm_rope(anima_ctx* ctx, void* qkv, int dtype, int L, int H, int D
 int anima_rope(anima_ctx* ctx, void* x, int dtype, int L, int H, int D, int row_stride, int col_off, const float* rope,
                int rope_rows) {
   ANIMA_REQUIRE(ctx && x && rope && L > 0 && H > 0 && D > 0 && D % 2 == 0 && rope_rows > 0, "anima_rope: bad argument");
+  ANIMA_ON_DEVICE(ctx);
   const long long n = static_cast<long long>(L) * H * (D / 2);
   ProfScope prof(ctx, "rope", 0, 2.0 * n * 2 * (dtype == ANIMA_F32 ? 4 : 2));
   if (dtype == ANIMA_F32) rope_kernel<float><<<grid1(n, 256), 256, 0, ctx->stream>>>((float*)x, L, H, D, row_stride, col_off, rope, rope_rows);
@@ -940,6 +996,7 @@ int anima_rope(anima_ctx* ctx, void* x, int dtype, int L, int H, int D, int row_
 int anima_lincomb(anima_ctx* ctx, float* y, long long n, const float* x0, const float* x1, const float* x2,
                   const float* x3, const float* c) {
   ANIMA_REQUIRE(ctx && y && c && n > 0, "anima_lincomb: bad argument");
+  ANIMA_ON_DEVICE(ctx);
   const float* xs[4] = {x0, x1, x2, x3};
   ANIMA_REQUIRE(al16(y), "anima_lincomb: y must be 16-byte aligned");
   for (int k = 0; k < 4; ++k) ANIMA_REQUIRE(!xs[k] || al16(xs[k]), "anima_lincomb: x%d must be 16-byte aligned", k);
@@ -950,6 +1007,7 @@ int anima_lincomb(anima_ctx* ctx, float* y, long long n, const float* x0, const 
 
 int anima_elementwise(anima_ctx* ctx, int op, const float* a, const float* b, float* y, long long n) {
   ANIMA_REQUIRE(ctx && a && y && n >= 0 && op >= 0 && op <= 3, "anima_elementwise: bad argument");
+  ANIMA_ON_DEVICE(ctx);
   ANIMA_REQUIRE(!(op == 1 || op == 3) || b, "anima_elementwise: binary op needs b");
   if (n == 0) return ANIMA_OK;
   elementwise_kernel<<<grid1(n, 256), 256, 0, ctx->stream>>>(op, a, b, y, n);
@@ -959,7 +1017,9 @@ int anima_elementwise(anima_ctx* ctx, int op, const float* a, const float* b, fl
 int anima_unpack_w4(anima_ctx* ctx, const uint8_t* packed, const uint8_t* s_rel, const float* codebook, int N, int K,
                     int8_t* out) {
   ANIMA_REQUIRE(ctx && packed && s_rel && codebook && out, "anima_unpack_w4: NULL argument");
+  ANIMA_ON_DEVICE(ctx);
   ANIMA_REQUIRE(N > 0 && K > 0 && K % 16 == 0, "anima_unpack_w4: K=%d must be a positive multiple of 16", K);
+  if (K % 32 == 0 && al16(packed) && al16(out)) return launch_w4_decode(ctx, packed, s_rel, codebook, N, K, out);
   const long long nb = static_cast<long long>(N) * K / 2;
   ProfScope prof(ctx, "unpack_w4", 0, nb * 3.0);
   unpack_w4_kernel<<<grid1(nb, 256), 256, 0, ctx->stream>>>(packed, s_rel, codebook, nb, K, out);
@@ -969,6 +1029,7 @@ int anima_unpack_w4(anima_ctx* ctx, const uint8_t* packed, const uint8_t* s_rel,
 int anima_matmul(anima_ctx* ctx, int M, int N, int K, float alpha, const float* A, int lda, const anima_weight* B,
                  int act, float* C, int ldc, int accumulate, const float* gate, int gate_off) {
   ANIMA_REQUIRE(ctx && A && B && B->data && C, "anima_matmul: NULL argument");
+  ANIMA_ON_DEVICE(ctx);
   ANIMA_REQUIRE(M > 0 && N > 0 && K > 0 && lda >= K && ldc >= N, "anima_matmul: bad shape");
   ANIMA_REQUIRE(B->kind == ANIMA_W_BF16 || B->kind == ANIMA_W_F32, "anima_matmul: weight kind %d (bf16 or f32 only)",
                 B->kind);
@@ -984,6 +1045,7 @@ int anima_matmul(anima_ctx* ctx, int M, int N, int K, float alpha, const float* 
 
 int anima_lora_down(anima_ctx* ctx, const anima_qact* x, const float* A, int r, float* T, int ldt) {
   ANIMA_REQUIRE(ctx && x && x->hi && x->scale && A && T && r > 0 && ldt >= r, "anima_lora_down: bad argument");
+  ANIMA_ON_DEVICE(ctx);
   ProfScope prof(ctx, "lora.down", 2.0 * x->rows * r * x->cols, 0);
   launch_simt<float, true>(ctx->stream, ctx->num_sms, x->rows, r, x->cols, 1.0f, nullptr, x->ld, A, x->cols, nullptr, 0, T,
                            ldt, 0, nullptr, 0, x->hi, x->lo, x->scale);
@@ -992,6 +1054,7 @@ int anima_lora_down(anima_ctx* ctx, const anima_qact* x, const float* A, int r, 
 
 int anima_patchify(anima_ctx* ctx, const float* latent, int B, int h, int w, float* patches) {
   ANIMA_REQUIRE(ctx && latent && patches && B > 0 && h > 0 && w > 0 && h % 2 == 0 && w % 2 == 0, "anima_patchify: bad argument");
+  ANIMA_ON_DEVICE(ctx);
   const long long n = static_cast<long long>(B) * (h / 2) * (w / 2) * 68;
   patchify_kernel<<<grid1(n, 256), 256, 0, ctx->stream>>>(latent, B, h, w, patches);
   return check_launch("patchify_kernel");
@@ -999,6 +1062,7 @@ int anima_patchify(anima_ctx* ctx, const float* latent, int B, int h, int w, flo
 
 int anima_unpatchify(anima_ctx* ctx, const float* o, int B, int h, int w, float* latent) {
   ANIMA_REQUIRE(ctx && o && latent && B > 0 && h > 0 && w > 0 && h % 2 == 0 && w % 2 == 0, "anima_unpatchify: bad argument");
+  ANIMA_ON_DEVICE(ctx);
   const long long n = static_cast<long long>(B) * 16 * h * w;
   unpatchify_kernel<<<grid1(n, 256), 256, 0, ctx->stream>>>(o, B, h, w, latent);
   return check_launch("unpatchify_kernel");
@@ -1006,6 +1070,7 @@ int anima_unpatchify(anima_ctx* ctx, const float* o, int B, int h, int w, float*
 
 int anima_timestep_embedding(anima_ctx* ctx, const float* sigmas, int B, float* temb) {
   ANIMA_REQUIRE(ctx && sigmas && temb && B > 0, "anima_timestep_embedding: bad argument");
+  ANIMA_ON_DEVICE(ctx);
   timestep_embedding_kernel<<<grid1(B * 1024LL, 256), 256, 0, ctx->stream>>>(sigmas, B, temb);
   return check_launch("timestep_embedding_kernel");
 }
@@ -1013,6 +1078,7 @@ int anima_timestep_embedding(anima_ctx* ctx, const float* sigmas, int B, float* 
 int anima_euler_step(anima_ctx* ctx, float* x, const float* v, const float* v_uncond, float cfg, float sigma,
                      float sigma_next, long long n, float* den_out) {
   ANIMA_REQUIRE(ctx && x && v && n > 0 && sigma > 0.f, "anima_euler_step: bad argument");
+  ANIMA_ON_DEVICE(ctx);
   euler_kernel<<<grid1(n, 256), 256, 0, ctx->stream>>>(x, v, v_uncond, cfg, sigma, sigma_next, n, den_out);
   return check_launch("euler_kernel");
 }

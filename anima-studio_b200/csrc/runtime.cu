@@ -7,7 +7,9 @@
 #include <cstring>
 #include <map>
 #include <mutex>
+#include <set>
 #include <string>
+#include <utility>
 #include <vector>
 
 #include "internal.h"
@@ -80,6 +82,40 @@ int make_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void*
   return ANIMA_OK;
 }
 
+// ------------------------------------------------------------------ devices
+
+DeviceScope::DeviceScope(const anima_ctx* ctx) {
+  int cur = 0;
+  cudaError_t e = cudaGetDevice(&cur);
+  if (e != cudaSuccess) {
+    status = check_cuda(e, "cudaGetDevice");
+    return;
+  }
+  if (cur == ctx->device) return;
+  e = cudaSetDevice(ctx->device);
+  if (e != cudaSuccess) {
+    status = check_cuda(e, "cudaSetDevice (the context's device)");
+    return;
+  }
+  prev = cur;
+}
+
+DeviceScope::~DeviceScope() {
+  if (prev >= 0) cudaSetDevice(prev);
+}
+
+int set_max_dynamic_smem(const void* fn, int bytes) {
+  int dev = 0;
+  ANIMA_CUDA(cudaGetDevice(&dev));
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count({fn, dev})) return ANIMA_OK;
+  ANIMA_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  done.insert({fn, dev});
+  return ANIMA_OK;
+}
+
 // ------------------------------------------------------------------ profiler
 
 struct ProfEntry {
@@ -142,7 +178,9 @@ int anima_ctx_create(int device, anima_ctx** out) {
   int n = 0;
   ANIMA_CUDA(cudaGetDeviceCount(&n));
   ANIMA_REQUIRE(device >= 0 && device < n, "anima_ctx_create: device %d out of range (%d devices)", device, n);
-  ANIMA_CUDA(cudaSetDevice(device));
+  anima_ctx probe;
+  probe.device = device;
+  ANIMA_ON_DEVICE(&probe);  // the caller's current device is left as it was
   cudaDeviceProp prop;
   ANIMA_CUDA(cudaGetDeviceProperties(&prop, device));
   if (prop.major != 10)
@@ -162,12 +200,14 @@ int anima_ctx_create(int device, anima_ctx** out) {
 
 int anima_ctx_destroy(anima_ctx* ctx) {
   if (!ctx) return ANIMA_OK;
+  ANIMA_ON_DEVICE(ctx);
   if (ctx->prof) {
     prof_collect(ctx);
     delete static_cast<ProfileState*>(ctx->prof);
   }
   if (ctx->attn_ws) cudaFree(ctx->attn_ws);
   if (ctx->attn_flags) cudaFree(ctx->attn_flags);
+  if (ctx->w4_ws) cudaFree(ctx->w4_ws);
   delete ctx;
   return ANIMA_OK;
 }
@@ -187,6 +227,7 @@ int anima_ctx_set_attention_split(anima_ctx* ctx, int mode) {
 
 int anima_sync(anima_ctx* ctx) {
   ANIMA_REQUIRE(ctx, "anima_sync: ctx is NULL");
+  ANIMA_ON_DEVICE(ctx);  // the error word and the flags below are this device's
   ANIMA_CUDA(cudaStreamSynchronize(ctx->stream));
   unsigned err = 0, zero = 0;
   ANIMA_CUDA(cudaMemcpyFromSymbol(&err, g_device_error, sizeof(err)));
@@ -232,6 +273,7 @@ __global__ void selftest_wait_kernel(unsigned long long timeout_ns, int* out) {
 int anima_selftest_wait_timeout(anima_ctx* ctx, unsigned timeout_us, int* result) {
   ANIMA_REQUIRE(ctx && result && timeout_us > 0 && timeout_us <= 2000000u,
                 "anima_selftest_wait_timeout: bad argument (timeout 1 us .. 2 s)");
+  ANIMA_ON_DEVICE(ctx);
   int* d = nullptr;
   ANIMA_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&d), 2 * sizeof(int), ctx->stream));
   selftest_wait_kernel<<<1, 32, 0, ctx->stream>>>(1000ull * timeout_us, d);
@@ -245,36 +287,42 @@ int anima_selftest_wait_timeout(anima_ctx* ctx, unsigned timeout_us, int* result
 
 int anima_alloc(anima_ctx* ctx, size_t bytes, void** out) {
   ANIMA_REQUIRE(ctx && out, "anima_alloc: NULL argument");
+  ANIMA_ON_DEVICE(ctx);
   ANIMA_CUDA(cudaMallocAsync(out, bytes ? bytes : 16, ctx->stream));
   return ANIMA_OK;
 }
 
 int anima_free(anima_ctx* ctx, void* ptr) {
   ANIMA_REQUIRE(ctx, "anima_free: ctx is NULL");
+  ANIMA_ON_DEVICE(ctx);
   if (ptr) ANIMA_CUDA(cudaFreeAsync(ptr, ctx->stream));
   return ANIMA_OK;
 }
 
 int anima_upload(anima_ctx* ctx, void* dst, const void* src, size_t bytes) {
   ANIMA_REQUIRE(ctx && dst && src, "anima_upload: NULL argument");
+  ANIMA_ON_DEVICE(ctx);
   ANIMA_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, ctx->stream));
   return ANIMA_OK;
 }
 
 int anima_download(anima_ctx* ctx, void* dst, const void* src, size_t bytes) {
   ANIMA_REQUIRE(ctx && dst && src, "anima_download: NULL argument");
+  ANIMA_ON_DEVICE(ctx);
   ANIMA_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, ctx->stream));
   return ANIMA_OK;
 }
 
 int anima_zero(anima_ctx* ctx, void* p, size_t bytes) {
   ANIMA_REQUIRE(ctx && p, "anima_zero: NULL argument");
+  ANIMA_ON_DEVICE(ctx);
   ANIMA_CUDA(cudaMemsetAsync(p, 0, bytes, ctx->stream));
   return ANIMA_OK;
 }
 
 int anima_profile_report(anima_ctx* ctx, char* buf, size_t cap) {
   ANIMA_REQUIRE(ctx && buf && cap > 0, "anima_profile_report: NULL argument");
+  ANIMA_ON_DEVICE(ctx);
   std::string s;
   if (!ctx->profile) {
     s = "profiling disabled (set ANIMA_PROFILE=1 before creating the context)\n";

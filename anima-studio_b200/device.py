@@ -206,7 +206,8 @@ class Context:
         check(self.lib.anima_ctx_set_stream(self.h, C.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)))
         return self.h
 
-    def call(self, name: str, *args, tag: str | None = None, work: float = 0.0):
+    def call(self, name: str, *args, tag: str | None = None, work: float = 0.0, kernels: int = 1):
+        """Run entry point `name` on torch's current stream; `kernels` = library kernels it enqueues."""
         h = self.bind_stream()
         kt = KernelTimer.active
         if kt is not None and name in kt.names:
@@ -218,7 +219,7 @@ class Context:
         else:
             check(getattr(self.lib, name)(h, *args))
         if name in LAUNCHING:
-            Context.launches += 1
+            Context.launches += kernels
 
     def sync(self):
         """gpu.sync: wait for the stream and raise on a device-side fault or timed-out wait."""

@@ -210,7 +210,8 @@ def linear(x, W, *, out: torch.Tensor | None = None, resid: bool = False, gate: 
     o.eps = eps
     qa = x.c()
     w = W.c()
-    ctx_for(x.hi).call("anima_linear", C.byref(qa), C.byref(w), C.byref(o), tag=name, work=2.0 * M * W.N * W.K)
+    ctx_for(x.hi).call("anima_linear", C.byref(qa), C.byref(w), C.byref(o), tag=name, work=2.0 * M * W.N * W.K,
+                       kernels=2 if W.kind == "w4" else 1)  # w4: the decode, then the GEMM
     del keep
     return out
 

@@ -8,7 +8,8 @@ reference ports from comfy_kitchen's eager backend (not vendored, no pinned vers
                               16, fp32 per-row scale, decoded on an int8 grid (quant.py:132-169)
 
 These run once, offline, to build weights for tests and benchmarks; they are not on the denoising
-path. tests/test_quant.py checks them bit for bit against the reference's outputs.
+path. tests/test_host.py checks them bit for bit against the reference's outputs (fixtures in
+tests/golden/ written by the reference's own quantizers).
 """
 
 from __future__ import annotations

@@ -87,7 +87,6 @@ def shard_rows(W: Linear, lo: int, hi: int) -> Linear:
                  W.bias[lo:hi].contiguous() if W.bias is not None else None,
                  name=W.name)
     if W.kind == "w4":
-        out.packed = W.packed[lo:hi].contiguous()
         out.s_rel = W.s_rel[lo:hi].contiguous()
         out.codebook = W.codebook
     return out
@@ -98,10 +97,9 @@ def shard_cols(W: Linear, lo: int, hi: int, keep_bias: bool) -> Linear:
     256-feature ConvRot groups; per-row scales stay those of the full rows."""
     if not (0 <= lo < hi <= W.K and lo % 256 == 0 and hi % 256 == 0):
         raise ValueError(f"{W.name}: columns [{lo}, {hi}) must be whole 256-groups inside K = {W.K}")
-    out = Linear(W.kind, W.N, hi - lo, W.data[:, lo:hi].contiguous(), W.scale,
-                 W.bias if keep_bias else None, name=W.name)
+    data = W.data[:, lo // 2:hi // 2] if W.kind == "w4" else W.data[:, lo:hi]  # w4: two codes a byte
+    out = Linear(W.kind, W.N, hi - lo, data.contiguous(), W.scale, W.bias if keep_bias else None, name=W.name)
     if W.kind == "w4":
-        out.packed = W.packed[:, lo // 2:hi // 2].contiguous()
         out.s_rel = W.s_rel[:, lo // 16:hi // 16].contiguous()
         out.codebook = W.codebook
     return out
@@ -122,7 +120,6 @@ def shard_stacked(W: Linear, tp: TPGroup, unit: int) -> Linear:
                  torch.cat([p.scale for p in pieces]).contiguous() if W.scale is not None else None,
                  None, name=W.name, parts=parts)
     if W.kind == "w4":
-        out.packed = torch.cat([p.packed for p in pieces], 0).contiguous()
         out.s_rel = torch.cat([p.s_rel for p in pieces], 0).contiguous()
         out.codebook = W.codebook
     return out

@@ -103,19 +103,41 @@ def setup_dist():
 
 # ----------------------------------------------------------------------------- reference arm (CPU)
 
-def run_reference(args, world, rank):
-    """The reference's algorithm (tools/reference.py, restated in numpy as oracle/) on the host
-    cores: each step is a bounded sample — one of the 28 blocks at L = 4096 — scaled to a full
-    denoising step (28 blocks)."""
-    if rank != 0:
-        return
+def host_threads():
+    """Threads for the CPU arms: every core this process may run on (torchrun sets
+    OMP_NUM_THREADS=1 for its ranks, which would otherwise throttle BLAS to one thread)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
+def blas_on_all_cores(cores):
+    """Lift the BLAS/OpenMP thread limits to `cores` whatever the environment says; returns the
+    threadpoolctl context (kept alive by the caller) or None."""
     import torch
 
+    torch.set_num_threads(cores)
+    try:
+        from threadpoolctl import threadpool_limits
+        return threadpool_limits(limits=cores)
+    except ImportError:
+        return None
+
+
+def run_reference(args, world, rank):
+    """The reference's algorithm (tools/reference.py, restated in numpy as oracle/) on the host
+    cores. A step of this arm is one bounded sample of the workload: one of the 28 DiT blocks at
+    L = 4096, so ms_per_step x steps is the timed region; `value` converts it to the metric's unit
+    (DiT denoising steps/s = 1 / (28 x block time)). Under torchrun only rank 0 runs (the host's
+    cores do the whole job whatever the GPU count); the other ranks exit without work."""
+    if rank != 0:
+        return
     import oracle
     from oracle import to_numpy as to_np
 
-    cores = os.cpu_count() or 1
-    torch.set_num_threads(cores)
+    cores = host_threads()
+    limits = blas_on_all_cores(cores)  # noqa: F841  (holds the thread limits for the run)
     syn = pkg("synthetic")
     seed, Hp = 1234, 64
     L = Hp * Hp
@@ -128,25 +150,25 @@ def run_reference(args, world, rank):
     cos, sin = oracle.dit_rope(Hp, Hp)
     cos, sin = np.concatenate([cos, cos], -1), np.concatenate([sin, sin], -1)
     times = []
-    t_start = time.perf_counter()
     for i in range(args.warmup + args.steps):
         t0 = time.perf_counter()
         oracle.dit_block(W, 0, x, ctx, emb, adaln_lora, cos, sin)
         times.append(time.perf_counter() - t0)
-        # keep the whole run within a few minutes: after 150 s, the steps timed so far stand for all
-        if i >= args.warmup and time.perf_counter() - t_start > 150.0:
-            break
-    timed = times[args.warmup:] or times[-1:]
-    block_s = statistics.mean(timed)
-    step_s = block_s * 28
-    v = 1.0 / step_s
+    timed = times[args.warmup:]
+    region_s = sum(timed)
+    block_s = region_s / len(timed)
+    v = 1.0 / (28 * block_s)
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "steps/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": block_s * 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "tokens": L, "blocks": 28},
+            "config": {"workload": WORKLOAD, "tokens": L, "blocks": 28,
+                       "step_of_this_arm": "one bounded sample: one DiT block at L=4096 (1/28 of a denoising step); "
+                                           "value = 1 / (28 x ms_per_step) denoising steps/s",
+                       "timed_region_s": region_s, "samples_timed": len(timed),
+                       "host": f"{cores} threads on the host's cores, rank 0 only"},
             "cpu_baseline": {"value": v, "unit": "steps/s", "cores": cores, "kind": "port",
-                             "sample": f"one DiT block at L=4096 per step ({block_s:.2f} s, {len(timed)} of "
-                                       f"{args.steps} steps timed), x28 blocks; numpy restatement of "
+                             "sample": f"{len(timed)} x one DiT block at L=4096 ({block_s:.2f} s each, "
+                                       f"{region_s:.1f} s timed), x28 blocks per denoising step; numpy restatement of "
                                        "tools/reference.py (fp32, BLAS threads = cores)"},
             "e2e": {"value": v, "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -156,12 +178,11 @@ def run_reference(args, world, rank):
 
 def cpu_baseline_sample(seconds_budget=25.0):
     """The oracle port timed on the host cores on a bounded sample (one block at L=4096)."""
-    import torch
-
     import oracle
     from oracle import to_numpy as to_np
 
-    cores = os.cpu_count() or 1
+    cores = host_threads()
+    limits = blas_on_all_cores(cores)  # noqa: F841
     syn = pkg("synthetic")
     seed, Hp = 1234, 64
     t = to_np(syn.global_tensors(seed))
@@ -462,6 +483,11 @@ def main():
     ap.add_argument("--res", type=int, default=1024, help="with --cfg: image side (1024 or 1536)")
     ap.add_argument("--tp", action="store_true",
                     help="single-image latency: heads sharded over the --gpus ranks, NCCL all-reduce per block")
+    ap.add_argument("--fmt", default="int8", choices=["int8", "mixed"],
+                    help="DiT weights: int8 (configs[2]) or W4A8 'mixed', blocks 2-27 W4A8 (configs[3])")
+    ap.add_argument("--lora", type=int, default=0,
+                    help="rank of a LoRA on q/k/v and both MLP linears of every block (configs[3]: 32); the "
+                         "line then also carries the step time without it (the LoRA overhead)")
     args = ap.parse_args()
     world, rank, local = setup_dist()
     if args.kernel:
@@ -483,22 +509,51 @@ def main():
     dev = pkg("device")
     syn, ditm, ops, pl = pkg("synthetic"), pkg("dit"), pkg("ops"), pkg("pipeline")
 
+    headline = args.fmt == "int8" and not args.lora
     cpu_base = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and headline:
         cpu_base = cpu_baseline_sample()  # before any CUDA work (keeps BLAS threads off the GPU feeder)
 
     seed = 1234
-    tensors = syn.dit_tensors(seed, "int8", 28, device="cuda")
+    # int8: Gaussian weights through the reference's int8 ConvRot quantizer (on the GPU); mixed: the
+    # stored formats drawn directly (W4 codes and fp8 group scales), the decode and GEMM cost the same
+    tensors = syn.dit_tensors(seed, args.fmt, 28, device="cuda", direct=args.fmt != "int8")
     dit = ditm.AnimaDiT(tensors, "cuda", precision=args.precision,
                         attn_dtype=torch.bfloat16 if args.attn == "bf16" else torch.float16)
     del tensors
     torch.cuda.empty_cache()
+    weight_bytes = sum(w.nbytes() for blk in dit.blocks for w in blk.values() if hasattr(w, "nbytes"))
     ctx = torch.cat([syn.randn(seed, "ctx", (256, 1024)), torch.zeros(256, 1024)]).cuda()
     cond = dit.prepare_context(ctx)
     sig = pl.sigmas_simple(8, 3.0)
     tcs = dit.time_cond_batch(sig[:-1])
     noise = syn.randn(seed + rank, "noise", (1, 16, 128, 128)).cuda()
     x = noise * sig[0]
+    lora_info = None
+    if args.lora:
+        # the same steps without the LoRA first (graphed), for the overhead the reference quotes
+        # (README.md:153: ~+20% per step)
+        g0 = pl.GraphedSampler(dit, cond, 8, 1, 128, 128)
+        g0.start(noise)
+        for i in range(3):
+            g0.replay(i)
+        torch.cuda.synchronize()
+        b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        b0.record()
+        for i in range(16):
+            g0.replay(i % 8)
+        b1.record()
+        torch.cuda.synchronize()
+        base_ms = b0.elapsed_time(b1) / 16
+        del g0
+        lora = pkg("lora")
+        targets = ("self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj", "mlp.layer1", "mlp.layer2")
+        lt = syn.lora_tensors(seed, targets, rank=args.lora, std=0.01, n_blocks=28, alpha=float(args.lora))
+        reg = lora.linear_registry(dit.blocks)
+        lo = lora.load_lora(lt, reg, device="cuda")
+        lora.attach_loras([reg], [(lo, 1.0)])
+        lora_info = {"rank": args.lora, "modules": lo.matched, "targets": list(targets),
+                     "ms_per_step_without_lora": base_ms}
     graphed = None
     if not args.no_graph:
         graphed = pl.GraphedSampler(dit, cond, 8, 1, 128, 128)
@@ -631,10 +686,22 @@ def main():
                     "launching stream in an instrumented replay of the timed steps; a16 runs two int8 MMAs per "
                     "product, so hw_ops_frac = planes x frac; traffic = DRAM bytes per launch from the ncu capture "
                     "in profiles/gemm_i8_mlp1_L4096.md"}
-    line = {"metric": METRIC, "value": value, "unit": "steps/s", "n_gpus": world, "steps": args.steps,
+    metric, workload = METRIC, WORKLOAD
+    if not headline:
+        metric = ("DiT denoise steps/sec at 1024^2 (4096 tokens), 28-block W4A8-mixed ConvRot DiT"
+                  + (f" + rank-{args.lora} LoRA" if args.lora else ""))
+        workload = ("BASELINE configs[3]: W4A8 'mixed' DiT (blocks 1 and 28 INT8, blocks 2-27 4-bit codes with fp8 "
+                    "group scales, decoded per linear into the int8 GEMM), ConvRot, 1024x1024, batch 1 per GPU, "
+                    "Euler steps, context 256x1024 zero-padded to 512 rows"
+                    + (f"; rank-{args.lora} LoRA (A, B ~ N(0, 0.01)) on q/k/v and both MLP linears of every block"
+                       if args.lora else ""))
+    if lora_info:
+        lora_info["overhead"] = (ms_max / args.steps) / lora_info["ms_per_step_without_lora"] - 1.0
+    line = {"metric": metric, "value": value, "unit": "steps/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "tokens": 4096, "blocks": 28, "batch_per_gpu": 1,
+            "config": {"workload": workload, "fmt": args.fmt, "lora": lora_info,
+                       "block_weight_bytes": weight_bytes, "tokens": 4096, "blocks": 28, "batch_per_gpu": 1,
                        "launch": "CUDA graph per step" if graphed is not None else "eager",
                        "precision": args.precision, "attention": args.attn, "ctx_rows": 512,
                        "parallelism": f"dp{world}", "images_per_s": value / 8,

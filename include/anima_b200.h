@@ -11,6 +11,9 @@
  *     app/gpu/device.js:170-216); device-side faults and timeouts surface at anima_sync(), as the
  *     reference surfaces WebGPU validation errors at read/sync (device.js:224-231).
  *   - A context is owned by one host thread at a time (the reference's single worker thread).
+ *   - Every call runs on its context's device, whatever device the calling thread has current, and
+ *     leaves the thread's current device as it found it; one thread may drive contexts on several
+ *     GPUs in turn. The context's stream must belong to its device.
  */
 #ifndef ANIMA_B200_H
 #define ANIMA_B200_H
@@ -152,7 +155,12 @@ int anima_unpack_w4(anima_ctx* ctx, const uint8_t* packed, const uint8_t* s_rel,
 
 /* ---------------------------------------------------------------- operators (ops.js) */
 /* ops.linear (ops.js:48-66) for ConvRot weights: tcgen05 kind::i8 GEMM of the quantized rows x
- * with W (kind I8; W4 must be unpacked with anima_unpack_w4 first), fused epilogue. */
+ * with W, fused epilogue. W of kind I8 is used as stored. W of kind W4 (the reference's "w4" path,
+ * app/gpu/gemm.js:141-158) stays packed in memory (0.5 byte per weight plus the fp8 group scales);
+ * each call first decodes it to its int8 grid (the arithmetic of anima_unpack_w4, so the result is
+ * bit-identical to unpacking once and passing kind I8) into a buffer the context owns (16 MiB or
+ * the layer's N*K bytes, allocated on the first W4 call and grown outside stream capture only),
+ * then runs the same GEMM on it. */
 int anima_linear(anima_ctx* ctx, const anima_qact* x, const anima_weight* W, const anima_linear_opts* o);
 
 /* runMatmul for "bf16"/"f32" weights (ops.js:14-33, gemm.js:81-127): C = epi(alpha A B^T),
@@ -193,7 +201,13 @@ int anima_qk_norm_rope(anima_ctx* ctx, void* qkv, int dtype, int L, int H, int D
 int anima_rope(anima_ctx* ctx, void* x, int dtype, int L, int H, int D, int row_stride, int col_off,
                const float* rope, int rope_rows);
 /* ops.attention (ops.js:166-208, kernels.js:147-299): non-causal multi-head attention, tcgen05
- * flash kernel, fp32 softmax. head_dim must be 128. */
+ * flash kernel, fp32 softmax. head_dim must be 128.
+ * The stream-K schedule (see anima_ctx_set_attention_split) launches one CTA per SM and lets a CTA
+ * wait, bounded at 2 s, for a partial result written by a lower-numbered CTA; it therefore needs
+ * all of the device's SMs to be available to this kernel at once. Where other work can hold SMs
+ * for long (MPS clients, green contexts, a long kernel on a concurrent stream), a wait can run out
+ * and the call then reports ANIMA_ERR_DEVICE at anima_sync; set the split mode to 0 (whole units,
+ * no waits between CTAs) on such hosts. */
 int anima_attention(anima_ctx* ctx, const anima_attention_args* a);
 /* anima_attention for callers that cannot call cudaMalloc (no reference counterpart): hosts whose
  * device memory belongs to another allocator or pool, or that must not allocate once running.

@@ -4,7 +4,10 @@ Runs only where the reference checkout exists (it imports tools/quant.py and too
 from REF: --ref, or the ANIMA_REFERENCE environment variable). Inputs come from the package's
 seeded synthetic generator, so the tests can rebuild identical inputs without the reference. Usage:
 
-    python tests/golden/make_golden.py --ref /path/to/anima-studio
+    python tests/golden/make_golden.py --ref /path/to/anima-studio [--only small|full]
+
+The full-size fixtures (--only full: 28 blocks at 1024^2, eleven reference forwards) take about
+ten minutes on 8 CPU cores and ~20 GB of host memory.
 """
 
 from __future__ import annotations
@@ -47,34 +50,137 @@ def np_of(d):
 
 class RefWeights:
     """Duck-typed tools/reference.py Weights over an in-memory comfy_quant dict; block tensors are
-    built on first access (one block at a time) to bound memory."""
+    built on first access (one block at a time) to bound memory. cache=True keeps every block and
+    its dequantized weights instead (many full-size forwards over the same checkpoint): the values
+    are the same as dequantizing on every access, as the reference's Weights does."""
 
-    def __init__(self, quant, make_block, globals_):
+    def __init__(self, quant, make_block, globals_, cache=False):
         self.quant = quant
         self.make_block = make_block
         self.t = dict(globals_)
         self.block = None
+        self.cache = cache
+        self.built = set()
+        self.deq = {}
+        self.prefix = ""
+        self.keys = _KeyView(self)
 
     def _ensure(self, name):
         if name.startswith("blocks."):
             i = int(name.split(".")[1])
-            if self.block != i:
+            if self.cache:
+                if i not in self.built:
+                    self.t.update(self.make_block(i))
+                    self.built.add(i)
+            elif self.block != i:
                 self.t = {k: v for k, v in self.t.items() if not k.startswith("blocks.")}
                 self.t.update(self.make_block(i))
                 self.block = i
 
     def __call__(self, name):
+        if name in self.deq:
+            return self.deq[name]
         self._ensure(name)
         base = name[: -len("weight")] if name.endswith("weight") else None
         if base is not None and base + "comfy_quant" in self.t:
             t = {s: self.t[base + s] for s in ("weight", "weight_scale", "weight_s_rel", "weight_s_channel", "weight_codebook", "comfy_quant") if base + s in self.t}
-            return self.quant.dequantize(t)
-        return self.t[name].float()
+            w = self.quant.dequantize(t)
+        else:
+            w = self.t[name].float()
+        if self.cache:
+            self.deq[name] = w
+        return w
+
+    def has(self, name):
+        self._ensure(name)
+        return name in self.t
+
+
+class _KeyView:
+    """`name in W.keys` for the reference's LoraMerged (it copies base.keys)."""
+
+    def __init__(self, w):
+        self.w = w
+
+    def __contains__(self, name):
+        return self.w.has(name)
+
+
+def full_size_fixtures(quant, R, syn):
+    """BASELINE's headline configuration and its two neighbours at full size (1024^2: a 128x128
+    latent, L = 4096 tokens), run through the reference's own dit_forward, Euler loop, CFG combine
+    (tools/reference.py:194-249, 345-360) and LoraMerged (tools/reference.py:51-90). Each fixture
+    keeps the velocity of the first pass, the final latent, and every 32nd token row of the residual
+    stream after block 0 (128 of 4096 rows, to bound the file); the tests rebuild the noise from its
+    seed with the reference's generator (torch_cpu_noise) and the weights from their seeds."""
+    import tempfile
+
+    from safetensors.torch import save_file
+
+    rows = slice(0, 4096, 32)
+    pad = torch.zeros(256, 1024)
+
+    # (a) the headline: 28 INT8 ConvRot blocks, 8 Euler steps (sigmas_simple(8, 3)), no CFG
+    seed = 41
+    Wf = RefWeights(quant, lambda i: syn.block_tensors(seed, i, "int8", 28, direct=True), syn.global_tensors(seed),
+                    cache=True)
+    ctx = torch.cat([syn.randn(seed, "golden.ctx", (256, 1024)), pad])
+    noise = R.torch_cpu_noise(seed, (1, 16, 1, 128, 128))[0, :, 0]
+    sig = R.sigmas_simple(8, 3.0)
+    xx = noise * sig[0]
+    dump, v0 = {}, None
+    for i in range(8):
+        s = sig[i]
+        v = R.dit_forward(Wf, xx, s, ctx, dump if i == 0 else None)
+        if i == 0:
+            v0 = v.clone()
+        den = xx - v * s
+        xx = den if sig[i + 1] == 0 else xx + (xx - den) / s * (sig[i + 1] - s)
+        print(f"headline step {i + 1}/8", flush=True)
+    np.savez_compressed(os.path.join(HERE, "forward_int8_1024.npz"), seed=seed, noise_sum=np.float64(noise.double().sum()),
+                        velocity0=v0.numpy(), latent_final=xx.numpy(),
+                        dit_block0_rows=dump["dit_block0"][rows].numpy(), rows_step=32)
+
+    # (b) CFG: the base model's 30-step schedule, first step, cfg 4.5 with a negative context
+    ctx_neg = torch.cat([syn.randn(seed, "golden.ctx_neg", (256, 1024)), pad])
+    sig30 = R.sigmas_simple(30, 3.0)
+    x0 = noise * sig30[0]
+    v = R.dit_forward(Wf, x0, sig30[0], ctx)
+    vn = R.dit_forward(Wf, x0, sig30[0], ctx_neg)
+    vg = vn + (v - vn) * 4.5
+    den = x0 - vg * sig30[0]
+    x1 = x0 + (x0 - den) / sig30[0] * (sig30[1] - sig30[0])
+    np.savez_compressed(os.path.join(HERE, "cfg_int8_1024.npz"), seed=seed, cfg=4.5, velocity_guided=vg.numpy(),
+                        latent_step1=x1.numpy())
+    print("cfg done", flush=True)
+    del Wf
+
+    # (c) W4A8 "mixed" (blocks 1..26 W4A8) + rank-32 LoRA on q/k/v and the MLP, one step
+    seed = 43
+    targets = ("self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj", "mlp.layer1", "mlp.layer2")
+    lt = syn.lora_tensors(seed, targets, rank=32, std=0.01, n_blocks=28, alpha=16.0)
+    base = RefWeights(quant, lambda i: syn.block_tensors(seed, i, "mixed", 28, direct=True), syn.global_tensors(seed),
+                      cache=True)
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "lora.safetensors")
+        save_file({k: v.contiguous() for k, v in lt.items()}, path)
+        Wm = R.LoraMerged(base, [(path, 0.9)])
+        ctx = torch.cat([syn.randn(seed, "golden.ctx", (256, 1024)), pad])
+        noise = R.torch_cpu_noise(seed, (1, 16, 1, 128, 128))[0, :, 0]
+        sig = R.sigmas_simple(8, 3.0)
+        dump = {}
+        v = R.dit_forward(Wm, noise * sig[0], sig[0], ctx, dump)
+    np.savez_compressed(os.path.join(HERE, "forward_mixed_lora_1024.npz"), seed=seed, strength=0.9, alpha=16.0,
+                        noise_sum=np.float64(noise.double().sum()), velocity0=v.numpy(),
+                        dit_block0_rows=dump["dit_block0"][rows].numpy(), rows_step=32)
+    print("mixed + LoRA done", flush=True)
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("ANIMA_REFERENCE"))
+    ap.add_argument("--only", choices=["small", "full"], default=None,
+                    help="small: sections 1-5 (L = 64 and the quantizers); full: the 1024^2 fixtures")
     args = ap.parse_args()
     if not args.ref:
         ap.error("give the reference checkout with --ref or ANIMA_REFERENCE")
@@ -82,6 +188,9 @@ def main():
     sys.path.insert(0, ROOT)
     syn = importlib.import_module("anima-studio_b200.synthetic")
     torch.set_grad_enabled(False)
+    if args.only == "full":
+        full_size_fixtures(quant, R, syn)
+        return
 
     # 1. int8 ConvRot quantizer + dequantizer (tools/quant.py:59-67, 81-83)
     w = syn.randn(1, "golden.int8", (64, 512), "cpu", 0.02)
@@ -187,6 +296,8 @@ def main():
         np.savez_compressed(os.path.join(HERE, f"forward_{fmt}_16x16.npz"), seed=seed, noise=noise.numpy(),
                             velocity0=v0.numpy(), latent_final=xx.numpy(), **{k: t.numpy() for k, t in dump.items()})
         print("forward", fmt, "done", flush=True)
+    if args.only is None:
+        full_size_fixtures(quant, R, syn)
     print("golden fixtures written to", HERE)
 
 
