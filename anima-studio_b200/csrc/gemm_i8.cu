@@ -79,9 +79,10 @@ struct Cfg {
   static constexpr int B_BYTES = BN * BK;
   static constexpr int STAGE_BYTES = NPLANES * A_BYTES + B_BYTES;
   static constexpr int STAGING_BYTES = 8 * 2 * 32 * 128;  // 8 epilogue warps x 2 x 4 KB
-  // LoRA: one [LORA_R, BN] fp32 slice of scale * B^T per epilogue warpgroup
-  static constexpr int LORA_BYTES = LORA ? 2 * LORA_R * BN * 4 : 0;
-  static constexpr int STAGES = (216 * 1024 - STAGING_BYTES - LORA_BYTES) / STAGE_BYTES;
+  // LoRA: one [LORA_R, BN] fp16 slice of scale * B^T per epilogue warpgroup (fp16 keeps three
+  // pipeline stages within the 227 KB a CTA may hold)
+  static constexpr int LORA_BYTES = LORA ? 2 * LORA_R * BN * 2 : 0;
+  static constexpr int STAGES = ((LORA ? 224 : 216) * 1024 - STAGING_BYTES - LORA_BYTES) / STAGE_BYTES;
   static constexpr int ACC_COLS = NPLANES * BN;
   // one accumulator buffer per epilogue warpgroup when two fit in TMEM, else one (the second
   // epilogue warpgroup then idles and the epilogue of a tile delays the next tile's MMAs)
@@ -128,14 +129,15 @@ __device__ __forceinline__ void issue_cols(uint32_t taddr, int col, uint32_t (&r
   if constexpr (NPLANES == 2) tmem_ldc<CH>(taddr + BN + col, rl);
 }
 
-// LoRA: v[j] += sum_i t[m, r0 + i] * bt[i, col + j], with this tile's slice of scale * B^T staged
-// in shared memory (bt_s [r][BN], read as 16-byte broadcasts: every lane of the warp works on the
-// same columns of a different row) and t = x_r A^T read from global memory (one row per lane, L1
-// resident across the tile's pieces). The products run as paired fp32 FMAs.
+// LoRA: v[j] += sum_i t[i] * bt[i, col + j]. The tile's slice of scale * B^T sits in shared memory
+// as fp16 (bt_s [r][BN], read as 16-byte broadcasts: every lane of the warp works on the same
+// columns of a different row) and converts to fp32 for paired fp32 FMAs; t = row m of x_r A^T (the
+// two partial products summed) is loaded once per tile and held in registers as fp16 pairs. The
+// side path's products thus carry fp16 operands (relative rounding 2^-11) with fp32 sums; the
+// LoRA delta is a small part of the output, so this adds ~1e-4 of it at most.
 struct LoraTile {
-  const float* bt_s;  // nullptr: no LoRA entry covers this tile
-  const float* t;     // row m of T at the entry's first rank
-  int t_lo;           // column offset of the second partial product of T (0: none)
+  const __half* bt_s;  // nullptr: no LoRA entry covers this tile
+  __half2 t[LORA_R / 2];
   int r;
 };
 
@@ -144,26 +146,24 @@ __device__ __forceinline__ void lora_cols(const LoraTile& lt, int col, float (&v
   f2 acc[CH / 2];
 #pragma unroll
   for (int j = 0; j < CH / 2; ++j) acc[j] = dup2(0.f);
-#pragma unroll 2
-  for (int i = 0; i < lt.r; i += 4) {
-    float4 t4 = __ldg(reinterpret_cast<const float4*>(lt.t + i));
-    if (lt.t_lo) {
-      const float4 l4 = __ldg(reinterpret_cast<const float4*>(lt.t + lt.t_lo + i));
-      t4.x += l4.x;
-      t4.y += l4.y;
-      t4.z += l4.z;
-      t4.w += l4.w;
-    }
-    const float tv[4] = {t4.x, t4.y, t4.z, t4.w};
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const float4* row = reinterpret_cast<const float4*>(lt.bt_s + (i + u) * BN + col);
-      const f2 tt = dup2(tv[u]);
+  for (int i4 = 0; i4 < LORA_R; i4 += 4) {
+    if (i4 < lt.r) {
 #pragma unroll
-      for (int q = 0; q < CH / 4; ++q) {
-        const float4 b = row[q];
-        acc[2 * q] = fma2(tt, make_float2(b.x, b.y), acc[2 * q]);
-        acc[2 * q + 1] = fma2(tt, make_float2(b.z, b.w), acc[2 * q + 1]);
+      for (int u = 0; u < 4; ++u) {
+        const uint4* row = reinterpret_cast<const uint4*>(lt.bt_s + (i4 + u) * BN + col);
+        const float2 tp = __half22float2(lt.t[(i4 + u) / 2]);
+        const f2 tt = dup2((u & 1) ? tp.y : tp.x);
+#pragma unroll
+        for (int q = 0; q < CH / 8; ++q) {
+          const uint4 b = row[q];
+          const uint32_t w[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 bf = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
+            acc[4 * q + e] = fma2(tt, bf, acc[4 * q + e]);
+          }
+        }
       }
     }
   }
@@ -300,14 +300,16 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap
     // software pipeline over 16-column pieces: the TMEM loads of piece c+1 are in flight while
     // piece c is finished and staged
     const bool resid = p.out_mode == ANIMA_OUT_RESID;
-    uint32_t rh[2][CH], rl[2][CH];
+    constexpr int PIPE = 2;
+    uint32_t rh[PIPE][CH], rl[PIPE][CH];
     issue_cols<BN, NPLANES, CH>(taddr, 0, rh[0], rl[0]);
     tmem_ld_wait(rh[0]);
     if constexpr (NPLANES == 2) tmem_ld_wait(rl[0]);
 #pragma unroll
     for (int c = 0; c < BN / CH; ++c) {
-      const int cur = c & 1;
-      if (c + 1 < BN / CH) issue_cols<BN, NPLANES, CH>(taddr, CH * (c + 1), rh[cur ^ 1], rl[cur ^ 1]);
+      const int cur = PIPE == 2 ? (c & 1) : 0;
+      if (PIPE == 2 && c + 1 < BN / CH)
+        issue_cols<BN, NPLANES, CH>(taddr, CH * (c + 1), rh[(cur + 1) % PIPE], rl[(cur + 1) % PIPE]);
       const int col = CH * c;
       const int chunk = col / chc, q = (col % chc) / CH;
       uint8_t* buf = stage + (chunk & 1) * STAGE_BUF;
@@ -324,9 +326,9 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap
       }
       stage_piece(buf, lane, p.out_dtype, q, v);
       if (q == ppc - 1) stage_flush(tm_out, buf, n0 + chunk * chc, y0, resid);
-      if (c + 1 < BN / CH) {
-        tmem_ld_wait(rh[cur ^ 1]);
-        if constexpr (NPLANES == 2) tmem_ld_wait(rl[cur ^ 1]);
+      if (PIPE == 2 && c + 1 < BN / CH) {
+        tmem_ld_wait(rh[(cur + 1) % PIPE]);
+        if constexpr (NPLANES == 2) tmem_ld_wait(rl[(cur + 1) % PIPE]);
       }
     }
     return;
@@ -452,7 +454,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* staging = smem + C::STAGES * C::STAGE_BYTES;  // 1024-aligned (stage sizes are)
-  float* lora_smem = reinterpret_cast<float*>(staging + C::STAGING_BYTES);
+  __half* lora_smem = reinterpret_cast<__half*>(staging + C::STAGING_BYTES);
   uint64_t* full = reinterpret_cast<uint64_t*>(staging + C::STAGING_BYTES + C::LORA_BYTES);
   uint64_t* empty = full + C::STAGES;
   uint64_t* acc_full = empty + C::STAGES;
@@ -598,7 +600,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       int mb, nb;
       tile_coords(p, tile, mb, nb);
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + buf * C::ACC_COLS;
-      LoraTile lt{nullptr, nullptr, 0, 0};
+      LoraTile lt;
+      lt.bt_s = nullptr;
+      lt.r = 0;
       if constexpr (LORA) {
         // the entry covering this tile (entries are BN-aligned): stage its slice of scale * B^T
         const int n0 = nb * BN;
@@ -606,17 +610,42 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int i = 0; i < p.lora_count; ++i)
           if (n0 >= p.lora_off[i] && n0 < p.lora_off[i] + p.lora_n[i]) e = i;
         if (e >= 0) {
-          float* bt_s = lora_smem + g * LORA_R * BN;
+          __half* bt_s = lora_smem + g * LORA_R * BN;
           const int r = p.lora_r[e];
           const int tid = threadIdx.x - g * 128;
-          for (int k = tid; k < r * BN / 4; k += 128) {
-            const int i = k / (BN / 4), c4 = k % (BN / 4);
-            reinterpret_cast<float4*>(bt_s)[k] =
-                __ldg(reinterpret_cast<const float4*>(p.lora_bt + static_cast<size_t>(p.lora_r0[e] + i) * p.ld_bt + n0) + c4);
+          for (int k = tid; k < r * BN / 8; k += 128) {  // 8 columns per step: two loads, one store
+            const int i = k / (BN / 8), c8 = k % (BN / 8);
+            const float4* src =
+                reinterpret_cast<const float4*>(p.lora_bt + static_cast<size_t>(p.lora_r0[e] + i) * p.ld_bt + n0) + 2 * c8;
+            const float4 a = __ldg(src), b = __ldg(src + 1);
+            const __half2 h0 = __floats2half2_rn(a.x, a.y), h1 = __floats2half2_rn(a.z, a.w);
+            const __half2 h2 = __floats2half2_rn(b.x, b.y), h3 = __floats2half2_rn(b.z, b.w);
+            reinterpret_cast<uint4*>(bt_s)[k] =
+                make_uint4(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1),
+                           *reinterpret_cast<const uint32_t*>(&h2), *reinterpret_cast<const uint32_t*>(&h3));
+          }
+          // this row's x_r A^T for the entry's ranks, both partial products summed, into registers
+          const int m = mb * BM + row;
+          const float* tr = p.lora_t + static_cast<size_t>(m < p.M ? m : 0) * p.ld_t + p.lora_r0[e];
+#pragma unroll
+          for (int i4 = 0; i4 < LORA_R; i4 += 4) {
+            float4 t4 = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (i4 < r) {
+              t4 = __ldg(reinterpret_cast<const float4*>(tr + i4));
+              if (p.lora_t_lo) {
+                const float4 l4 = __ldg(reinterpret_cast<const float4*>(tr + p.lora_t_lo + i4));
+                t4.x += l4.x;
+                t4.y += l4.y;
+                t4.z += l4.z;
+                t4.w += l4.w;
+              }
+            }
+            lt.t[i4 / 2] = __floats2half2_rn(t4.x, t4.y);
+            lt.t[i4 / 2 + 1] = __floats2half2_rn(t4.z, t4.w);
           }
           wg_sync_and(g, true);
-          const int m = mb * BM + row;
-          lt = LoraTile{bt_s, p.lora_t + static_cast<size_t>(m < p.M ? m : 0) * p.ld_t + p.lora_r0[e], p.lora_t_lo, r};
+          lt.bt_s = bt_s;
+          lt.r = r;
         }
       }
       epilogue_tile<BN, NPLANES, LORA>(p, &tm_out, staging + warp * 2 * STAGE_BUF, taddr, mb * BM + row,

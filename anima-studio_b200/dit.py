@@ -152,6 +152,20 @@ class AnimaDiT:
         self._rope = {}
         self._bufs = {}
 
+    @classmethod
+    def from_file(cls, path: str, device="cuda", prefix: str = "model.diffusion_model.", **kw) -> "AnimaDiT":
+        """A DiT from a comfy_quant safetensors checkpoint (SafeTensors.open + AnimaDiT.load,
+        app/weights.js:29-41, app/models/dit.js:80-129); tensors stream from the mapped file to
+        the device one by one."""
+        from .checkpoint import open_dit
+
+        tensors = open_dit(path, prefix)
+        try:
+            return cls(tensors, device, **kw)
+        finally:
+            tensors.release()
+            tensors.st.close()
+
     # ------------------------------------------------------------------ time conditioning
 
     def time_cond_batch(self, sigmas) -> list[TimeCond]:

@@ -522,7 +522,8 @@ def main():
                         attn_dtype=torch.bfloat16 if args.attn == "bf16" else torch.float16)
     del tensors
     torch.cuda.empty_cache()
-    weight_bytes = sum(w.nbytes() for blk in dit.blocks for w in blk.values() if hasattr(w, "nbytes"))
+    Linear = pkg("weights").Linear
+    weight_bytes = sum(w.nbytes() for blk in dit.blocks for w in blk.values() if isinstance(w, Linear))
     ctx = torch.cat([syn.randn(seed, "ctx", (256, 1024)), torch.zeros(256, 1024)]).cuda()
     cond = dit.prepare_context(ctx)
     sig = pl.sigmas_simple(8, 3.0)

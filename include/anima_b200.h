@@ -98,7 +98,8 @@ typedef struct {
      int8 planes). lora_t [M, ld_t] holds x_r A^T of all entries stacked (or anima_lora_down's
      result); lora_bt [R, ld_bt] holds scale_e * B_e^T in the entry's columns (only those are read).
      Entries: off and n multiples of 128, r a multiple of 4 and at most 32, at most 4 entries;
-     lora_t NULL = none. */
+     lora_t NULL = none. The epilogue multiplies fp16 copies of t and lora_bt with fp32 sums
+     (the delta is a small part of y; it adds ~2^-11 of the delta). */
   const float* lora_t;
   int ld_t;
   int lora_t_lo;

@@ -281,7 +281,13 @@ def _lora_ref(qa, entries, N):
                                        ([(0, 2048, 32, 1.0), (2048, 2048, 32, 1.0)], "qkv"),
                                        ([(0, 6144, 6, 1.0)], "store")])
 def test_linear_lora_epilogue(ops, spec, mode):
+    """The fused side path multiplies fp16 copies of x_r A^T and scale * B^T (fp32 sums), so the
+    output carries ~2^-11 of the LoRA delta (a few % of y here) on top of the base GEMM's fp32
+    rounding: 3e-5 of the output where the base path alone is held to 2e-6. The [M, N] delta
+    fallback (rank 6) stays fp32."""
     M, K = 260, 2048
+    fused = all(r % 4 == 0 for (_, _, r, _) in spec)
+    tol = 3e-5 if fused else 2e-6
     N = 6144 if mode in ("store", "qkv") else 2048
     lin, wq, ws = make_linear(N, K, 8)
     lin.lora = [{k: v for k, v in e.items() if not k.endswith("_np")} for e in _lora_entries(K, spec, 50)]
@@ -290,13 +296,14 @@ def test_linear_lora_epilogue(ops, spec, mode):
     y = gemm_ref(qa, wq, ws) + _lora_ref(qa, ents, N)
     if mode == "store":
         out = ops.linear(qa, lin, act="gelu").cpu().numpy()
-        assert rel_l2(out, oracle.gelu(y.astype(np.float32))) < 2e-6
+        assert rel_l2(out, oracle.gelu(y.astype(np.float32))) < tol
     elif mode == "resid":
         x0 = randn((M, N), 34)
         mod = randn((6144,), 35, 0.5)
         out = x0.clone().to(DEV)
         ops.linear(qa, lin, out=out, resid=True, gate=mod.to(DEV), g_off=4096)
-        assert rel_l2(out.cpu().numpy(), x0.numpy() + mod[4096:].numpy() * y) < 1e-6
+        ref = x0.numpy() + mod[4096:].numpy() * y
+        assert rel_l2(out.cpu().numpy() - x0.numpy(), ref - x0.numpy()) < tol
     else:
         Hp, Wp = 10, 26
         qn, kn = 1 + randn((128,), 36, 0.1), 1 + randn((128,), 37, 0.1)
@@ -309,7 +316,7 @@ def test_linear_lora_epilogue(ops, spec, mode):
         sin = np.concatenate([sin, sin], -1)[:, None]
         q = oracle.rms_norm(yf[:, :2048].reshape(M, 16, 128), qn.numpy())
         q = q * cos + oracle.rotate_half(q) * sin
-        assert rel_l2(out[:, :2048], q.reshape(M, -1)) < 2e-6
+        assert rel_l2(out[:, :2048], q.reshape(M, -1)) < tol
         assert rel_l2(out[:, 4096:], yf[:, 4096:]) < 1e-6
 
 
