@@ -95,14 +95,13 @@ class AnimaDiT:
     """Weights resident on one GPU plus the forward pass (app/models/dit.js:80-129, 253-325)."""
 
     def __init__(self, tensors: dict, device="cuda", precision: str = "a16", attn_dtype=torch.float16,
-                 n_blocks: int | None = None, tp=None):
-        """tp: a sharding.TPGroup to hold only this rank's heads / MLP features (tensor parallelism);
-        every rank of the group then runs forward() on the same inputs."""
+                 n_blocks: int | None = None, seq=None):
+        """seq: a sharding.SeqGroup to split every image's token rows over its ranks (sequence
+        parallelism, the single-image latency mode); every rank holds all weights, calls forward()
+        with the same inputs and gets the same velocity."""
         if precision not in ("a16", "a8"):
             raise ValueError("precision must be 'a16' (two int8 planes) or 'a8' (W8A8)")
-        self.tp = tp if tp is not None and tp.world > 1 else None
-        world = self.tp.world if self.tp else 1
-        self.heads_local, self.d_local, self.mlp_local = HEADS // world, D // world, MLP // world
+        self.seq = seq if seq is not None and seq.world > 1 else None
         self.device = torch.device(device)
         self.planes = 2 if precision == "a16" else 1
         self.precision = precision
@@ -134,9 +133,6 @@ class AnimaDiT:
                 "cross_kn": vector(tensors, p + "cross_attn.k_norm.weight", dv),
                 "l1": lin(p + "mlp.layer1."), "l2": lin(p + "mlp.layer2."),
             }
-            if self.tp:
-                from .sharding import shard_block
-                blk = shard_block(blk, self.tp, HD)
             for m in ("adaln_modulation_self_attn", "adaln_modulation_cross_attn", "adaln_modulation_mlp"):
                 mod_w1.append(tensors[p + m + ".1.weight"])
                 mod_w2.append(lin(p + m + ".2."))
@@ -151,6 +147,13 @@ class AnimaDiT:
         self.final_linear = lin("final_layer.linear.")
         self._rope = {}
         self._bufs = {}
+
+    def set_seq(self, seq) -> None:
+        """Switch sequence parallelism on (a sharding.SeqGroup with world > 1) or off (None) for
+        later forwards; the weights are the same either way."""
+        self.seq = seq if seq is not None and seq.world > 1 else None
+        self._bufs = {}
+        self._rope = {}
 
     @classmethod
     def from_file(cls, path: str, device="cuda", prefix: str = "model.diffusion_model.", **kw) -> "AnimaDiT":
@@ -201,14 +204,13 @@ class AnimaDiT:
         c2 = ctx.reshape(B * Lk, CTX_DIM).to(self.device, torch.float32).contiguous()
         cq = ops.rotate_quant(c2, self.planes)
         ks, vs = [], []
-        Dl = self.d_local
         for blk in self.blocks:
-            k = torch.empty(B * Lk, Dl, dtype=self.attn_dtype, device=self.device)
-            v = torch.empty(B * Lk, Dl, dtype=self.attn_dtype, device=self.device)
+            k = torch.empty(B * Lk, D, dtype=self.attn_dtype, device=self.device)
+            v = torch.empty(B * Lk, D, dtype=self.attn_dtype, device=self.device)
             ops.linear(cq, blk["cross_k"], out=k, mode="head_norm", qk=(blk["cross_kn"],))
             ops.linear(cq, blk["cross_v"], out=v)
-            ks.append(k.view(B, Lk, Dl))
-            vs.append(v.view(B, Lk, Dl))
+            ks.append(k.view(B, Lk, D))
+            vs.append(v.view(B, Lk, D))
         kl = None
         if key_len is not None:
             kl = torch.as_tensor(key_len, dtype=torch.int32).reshape(-1).to(self.device)
@@ -218,72 +220,86 @@ class AnimaDiT:
 
     # ------------------------------------------------------------------ forward
 
-    def rope(self, Hp: int, Wp: int) -> torch.Tensor:
-        key = (Hp, Wp)
+    def rope(self, Hp: int, Wp: int, rows: tuple[int, int] | None = None) -> torch.Tensor:
+        """cos then sin of the RoPE table for an Hp x Wp patch grid; rows = (lo, hi) keeps only
+        those token rows (a sequence-parallel rank's slice), as [hi - lo, 64] cos then sin."""
+        key = (Hp, Wp, rows)
         if key not in self._rope:
-            self._rope[key] = torch.from_numpy(rope_table(Hp, Wp)).to(self.device)
+            t = rope_table(Hp, Wp)
+            if rows is not None:
+                L = Hp * Wp
+                t = np.concatenate([t[rows[0]:rows[1]], t[L + rows[0]:L + rows[1]]], 0)
+            self._rope[key] = torch.from_numpy(np.ascontiguousarray(t)).to(self.device)
         return self._rope[key]
 
-    def _buffers(self, M: int):
-        b = self._bufs.get(M)
+    def _buffers(self, M: int, B: int = 1):
+        """Activations of one forward over M = B x (local) L rows, reused across calls."""
+        b = self._bufs.get((M, B))
         if b is None:
             dv = self.device
-            Dl, Fl = self.d_local, self.mlp_local
             b = {
                 "qa": ops.QuantRows.empty(M, D, self.planes, dv),
-                "qo": ops.QuantRows.empty(M, Dl, self.planes, dv) if self.tp else None,
-                "qh": ops.QuantRows.empty(M, Fl, self.planes, dv),
-                "qkv": torch.empty(M, 3 * Dl, dtype=self.attn_dtype, device=dv),
-                "o": torch.empty(M, Dl, dtype=self.attn_dtype, device=dv),
-                "q": torch.empty(M, Dl, dtype=self.attn_dtype, device=dv),
-                "h": torch.empty(M, Fl, dtype=torch.float16, device=dv),
+                "qh": ops.QuantRows.empty(M, MLP, self.planes, dv),
+                "qkv": torch.empty(M, 3 * D, dtype=self.attn_dtype, device=dv),
+                "o": torch.empty(M, D, dtype=self.attn_dtype, device=dv),
+                "q": torch.empty(M, D, dtype=self.attn_dtype, device=dv),
+                "h": torch.empty(M, MLP, dtype=torch.float16, device=dv),
             }
-            self._bufs = {M: b}
+            if self.seq:
+                Lr = M // B
+                # this rank's k|v rows, then every rank's, per image: [B, world * Lr, 4096]
+                b["kv_mine"] = torch.empty(B, Lr, 2 * D, dtype=self.attn_dtype, device=dv)
+                b["kv_all"] = torch.empty(B, self.seq.world * Lr, 2 * D, dtype=self.attn_dtype, device=dv)
+            self._bufs = {(M, B): b}
         return b
 
     def block(self, i: int, x: torch.Tensor, cond: Cond, tc: TimeCond, B: int, L: int, cs: torch.Tensor,
               bufs: dict):
         """One transformer block, in place on x [B L, 2048] (dit.js:261-314)."""
+        """One transformer block, in place on x [B L, 2048] (dit.js:261-314). With sequence
+        parallelism x, L and cs are this rank's rows; self-attention gathers k|v of all rows."""
         blk = self.blocks[i]
-        if self.tp and any(blk[k].lora for k in ("qkv", "self_o", "cross_q", "cross_o", "l1", "l2")):
-            raise NotImplementedError("LoRA side paths are not supported with tensor parallelism")
         m_self, m_cross, m_mlp = tc.block(i)
         qa, qh = bufs["qa"], bufs["qh"]
-        qo = bufs["qo"] if self.tp else qa   # rotated attention output (this rank's heads)
-        H, Dl = self.heads_local, self.d_local
         # self-attention
         ops.layernorm_mod_quant(x, m_self, 0, D, D, out=qa)
         qkv = ops.linear(qa, blk["qkv"], out=bufs["qkv"], mode="qkv", qk=(blk["self_qn"], blk["self_kn"]),
-                         rope_cs=cs, n_q=Dl, name="dit.self.qkv")
-        a = ops.attention(qkv, qkv, qkv, Lq=L, Lk=L, H=H, D=HD, ldq=3 * Dl, ldk=3 * Dl, ldv=3 * Dl, q_off=0,
-                          k_off=Dl, v_off=2 * Dl, batch=B, q_bstride=L * 3 * Dl, k_bstride=L * 3 * Dl,
-                          v_bstride=L * 3 * Dl, out=bufs["o"], name="attn.self")
-        ops.rotate_quant(a, out=qo)
-        self._row_parallel(qo, blk["self_o"], x, m_self, "dit.self.out")
+                         rope_cs=cs, n_q=D, name="dit.self.qkv")
+        if self.seq:
+            kv = self._gather_kv(qkv, B, L, bufs)
+            Lk = kv.shape[1]
+            a = ops.attention(qkv, kv, kv, Lq=L, Lk=Lk, H=HEADS, D=HD, ldq=3 * D, ldk=2 * D, ldv=2 * D, q_off=0,
+                              k_off=0, v_off=D, batch=B, q_bstride=L * 3 * D, k_bstride=Lk * 2 * D,
+                              v_bstride=Lk * 2 * D, out=bufs["o"], name="attn.self")
+        else:
+            a = ops.attention(qkv, qkv, qkv, Lq=L, Lk=L, H=HEADS, D=HD, ldq=3 * D, ldk=3 * D, ldv=3 * D, q_off=0,
+                              k_off=D, v_off=2 * D, batch=B, q_bstride=L * 3 * D, k_bstride=L * 3 * D,
+                              v_bstride=L * 3 * D, out=bufs["o"], name="attn.self")
+        ops.rotate_quant(a, out=qa)
+        ops.linear(qa, blk["self_o"], out=x, resid=True, gate=m_self, g_off=2 * D, name="dit.self.out")
         # cross-attention against the per-prompt keys/values
         ops.layernorm_mod_quant(x, m_cross, 0, D, D, out=qa)
         q = ops.linear(qa, blk["cross_q"], out=bufs["q"], mode="head_norm", qk=(blk["cross_qn"],), name="dit.cross.q")
-        kb = cond.Lk * Dl if cond.batch == B else 0
-        a = ops.attention(q, cond.k[i], cond.v[i], Lq=L, Lk=cond.Lk, H=H, D=HD, batch=B, q_bstride=L * Dl,
+        kb = cond.Lk * D if cond.batch == B else 0
+        a = ops.attention(q, cond.k[i], cond.v[i], Lq=L, Lk=cond.Lk, H=HEADS, D=HD, batch=B, q_bstride=L * D,
                           k_bstride=kb, v_bstride=kb, key_len=cond.key_len, out=bufs["o"], name="attn.cross")
-        ops.rotate_quant(a, out=qo)
-        self._row_parallel(qo, blk["cross_o"], x, m_cross, "dit.cross.out")
+        ops.rotate_quant(a, out=qa)
+        ops.linear(qa, blk["cross_o"], out=x, resid=True, gate=m_cross, g_off=2 * D, name="dit.cross.out")
         # MLP
         ops.layernorm_mod_quant(x, m_mlp, 0, D, D, out=qa)
         # layer1 stores its pre-activation (fp16); GELU runs in the memory-bound ConvRot+quant pass
         h = ops.linear(qa, blk["l1"], out=bufs["h"], name="dit.mlp1")
         ops.rotate_quant(h, out=qh, act="gelu")
-        self._row_parallel(qh, blk["l2"], x, m_mlp, "dit.mlp2")
+        ops.linear(qh, blk["l2"], out=x, resid=True, gate=m_mlp, g_off=2 * D, name="dit.mlp2")
 
-    def _row_parallel(self, xq, W, x: torch.Tensor, gate: torch.Tensor, name: str):
-        """x += gate[2D:] * (xq W^T + bias): the gated-residual GEMM. Under tensor parallelism W
-        holds this rank's input features; ranks other than 0 accumulate into a zeroed x, and the
-        all-reduce sums the partial products onto every rank's copy."""
-        if self.tp and self.tp.rank != 0:
-            x.zero_()
-        ops.linear(xq, W, out=x, resid=True, gate=gate, g_off=2 * D, name=name)
-        if self.tp:
-            self.tp.all_reduce(x)
+    def _gather_kv(self, qkv: torch.Tensor, B: int, L: int, bufs: dict) -> torch.Tensor:
+        """k|v of this rank's rows (columns 2048.. of the qkv output) gathered from every rank, per
+        image, in global row order: [B, world * L, 4096]."""
+        mine, allkv = bufs["kv_mine"], bufs["kv_all"]
+        mine.copy_(qkv.view(B, L, 3 * D)[:, :, D:])
+        for b in range(B):
+            self.seq.all_gather(allkv[b], mine[b])
+        return allkv
 
     def forward(self, latent: torch.Tensor, cond: Cond, tc: TimeCond, on_block=None) -> torch.Tensor:
         """Velocity [B, 16, h, w] for latents [B, 16, h, w] on the device (dit.js:253-325)."""
@@ -292,14 +308,23 @@ class AnimaDiT:
         B, C, h, w = latent.shape
         Hp, Wp = h // 2, w // 2
         L = Hp * Wp
-        M = B * L
-        x = ops.matmul(ops.patchify(latent.contiguous()), self.x_embed)   # [M, 2048] fp32 residual stream
-        cs = self.rope(Hp, Wp)
-        bufs = self._buffers(M)
+        patches = ops.patchify(latent.contiguous())                      # [B L, 68]
+        rows = None
+        if self.seq:
+            rows = self.seq.span(L)
+            L = rows[1] - rows[0]                                          # this rank's rows of each image
+            patches = patches.view(B, Hp * Wp, 68)[:, rows[0]:rows[1]].reshape(B * L, 68)
+        x = ops.matmul(patches, self.x_embed)                              # [B L, 2048] fp32 residual stream
+        cs = self.rope(Hp, Wp, rows)
+        bufs = self._buffers(B * L, B)
         for i in range(self.n_blocks):
             self.block(i, x, cond, tc, B, L, cs, bufs)
             if on_block is not None:
                 on_block(i, x)
         n = ops.layernorm_mod(x, tc.final, 0, D, D)
-        o = ops.matmul(n, self.final_linear)                              # [M, 64] "(p1 p2 c)"
+        o = ops.matmul(n, self.final_linear)                              # [B L, 64] "(p1 p2 c)"
+        if self.seq:
+            parts = torch.empty(self.seq.world, B * L, 64, dtype=o.dtype, device=o.device)
+            self.seq.all_gather(parts, o)
+            o = parts.view(self.seq.world, B, L, 64).transpose(0, 1).reshape(B * Hp * Wp, 64)
         return ops.unpatchify(o, B, h, w)

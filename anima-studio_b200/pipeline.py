@@ -191,7 +191,8 @@ class GraphedSampler:
     the number of library kernels its capture enqueued to device.Context.launches."""
 
     def __init__(self, dit: AnimaDiT, cond: Cond, steps: int, batch: int, h: int, w: int, cfg: float = 1.0,
-                 uncond: Cond | None = None, shift: float = 3.0):
+                 uncond: Cond | None = None, shift: float = 3.0, capture: int | None = None):
+        """capture: graph only the first `capture` steps (a benchmark that replays those), else all."""
         self.dit, self.steps = dit, steps
         self.sig = sigmas_simple(steps, shift)
         self.tcs = dit.time_cond_batch(self.sig[:-1])
@@ -211,7 +212,7 @@ class GraphedSampler:
         self.x.zero_()
         self.launches = []  # library kernels in each captured step
         from .device import Context
-        for i in range(steps):
+        for i in range(steps if capture is None else min(capture, steps)):
             g = torch.cuda.CUDAGraph()
             n0 = Context.launches
             with torch.cuda.graph(g, pool=self.pool, stream=stream):
@@ -220,6 +221,9 @@ class GraphedSampler:
             self.pool = g.pool()
             self.graphs.append(g)
         torch.cuda.synchronize(dit.device)
+        # the graphs read and write the model's activation buffers by address: keep them alive even
+        # if the model later runs another shape (which replaces its buffer set)
+        self._keep = list(dit._bufs.values())
 
     def _step(self, i: int):
         s, s1 = self.sig[i], self.sig[i + 1]
@@ -240,6 +244,8 @@ class GraphedSampler:
         Context.launches += self.launches[i]
 
     def run(self, noise: torch.Tensor) -> torch.Tensor:
+        if len(self.graphs) != self.steps:
+            raise RuntimeError("run() needs every step captured (capture=None)")
         self.start(noise)
         for g in self.graphs:
             g.replay()

@@ -328,135 +328,176 @@ def kernel_case(args):
                       "ms_min": min(ts), "rate": rate, "unit": unit, "reps": args.reps}), flush=True)
 
 
-def run_tp(args, world, rank, local):
-    """One image denoised by all ranks together (head-sharded tensor parallelism): the latency
-    mode. Eager launches (the per-block all-reduces stay outside CUDA graphs)."""
-    import torch
-    import torch.distributed as dist
-    from datetime import timedelta
-
-    torch.cuda.set_device(local)
+def _barrier(world):
     if world > 1:
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
-    syn, ditm, ops, pl, sh = pkg("synthetic"), pkg("dit"), pkg("ops"), pkg("pipeline"), pkg("sharding")
-    seed = 1234
-    tensors = syn.dit_tensors(seed, "int8", 28, device="cuda")
-    dit = ditm.AnimaDiT(tensors, "cuda", precision=args.precision,
-                        attn_dtype=torch.bfloat16 if args.attn == "bf16" else torch.float16,
-                        tp=sh.TPGroup(rank, world, None))
-    del tensors
-    torch.cuda.empty_cache()
-    ctx = torch.cat([syn.randn(seed, "ctx", (256, 1024)), torch.zeros(256, 1024)]).cuda()
-    cond = dit.prepare_context(ctx)
-    sig = pl.sigmas_simple(8, 3.0)
-    tcs = dit.time_cond_batch(sig[:-1])
-    noise = syn.randn(seed, "noise", (1, 16, 128, 128)).cuda()   # the same image on every rank
-    x = noise * sig[0]
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def time_graphed(gs, noise, steps, warmup, world):
+    """Replay a GraphedSampler's captured steps in order (restarting from the noise after the last
+    one): `warmup` untimed steps, then `steps` timed with CUDA events on the replay stream between
+    device synchronizations and barriers; returns the max over ranks in ms."""
+    import torch
+
+    sh = pkg("sharding")
+    n = len(gs.graphs)
+    gs.start(noise)
 
     def step(i):
-        j = i % 8
-        v = dit.forward(x, cond, tcs[j])
-        ops.euler_step(x, v, sig[j], sig[j + 1])
-        if j == 7:
-            x.copy_(noise * sig[0])
+        j = i % n
+        gs.replay(j)
+        if j == n - 1:
+            gs.start(noise)
 
-    for i in range(args.warmup):
+    for i in range(warmup):
         step(i)
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    clocks = ClockSampler(local)
+    _barrier(world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for i in range(args.steps):
-        step(args.warmup + i)
+    for i in range(steps):
+        step(warmup + i)
     e1.record()
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    clk = clocks.stop()
-    ms = sh.max_over_ranks(e0.elapsed_time(e1), "cuda")
-    if world > 1:
-        dist.destroy_process_group()
-    if rank != 0:
-        return
-    line = {"metric": "DiT denoise steps/sec at 1024^2 (4096 tokens) for one image, head-sharded tensor parallel",
-            "value": args.steps / (ms * 1e-3), "unit": "steps/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": {"workload": "BASELINE configs[4] latency run: one 1024x1024 image, 28 INT8 ConvRot blocks, "
-                                   "16 heads and the 8192 MLP features split over the ranks, 3 NCCL all-reduces "
-                                   "of the fp32 residual stream per block", "parallelism": f"tp{world}",
-                       "launch": "eager", "precision": args.precision, "attention": args.attn},
-            "clocks": clk}
-    print(json.dumps(line), flush=True)
+    _barrier(world)
+    return sh.max_over_ranks(e0.elapsed_time(e1), "cuda")
 
 
-def run_cfg(args, world, rank, local):
-    """the base model with classifier-free guidance (cond + negative context
-    as one batch of 2 per image), Euler, 30 steps per image at 1024^2 or 1536^2; images (seeds) are
-    split over the ranks with no collective on the data path (weak scaling)."""
+def step_profile(dit, fn, peaks):
+    """One eager pass of fn() with CUDA events around every linear and attention launch: ms and
+    achieved rate per op family (int8 TOPS for the linears, TFLOP/s for attention)."""
+    dev = pkg("device")
+    with dev.KernelTimer({"anima_linear", "anima_attention"}) as kt:
+        fn()
+    summ = kt.summary()
+    out = {}
+    for name, unit in (("anima_linear", "TOPS"), ("anima_attention", "TFLOP/s")):
+        ms = sum(v[1] for k, v in summ.items() if k[0] == name)
+        work = sum(v[2] for k, v in summ.items() if k[0] == name)
+        rate = work / (ms * 1e-3) / 1e12 if ms else None
+        out[name.replace("anima_", "")] = {"ms": ms, "rate": rate, "unit": unit}
+    if out["attention"]["rate"] and peaks.get("bf16_tflops"):
+        out["attention"]["frac_of_bf16_peak"] = out["attention"]["rate"] / peaks["bf16_tflops"]
+    return out
+
+
+def measure_cfg(dit, seed, res, cfg, steps, warmup, world, rank, peaks, int8_peak=None):
+    """BASELINE configs[4] on this model: classifier-free guidance (cond and a negative context as
+    one batch of 2 per image), Euler over the base model's 30-step schedule, res x res; each rank
+    denoises its own image (its first seed of the 64), no collective on the data path."""
     import torch
-    import torch.distributed as dist
-    from datetime import timedelta
 
-    torch.cuda.set_device(local)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
-    syn, ditm, pl, sh = pkg("synthetic"), pkg("dit"), pkg("pipeline"), pkg("sharding")
-    seed, steps_per_image = 1234, 30
-    lat = args.res // 8
-    tensors = syn.dit_tensors(seed, "int8", 28, device="cuda")
+    syn, pl = pkg("synthetic"), pkg("pipeline")
+    lat = res // 8
+    pad = torch.zeros(256, 1024)
+    cond = dit.prepare_context(torch.cat([syn.randn(seed, "ctx", (256, 1024)), pad]).cuda())
+    uncond = dit.prepare_context(torch.cat([syn.randn(seed, "ctx_neg", (256, 1024)), pad]).cuda())
+    image = pkg("sharding").seed_shard(64, rank, world)[0] if world <= 64 else rank
+    noise = syn.randn(seed + image, "noise", (1, 16, lat, lat)).cuda()
+    gs = pl.GraphedSampler(dit, cond, 30, 1, lat, lat, cfg=cfg, uncond=uncond, capture=min(8, 30))
+    ms = time_graphed(gs, noise, steps, warmup, world)
+    del gs
+    both = pkg("dit").Cond.stack([cond, uncond])
+    tc = dit.time_cond(pl.sigmas_simple(30, 3.0)[0])
+    x2 = torch.cat([noise, noise])
+    prof = step_profile(dit, lambda: dit.forward(x2, both, tc), peaks)
+    if int8_peak and prof["linear"]["rate"]:
+        prof["linear"]["frac_of_int8_peak"] = prof["linear"]["rate"] / int8_peak
+    steps_per_s = world * steps / (ms * 1e-3)
+    tokens = (lat // 2) ** 2
+    return {"res": res, "tokens": tokens, "rows_per_gemm": 2 * tokens, "cfg": cfg, "steps_per_image": 30,
+            "steps_per_s": steps_per_s, "images_per_s": steps_per_s / 30, "ms_per_step": ms / steps,
+            "steps_timed_per_rank": steps, "job": f"64 seeded images split over {world} rank(s); rate from "
+            f"{steps} timed steps per rank", "per_op": prof}
+
+
+def measure_seq(dit, seed, steps, warmup, world, rank):
+    """One image denoised by all ranks together: its 4096 token rows split over the ranks
+    (sequence parallelism, one k|v all-gather per block), Euler 8-step schedule, CUDA graph per
+    step with the all-gathers captured in it. Returns the single-image rate."""
+    import torch
+
+    syn, pl, sh = pkg("synthetic"), pkg("pipeline"), pkg("sharding")
+    dit.set_seq(sh.SeqGroup(rank, world, None))
+    try:
+        cond = dit.prepare_context(torch.cat([syn.randn(seed, "ctx", (256, 1024)), torch.zeros(256, 1024)]).cuda())
+        noise = syn.randn(seed, "noise", (1, 16, 128, 128)).cuda()   # the same image on every rank
+        gs = pl.GraphedSampler(dit, cond, 8, 1, 128, 128)
+        ms = time_graphed(gs, noise, steps, warmup, world)
+        del gs
+    finally:
+        dit.set_seq(None)
+    return {"workload": "one 1024x1024 image, 28 INT8 ConvRot blocks, token rows split over the ranks, one "
+                        "all-gather of k|v (fp16, 16 MiB) per block, CUDA graph per step", "n_gpus": world,
+            "steps_per_s": steps / (ms * 1e-3), "ms_per_step": ms / steps, "steps": steps, "scaling": "strong"}
+
+
+def load_model(args, seed, fmt="int8"):
+    import torch
+
+    syn, ditm = pkg("synthetic"), pkg("dit")
+    tensors = syn.dit_tensors(seed, fmt, 28, device="cuda", direct=fmt != "int8")
     dit = ditm.AnimaDiT(tensors, "cuda", precision=args.precision,
                         attn_dtype=torch.bfloat16 if args.attn == "bf16" else torch.float16)
     del tensors
     torch.cuda.empty_cache()
-    pad = torch.zeros(256, 1024)
-    cond = dit.prepare_context(torch.cat([syn.randn(seed, "ctx", (256, 1024)), pad]).cuda())
-    uncond = dit.prepare_context(torch.cat([syn.randn(seed, "ctx_neg", (256, 1024)), pad]).cuda())
-    image = sh.seed_shard(64, rank, world)[0] if world <= 64 else rank  # this rank's first seed of the 64
-    noise = syn.randn(seed + image, "noise", (1, 16, lat, lat)).cuda()
-    graphed = pl.GraphedSampler(dit, cond, steps_per_image, 1, lat, lat, cfg=args.cfg, uncond=uncond)
-    graphed.start(noise)
+    return dit
 
-    def step(i):
-        j = i % steps_per_image
-        graphed.replay(j)
-        if j == steps_per_image - 1:
-            graphed.start(noise)
 
-    for i in range(args.warmup):
-        step(i)
-    torch.cuda.synchronize()
+def init_dist(world, local):
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    torch.cuda.set_device(local)
     if world > 1:
-        dist.barrier()
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+
+
+def run_tp(args, world, rank, local):
+    """--tp: the single-image latency run alone (sequence parallel over the --gpus ranks)."""
+    import torch.distributed as dist
+
+    init_dist(world, local)
+    dit = load_model(args, 1234)
     clocks = ClockSampler(local)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for i in range(args.steps):
-        step(args.warmup + i)
-    e1.record()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
+    r = measure_seq(dit, 1234, args.steps, args.warmup, world, rank)
     clk = clocks.stop()
-    ms = sh.max_over_ranks(e0.elapsed_time(e1), "cuda")
-    del graphed
     if world > 1:
         dist.destroy_process_group()
     if rank != 0:
         return
-    value = world * args.steps / (ms * 1e-3)
-    tokens = (lat // 2) ** 2
-    line = {"metric": f"DiT denoise steps/sec with CFG (batch 2 per image) at {args.res}^2 ({tokens} tokens)",
-            "value": value, "unit": "steps/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "int8", "data": "synthetic",
+    line = {"metric": "DiT denoise steps/sec at 1024^2 (4096 tokens) for one image, sequence parallel",
+            "value": r["steps_per_s"], "unit": "steps/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": "BASELINE configs[4] latency run: " + r["workload"], "parallelism": f"sp{world}",
+                       "precision": args.precision, "attention": args.attn}, "clocks": clk}
+    print(json.dumps(line), flush=True)
+
+
+def run_cfg(args, world, rank, local):
+    """--cfg: the configs[4] CFG run alone at --res (seeds split over the ranks, weak scaling)."""
+    import torch.distributed as dist
+
+    init_dist(world, local)
+    dit = load_model(args, 1234)
+    peaks = load_peaks()
+    clocks = ClockSampler(local)
+    r = measure_cfg(dit, 1234, args.res, args.cfg, args.steps, args.warmup, world, rank, peaks)
+    clk = clocks.stop()
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {"metric": f"DiT denoise steps/sec with CFG (batch 2 per image) at {args.res}^2 ({r['tokens']} tokens)",
+            "value": r["steps_per_s"], "unit": "steps/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
             "config": {"workload": f"BASELINE configs[4]: base model, INT8 ConvRot, cfg {args.cfg} with a negative "
-                                   f"context (cond and uncond as one batch of 2), Euler {steps_per_image} steps per "
-                                   f"image, {args.res}x{args.res}, one image per GPU at a time (seeds split over "
-                                   "the ranks)", "tokens": tokens, "rows_per_gemm": 2 * tokens,
-                       "images_per_s": value / steps_per_image, "launch": "CUDA graph per step",
+                                   f"context (cond and uncond as one batch of 2), Euler 30 steps per image, "
+                                   f"{args.res}x{args.res}", **r, "launch": "CUDA graph per step",
                        "parallelism": f"dp{world}", "precision": args.precision, "attention": args.attn},
             "clocks": clk}
     print(json.dumps(line), flush=True)
@@ -482,7 +523,9 @@ def main():
                     help="BASELINE configs[4]: guidance scale with a negative context (batch 2 per image), 30 steps")
     ap.add_argument("--res", type=int, default=1024, help="with --cfg: image side (1024 or 1536)")
     ap.add_argument("--tp", action="store_true",
-                    help="single-image latency: heads sharded over the --gpus ranks, NCCL all-reduce per block")
+                    help="single-image latency alone: token rows split over the --gpus ranks (sequence parallel)")
+    ap.add_argument("--no-sub", action="store_true",
+                    help="skip the configs[4] measurements the default line carries (cfg; tp at N > 1)")
     ap.add_argument("--fmt", default="int8", choices=["int8", "mixed"],
                     help="DiT weights: int8 (configs[2]) or W4A8 'mixed', blocks 2-27 W4A8 (configs[3])")
     ap.add_argument("--lora", type=int, default=0,
@@ -644,10 +687,24 @@ def main():
                       "dit.js:256,322)"}
 
     peaks = load_peaks()
+    # BASELINE configs[4] on every run (all ranks, same order): the CFG sweep at 1024^2 and 1536^2
+    # (each rank its own image), and with more than one rank the single-image sequence-parallel run
+    subs = {}
+    if headline and not args.no_sub:
+        graphed = None  # the headline graphs are done; free their pool before the larger shapes
+        torch.cuda.empty_cache()
+        subs["cfg"] = [measure_cfg(dit, seed, res, 4.5, n, 3, world, rank, peaks)
+                       for res, n in ((1024, 12), (1536, 6))]
+        if world > 1:
+            subs["tp"] = measure_seq(dit, seed, 16, 3, world, rank)
     int8_peak = measure_int8_peak(torch) if rank == 0 else None
     dist.destroy_process_group() if world > 1 else None
     if rank != 0:
         return
+    for c in subs.get("cfg", []):
+        lin = c["per_op"]["linear"]
+        if int8_peak and lin["rate"]:
+            lin["frac_of_int8_peak"] = lin["rate"] / int8_peak
 
     # roofline of the dominant kernel: the int8 GEMM over all its launches in a step, and the
     # north star's 2048->8192 linear (mlp1) alone
@@ -707,7 +764,7 @@ def main():
                        "precision": args.precision, "attention": args.attn, "ctx_rows": 512,
                        "parallelism": f"dp{world}", "images_per_s": value / 8,
                        "l2": "inputs larger than L2: 1.5 GB of int8 weights stream through every step"},
-            "roofline": roof, "cpu_baseline": cpu_base, "e2e": e2e,
+            "roofline": roof, "cpu_baseline": cpu_base, "e2e": e2e, **subs,
             "gpu_launches": launches, "gpu_launches_per_step": launches / args.steps, "clocks": clk}
     print(json.dumps(line), flush=True)
 

@@ -1,9 +1,10 @@
-"""Multi-GPU partitioning logic on the CPU: data-parallel seed shards and timing reduction, and the
-head-sharded tensor-parallel weight split, exercised with world-size-2 `gloo` process groups.
+"""Multi-GPU partitioning logic on the CPU, with world-size-2 `gloo` process groups: data-parallel
+seed shards and timing reduction, and the sequence-parallel split of one image's token rows.
 
-The tensor-parallel checks run the oracle's fp32 math (dequantized ConvRot weights) on each rank's
-shard and sum the partial products with the same all-reduce the GPU path uses; the result must
-equal the unsharded product. The CUDA kernels themselves are covered by the GPU tests."""
+The sequence-parallel check runs the oracle's fp32 math (dequantized ConvRot weights) the way the
+GPU path splits it: each rank computes every row-local part of a DiT block on its own rows, and
+gathers k and v of all rows for self-attention with the same all-gather; its rows must equal the
+one-process block. The CUDA kernels themselves are covered by the GPU tests."""
 
 import os
 import socket
@@ -37,21 +38,6 @@ def _init(rank, world, port):
     return dist
 
 
-def _convrot_linear(seed, N, K, parts=None):
-    """An int8 ConvRot Linear (CPU tensors) and its dequantized fp32 weight."""
-    quant, W = pkg("quant"), pkg("weights")
-    g = torch.Generator().manual_seed(seed)
-    w = torch.randn(N, K, generator=g) * 0.02
-    t = quant.quantize_int8_convrot(w)
-    lin = W.Linear("i8", N, K, t["weight"].contiguous(), t["weight_scale"].reshape(-1).float().contiguous(),
-                   torch.randn(N, generator=g) * 0.1, name="lin")
-    if parts:
-        lin.parts = parts
-        lin.bias = None
-    deq = oracle.dequantize_int8_convrot(t["weight"].numpy(), t["weight_scale"].numpy())
-    return lin, deq
-
-
 def test_seed_shards_cover_every_item_once():
     sh = pkg("sharding")
     for n in (1, 7, 64):
@@ -62,21 +48,16 @@ def test_seed_shards_cover_every_item_once():
             assert max(sizes) - min(sizes) <= 1
 
 
-def test_shards_reassemble():
+def test_seq_spans():
     sh = pkg("sharding")
-    lin, _ = _convrot_linear(1, 512, 1024)
-    for world in (2, 4):
-        rows = [sh.shard_rows(lin, r * 512 // world, (r + 1) * 512 // world) for r in range(world)]
-        assert torch.equal(torch.cat([s.data for s in rows]), lin.data)
-        assert torch.equal(torch.cat([s.scale for s in rows]), lin.scale)
-        cols = [sh.shard_cols(lin, r * 1024 // world, (r + 1) * 1024 // world, keep_bias=r == 0) for r in range(world)]
-        assert torch.equal(torch.cat([s.data for s in cols], 1), lin.data)
-        assert all(torch.equal(s.scale, lin.scale) for s in cols)
-        assert cols[0].bias is not None and all(s.bias is None for s in cols[1:])
+    for world in (1, 2, 4, 8):
+        spans = [sh.SeqGroup(r, world).span(4096) for r in range(world)]
+        assert spans[0][0] == 0 and spans[-1][1] == 4096
+        assert all(spans[i][1] == spans[i + 1][0] for i in range(world - 1))
     with pytest.raises(ValueError):
-        sh.shard_cols(lin, 0, 100, keep_bias=True)  # not a whole ConvRot group
+        sh.SeqGroup(0, 3).span(4096)   # 4096 rows do not split three ways
     with pytest.raises(ValueError):
-        sh.TPGroup(0, 3).span(2048, 128)            # 16 heads do not split three ways
+        sh.SeqGroup(2, 2).span(64)
 
 
 def _dp_worker(rank, world, port):
@@ -95,37 +76,65 @@ def test_data_parallel_helpers_gloo():
     _spawn(_dp_worker)
 
 
-def _tp_worker(rank, world, port):
+def _seq_block(W, i, x, ctx, emb, adaln_lora, cos, sin, seq):
+    """oracle.dit_block with the token rows split over the ranks: x, cos, sin are this rank's rows;
+    self-attention's k and v are gathered from every rank in rank (= row) order."""
+    import torch.distributed as dist
+
+    O = oracle
+    p = f"blocks.{i}."
+    H, HD = 16, 128
+
+    def gather(t):
+        parts = [torch.empty_like(torch.from_numpy(t)) for _ in range(seq.world)]
+        dist.all_gather(parts, torch.from_numpy(np.ascontiguousarray(t)))
+        return torch.cat(parts).numpy()
+
+    L = x.shape[0]
+    sh, sc, g = O.block_mod(W, p + "adaln_modulation_self_attn", emb, adaln_lora)
+    n = O.layer_norm(x) * (1 + sc) + sh
+    a = p + "self_attn."
+    q = O.rms_norm((n @ W(a + "q_proj.weight").T).reshape(L, H, HD), W(a + "q_norm.weight")).transpose(1, 0, 2)
+    k = O.rms_norm((n @ W(a + "k_proj.weight").T).reshape(L, H, HD), W(a + "k_norm.weight")).transpose(1, 0, 2)
+    v = (n @ W(a + "v_proj.weight").T).reshape(L, H, HD).transpose(1, 0, 2)
+    q = q * cos + O.rotate_half(q) * sin
+    k = k * cos + O.rotate_half(k) * sin
+    k_all = gather(k.transpose(1, 0, 2).astype(np.float32)).transpose(1, 0, 2)
+    v_all = gather(v.transpose(1, 0, 2).astype(np.float32)).transpose(1, 0, 2)
+    o = O.attention(q, k_all, v_all).transpose(1, 0, 2).reshape(L, H * HD)
+    x = x + g * (o @ W(a + "output_proj.weight").T)
+    sh, sc, g = O.block_mod(W, p + "adaln_modulation_cross_attn", emb, adaln_lora)
+    n = O.layer_norm(x) * (1 + sc) + sh
+    from oracle import ref_np
+
+    x = x + g * ref_np._attn(W, p + "cross_attn.", n, ctx, cos, sin, False)
+    sh, sc, g = O.block_mod(W, p + "adaln_modulation_mlp", emb, adaln_lora)
+    n = O.layer_norm(x) * (1 + sc) + sh
+    return (x + g * (O.gelu(n @ W(p + "mlp.layer1.weight").T) @ W(p + "mlp.layer2.weight").T)).astype(np.float32)
+
+
+def _seq_worker(rank, world, port):
     dist = _init(rank, world, port)
-    sh = pkg("sharding")
-    tp = sh.TPGroup(rank, world, None)
-    rng = np.random.default_rng(7)
-    x = rng.standard_normal((33, 2048)).astype(np.float32)
-
-    # row-parallel (out-projection): input features split, partial products summed, bias once
-    lin, deq = _convrot_linear(3, 256, 2048)
-    lo, hi = tp.span(2048, 128)
-    shard = sh.shard_cols(lin, lo, hi, keep_bias=rank == 0)
-    part_deq = oracle.dequantize_int8_convrot(shard.data.numpy(), shard.scale.numpy())
-    y = x[:, lo:hi] @ part_deq.T
-    if shard.bias is not None:
-        y = y + shard.bias.numpy()
-    yt = tp.all_reduce(torch.from_numpy(np.ascontiguousarray(y)))
-    ref = x @ deq.T + lin.bias.numpy()
-    assert np.abs(yt.numpy() - ref).max() <= 1e-4 * np.abs(ref).max()
-
-    # column-parallel stacked q|k|v: each part cut to this rank's heads
-    qkv, deq3 = _convrot_linear(5, 3 * 512, 2048, parts=[("q", 0, 512), ("k", 512, 512), ("v", 1024, 512)])
-    s3 = sh.shard_stacked(qkv, tp, 128)
-    assert s3.N == 3 * 512 // world and [p[2] for p in s3.parts] == [512 // world] * 3
-    got = x @ oracle.dequantize_int8_convrot(s3.data.numpy(), s3.scale.numpy()).T
-    full = x @ deq3.T
-    h0, h1 = tp.span(512, 128)
-    want = np.concatenate([full[:, o + h0:o + h1] for o in (0, 512, 1024)], 1)
-    assert np.abs(got - want).max() <= 1e-5 * np.abs(want).max()
+    sh, syn = pkg("sharding"), pkg("synthetic")
+    seq = sh.SeqGroup(rank, world, None)
+    t = oracle.to_numpy(syn.global_tensors(3))
+    t.update(oracle.to_numpy(syn.block_tensors(3, 0, "int8", 28, direct=True)))
+    W = oracle.DequantWeights(t)
+    Hp, Wp = 4, 8
+    L = Hp * Wp
+    x = syn.randn(3, "x", (L, 2048)).numpy()
+    ctx = syn.randn(3, "ctx", (40, 1024)).numpy()
+    _, adaln_lora, emb = oracle.time_cond(W, 0.7)
+    cos, sin = oracle.dit_rope(Hp, Wp)
+    cos, sin = np.concatenate([cos, cos], -1), np.concatenate([sin, sin], -1)
+    full = oracle.dit_block(W, 0, x, ctx, emb, adaln_lora, cos, sin)
+    lo, hi = seq.span(L)
+    mine = _seq_block(W, 0, x[lo:hi], ctx, emb, adaln_lora, cos[lo:hi], sin[lo:hi], seq)
+    err = np.abs(mine - full[lo:hi]).max() / np.abs(full[lo:hi]).max()
+    assert err < 1e-5, err
     dist.destroy_process_group()
 
 
 @pytest.mark.parametrize("world", [2])
-def test_tensor_parallel_split_gloo(world):
-    _spawn(_tp_worker, world)
+def test_sequence_parallel_block_gloo(world):
+    _spawn(_seq_worker, world)

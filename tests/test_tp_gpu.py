@@ -1,6 +1,7 @@
-"""Head-sharded tensor parallelism on 2 GPUs (NCCL): the sharded forward must match the one-GPU
-forward of the same weights. Each rank quantizes its own slice of the attention output and the
-MLP hidden with its own per-token scale, so the two runs differ by quantization noise only."""
+"""Sequence parallelism on 2 GPUs (NCCL): one image's token rows split over the ranks, k|v gathered
+for self-attention. The split forward must match the one-GPU forward of the same weights (the
+same kernels on fewer rows; only the GEMM tiling of the row slices differs) and the reference's
+own 28-block forward + 2 Euler steps at a 16x16 latent (tests/golden/forward_int8_16x16.npz)."""
 
 import os
 import socket
@@ -10,7 +11,7 @@ import pytest
 import torch
 import torch.multiprocessing as mp
 
-from conftest import pkg
+from conftest import GOLDEN, pkg
 
 pytestmark = pytest.mark.gpu
 
@@ -32,31 +33,44 @@ def _worker(rank, world, port, out_path):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
                             device_id=torch.device("cuda", rank))
     syn, ditm, sh, pl = pkg("synthetic"), pkg("dit"), pkg("sharding"), pkg("pipeline")
-    tensors = syn.dit_tensors(31, "int8", 2)
-    ctx = syn.randn(31, "ctx", (77, 1024)).cuda()
-    noise = syn.randn(31, "noise", (1, 16, 32, 32)).cuda()
-    dit = ditm.AnimaDiT(tensors, "cuda", n_blocks=2, tp=sh.TPGroup(rank, world, None))
+    g = dict(np.load(os.path.join(GOLDEN, "forward_int8_16x16.npz")))
+    seed = int(g["seed"])
+    tensors = syn.dit_tensors(seed, "int8", 28, direct=True)
+    ctx = torch.cat([syn.randn(seed, "golden.ctx", (256, 1024)), torch.zeros(256, 1024)]).cuda()
+    noise = torch.from_numpy(g["noise"])[None].cuda()
+    dit = ditm.AnimaDiT(tensors, "cuda", seq=sh.SeqGroup(rank, world, None))
     cond = dit.prepare_context(ctx)
-    tc = dit.time_cond(0.8)
-    v_tp = dit.forward(noise * 0.8, cond, tc)
-    lat_tp = pl.denoise_loop(dit, noise, cond, 2)
+    sig = pl.sigmas_simple(2, 3.0)
+    x0 = (noise * np.float32(sig[0])).contiguous()
+    v_sp = dit.forward(x0, cond, dit.time_cond(sig[0]))
+    lat_sp = pl.denoise_loop(dit, noise, cond, 2)
+    # the graphed sampler with the all-gathers captured in its graphs
+    gs = pl.GraphedSampler(dit, cond, 2, 1, 16, 16)
+    lat_graph = gs.run(noise).clone()
+    del gs
     torch.cuda.synchronize()
     if rank == 0:
-        ref = ditm.AnimaDiT(tensors, "cuda", n_blocks=2)
-        cref = ref.prepare_context(ctx)
-        v_1 = ref.forward(noise * 0.8, cref, ref.time_cond(0.8))
-        lat_1 = pl.denoise_loop(ref, noise, cref, 2)
-        np.savez(out_path, v_tp=v_tp.cpu().numpy(), v_1=v_1.cpu().numpy(), lat_tp=lat_tp.cpu().numpy(),
-                 lat_1=lat_1.cpu().numpy())
+        dit.set_seq(None)
+        cref = dit.prepare_context(ctx)
+        v_1 = dit.forward(x0, cref, dit.time_cond(sig[0]))
+        lat_1 = pl.denoise_loop(dit, noise, cref, 2)
+        np.savez(out_path, v_sp=v_sp.cpu().numpy(), v_1=v_1.cpu().numpy(), lat_sp=lat_sp.cpu().numpy(),
+                 lat_1=lat_1.cpu().numpy(), lat_graph=lat_graph.cpu().numpy())
     dist.barrier()
     dist.destroy_process_group()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_tensor_parallel_matches_single_gpu(tmp_path):
-    out = str(tmp_path / "tp.npz")
+def test_sequence_parallel_matches_single_gpu_and_reference(tmp_path):
+    out = str(tmp_path / "sp.npz")
     mp.spawn(_worker, args=(2, _free_port(), out), nprocs=2, join=True)
     r = np.load(out)
+    g = np.load(os.path.join(GOLDEN, "forward_int8_16x16.npz"))
     rel = lambda a, b: float(np.linalg.norm(a - b) / np.linalg.norm(b))  # noqa: E731
-    assert rel(r["v_tp"], r["v_1"]) < 1e-3
-    assert rel(r["lat_tp"], r["lat_1"]) < 1e-3
+    print(f"sp2 vs 1 GPU: velocity {rel(r['v_sp'], r['v_1']):.2e} latent {rel(r['lat_sp'], r['lat_1']):.2e}; "
+          f"vs reference: velocity {rel(r['v_sp'][0], g['velocity0']):.2e} latent {rel(r['lat_sp'][0], g['latent_final']):.2e}")
+    assert rel(r["v_sp"], r["v_1"]) < 1e-4
+    assert rel(r["lat_sp"], r["lat_1"]) < 1e-4
+    assert rel(r["lat_graph"], r["lat_sp"]) < 1e-6
+    assert rel(r["v_sp"][0], g["velocity0"]) < 3e-3
+    assert rel(r["lat_sp"][0], g["latent_final"]) < 3e-3
