@@ -4,3 +4,4 @@
 #include "rowops.cu"
 #include "gemm_i8.cu"
 #include "attention.cu"
+#include "peer.cu"

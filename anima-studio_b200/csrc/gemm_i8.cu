@@ -16,6 +16,8 @@
 // The accumulators are double-buffered in TMEM (2 x NPLANES x BN = 512 columns), one buffer per
 // epilogue warpgroup, so the epilogues of two tiles overlap the MMAs of the next.
 
+#include <cstring>
+
 #include "internal.h"
 #include "sm100.cuh"
 
@@ -55,8 +57,16 @@ struct Params {
   int ld_bt;
   int lora_count;
   int lora_off[4], lora_n[4], lora_r0[4], lora_r[4];
+  // sequence-parallel k|v exchange (see anima_linear_opts): k|v pieces go to the peer maps
+  int peer_count, peer_row0, peer_rows;
   int num_m_blocks, num_n_blocks, num_k_blocks, num_tiles;
   int group_m;
+};
+
+// Tensor maps over every rank's gathered k|v buffer (3D: columns, rows of an image, image), as
+// mapped in this process; only peer_count of them are encoded.
+struct PeerMaps {
+  CUtensorMap m[8];
 };
 
 // Tile order: groups of group_m m-blocks, n-blocks outermost within a group, so the CTAs in flight
@@ -278,6 +288,21 @@ __device__ __forceinline__ void stage_flush(const CUtensorMap* tm, const uint8_t
   __syncwarp();
 }
 
+// Sequence-parallel qkv: a full staging buffer of k|v columns (x >= n_q) goes to every rank's
+// gathered k|v buffer at this rank's rows instead of to the local output (one bulk group).
+__device__ __forceinline__ void stage_flush_peers(const Params& p, const PeerMaps* pm, const uint8_t* buf, int x,
+                                                  int y) {
+  fence_proxy_async_smem();
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) {
+    const int item = y / p.peer_rows;
+    const int row = p.peer_row0 + (y - item * p.peer_rows);
+    for (int r = 0; r < p.peer_count; ++r) tma_store_3d(&pm->m[r], buf, x - p.n_q, row, item);
+    bulk_commit();
+  }
+  __syncwarp();
+}
+
 // Before rewriting a staging buffer: at most N of this warp's stores may still be reading.
 template <int N>
 __device__ __forceinline__ void stage_acquire() {
@@ -288,8 +313,9 @@ __device__ __forceinline__ void stage_acquire() {
 // One tile's epilogue for this warp's 32 rows (m = row of this lane) over BN columns from n0.
 // stage: this warp's two staging buffers; y0: first row of the warp's quadrant.
 template <int BN, int NPLANES, bool LORA>
-__device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap* tm_out, uint8_t* stage,
-                                              uint32_t taddr, int m, int y0, int n0, const LoraTile& lt) {
+__device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap* tm_out, const PeerMaps* pm,
+                                              uint8_t* stage, uint32_t taddr, int m, int y0, int n0,
+                                              const LoraTile& lt) {
   const bool row_ok = m < p.M;
   const int lane = threadIdx.x & 31;
   const int esz = p.out_dtype == ANIMA_F32 ? 4 : 2;
@@ -351,7 +377,12 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap
         float v[CH];
         load_cols<BN, NPLANES, LORA, CH>(p, taddr, h0 + col, m, nh + col, row_ok, v, true, lt);
         stage_piece(buf, lane, p.out_dtype, q, v);
-        if (q == ppc - 1) stage_flush(tm_out, buf, nh + chunk * chc, y0, false);
+        if (q == ppc - 1) {
+          if (p.peer_count)
+            stage_flush_peers(p, pm, buf, nh + chunk * chc, y0);
+          else
+            stage_flush(tm_out, buf, nh + chunk * chc, y0, false);
+        }
       }
       continue;
     }
@@ -397,8 +428,13 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap
         stage_piece(stage + STAGE_BUF, lane, p.out_dtype, q, v2);
         if (q == ppc - 1) {
           const int x0 = nh + (c / chc) * chc;
-          stage_flush(tm_out, stage, x0, y0, false);
-          stage_flush(tm_out, stage + STAGE_BUF, x0 + 64, y0, false);
+          if (is_k && p.peer_count) {
+            stage_flush_peers(p, pm, stage, x0, y0);
+            stage_flush_peers(p, pm, stage + STAGE_BUF, x0 + 64, y0);
+          } else {
+            stage_flush(tm_out, stage, x0, y0, false);
+            stage_flush(tm_out, stage + STAGE_BUF, x0 + 64, y0, false);
+          }
         }
       }
     } else {
@@ -449,7 +485,7 @@ template <int BN, int NPLANES, bool LORA>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tm_hi, const __grid_constant__ CUtensorMap tm_lo,
                    const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_out,
-                   const Params p) {
+                   const Params p, const __grid_constant__ PeerMaps pm) {
   using C = Cfg<BN, NPLANES, LORA>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -648,8 +684,8 @@ __global__ void __launch_bounds__(THREADS, 1)
           lt.r = r;
         }
       }
-      epilogue_tile<BN, NPLANES, LORA>(p, &tm_out, staging + warp * 2 * STAGE_BUF, taddr, mb * BM + row,
-                                 mb * BM + quad * 32, nb * BN, lt);
+      epilogue_tile<BN, NPLANES, LORA>(p, &tm_out, &pm, staging + warp * 2 * STAGE_BUF, taddr, mb * BM + row,
+                                       mb * BM + quad * 32, nb * BN, lt);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
@@ -735,6 +771,25 @@ int launch(anima_ctx* ctx, const anima_qact* x, const anima_weight* W, const ani
     p.lora_r0[e] = o->lora_r0[e];
     p.lora_r[e] = o->lora_r[e];
   }
+  PeerMaps pm;
+  memset(&pm, 0, sizeof(pm));
+  p.peer_count = o->peer_count;
+  p.peer_row0 = o->peer_row0;
+  p.peer_rows = o->peer_rows > 0 ? o->peer_rows : 1;
+  if (o->peer_count > 0) {
+    const int esz = o->out_dtype == ANIMA_F32 ? 4 : 2;
+    const CUtensorMapDataType odt = o->out_dtype == ANIMA_F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                    : o->out_dtype == ANIMA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                                 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const uint64_t cols = static_cast<uint64_t>(N - o->n_q);
+    uint64_t dims[3] = {cols, static_cast<uint64_t>(o->peer_item_rows), static_cast<uint64_t>(M / o->peer_rows)};
+    uint64_t str[2] = {cols * esz, cols * esz * static_cast<uint64_t>(o->peer_item_rows)};
+    uint32_t box[3] = {static_cast<uint32_t>(128 / esz), 32, 1};
+    for (int r = 0; r < o->peer_count; ++r) {
+      st = make_tmap(&pm.m[r], odt, 3, o->peer_kv[r], dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
+      if (st) return st;
+    }
+  }
   p.num_m_blocks = (M + BM - 1) / BM;
   p.num_n_blocks = N / BN;
   p.num_k_blocks = K / BK;
@@ -750,7 +805,7 @@ int launch(anima_ctx* ctx, const anima_qact* x, const anima_weight* W, const ani
   const int grid = p.num_tiles < ctx->num_sms ? p.num_tiles : ctx->num_sms;
   ProfScope prof(ctx, NPLANES == 2 ? "linear.i8x2" : "linear.i8", 2.0 * M * N * K,
                  static_cast<double>(M) * K * NPLANES + static_cast<double>(N) * K);
-  gemm_i8_kernel<BN, NPLANES, LORA><<<grid, THREADS, C::SMEM_BYTES, ctx->stream>>>(tm_hi, tm_lo, tm_w, tm_out, p);
+  gemm_i8_kernel<BN, NPLANES, LORA><<<grid, THREADS, C::SMEM_BYTES, ctx->stream>>>(tm_hi, tm_lo, tm_w, tm_out, p, pm);
   return check_launch("gemm_i8_kernel");
 }
 
@@ -817,6 +872,16 @@ extern "C" int anima_linear(anima_ctx* ctx, const anima_qact* x, const anima_wei
     ANIMA_REQUIRE(o->n_q % 128 == 0 && 2 * o->n_q <= W->N, "anima_linear: bad n_q %d", o->n_q);
   }
   if (o->out_mode == ANIMA_OUT_HEAD_NORM) ANIMA_REQUIRE(o->norm_q, "anima_linear: head-norm epilogue needs norm_q");
+  if (o->peer_count != 0) {
+    ANIMA_REQUIRE(o->out_mode == ANIMA_OUT_QKV_NORM_ROPE && o->peer_count > 0 && o->peer_count <= 8,
+                  "anima_linear: the k|v exchange takes 1-8 buffers and the qkv epilogue");
+    ANIMA_REQUIRE(o->peer_rows > 0 && o->peer_rows % 32 == 0 && x->rows % o->peer_rows == 0 && o->peer_row0 >= 0 &&
+                      o->peer_row0 + o->peer_rows <= o->peer_item_rows,
+                  "anima_linear: k|v exchange rows (row0 %d, rows %d of %d per image, M %d) invalid", o->peer_row0,
+                  o->peer_rows, o->peer_item_rows, x->rows);
+    for (int r = 0; r < o->peer_count; ++r)
+      ANIMA_REQUIRE(o->peer_kv[r] && aligned16(o->peer_kv[r]), "anima_linear: k|v buffer %d missing or unaligned", r);
+  }
   if (o->lora_t) {
     ANIMA_REQUIRE(o->lora_bt && o->lora_count >= 1 && o->lora_count <= 4, "anima_linear: LoRA needs t, bt and 1-4 entries");
     ANIMA_REQUIRE(aligned16(o->lora_t) && aligned16(o->lora_bt) && o->ld_t % 4 == 0 && o->ld_bt % 4 == 0 &&

@@ -238,12 +238,13 @@ int anima_sync(anima_ctx* ctx) {
       ANIMA_CUDA(cudaMemset(ctx->attn_flags, 0, static_cast<size_t>(ctx->num_sms) * 16 * sizeof(unsigned)));
     if (ctx->attn_static_ws)
       ANIMA_CUDA(cudaMemset(ctx->attn_static_ws, 0, static_cast<size_t>(ctx->num_sms) * 16 * sizeof(unsigned)));
-    return set_error(ANIMA_ERR_DEVICE, "device error flags 0x%x (%s%s%s%s%s)", err,
+    return set_error(ANIMA_ERR_DEVICE, "device error flags 0x%x (%s%s%s%s%s%s)", err,
                      (err & kErrTimeoutFull) ? "data wait timed out; " : "",
                      (err & kErrTimeoutEmpty) ? "stage wait timed out; " : "",
                      (err & kErrTimeoutAcc) ? "accumulator wait timed out; " : "",
                      (err & kErrTimeoutDrain) ? "drain after abort timed out; " : "",
-                     (err & kErrBadArgs) ? "kernel rejected its arguments; " : "");
+                     (err & kErrBadArgs) ? "kernel rejected its arguments; " : "",
+                     (err & kErrPeerWait) ? "cross-GPU barrier timed out waiting for another rank; " : "");
   }
   if (ctx->profile) prof_collect(ctx);
   return ANIMA_OK;

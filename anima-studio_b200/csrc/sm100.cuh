@@ -22,6 +22,7 @@ enum DeviceError : unsigned {
   kErrTimeoutAcc = 1u << 2,     // accumulator hand-off timed out
   kErrTimeoutDrain = 1u << 3,   // draining in-flight copies after an abort timed out
   kErrBadArgs = 1u << 4,        // a kernel saw arguments it cannot handle
+  kErrPeerWait = 1u << 5,       // a cross-GPU barrier waited too long for another rank
 };
 
 // Defined once: the library is built as a single translation unit (anima_b200.cu).
@@ -136,6 +137,14 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void*
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
                    reinterpret_cast<uint64_t>(map)),
                "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+
+// Store a tile to a 3D tensor map (x innermost). Used for k|v tiles sent to other ranks' buffers.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int x, int y, int z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
                : "memory");
 }
 

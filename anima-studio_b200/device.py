@@ -33,7 +33,8 @@ EXPORTS = [
     "anima_rotate", "anima_rotate_quant", "anima_act_rotate_quant", "anima_quant_rows", "anima_rmsnorm", "anima_qk_norm_rope", "anima_rope",
     "anima_attention", "anima_attention_noalloc", "anima_elementwise", "anima_zero", "anima_patchify", "anima_unpatchify",
     "anima_timestep_embedding", "anima_euler_step", "anima_lincomb", "anima_selftest_wait_timeout",
-    "anima_ctx_set_attention_split",
+    "anima_ctx_set_attention_split", "anima_ipc_alloc", "anima_ipc_open", "anima_ipc_close", "anima_ipc_free",
+    "anima_peer_barrier",
 ]
 
 
@@ -62,7 +63,14 @@ class LinearOpts(C.Structure):
                 ("rope_rows", C.c_int), ("n_q", C.c_int), ("eps", C.c_float),
                 ("lora_t", C.c_void_p), ("ld_t", C.c_int), ("lora_t_lo", C.c_int), ("lora_bt", C.c_void_p), ("ld_bt", C.c_int),
                 ("lora_count", C.c_int), ("lora_off", C.c_int * 4), ("lora_n", C.c_int * 4),
-                ("lora_r0", C.c_int * 4), ("lora_r", C.c_int * 4)]
+                ("lora_r0", C.c_int * 4), ("lora_r", C.c_int * 4),
+                ("peer_count", C.c_int), ("peer_kv", C.c_void_p * 8), ("peer_row0", C.c_int), ("peer_rows", C.c_int),
+                ("peer_item_rows", C.c_int)]
+
+
+class PeerGroup(C.Structure):
+    _fields_ = [("rank", C.c_int), ("world", C.c_int), ("flags", C.c_void_p * 8), ("counter", C.c_void_p),
+                ("timeout_us", C.c_uint)]
 
 
 class AttentionArgs(C.Structure):
@@ -114,6 +122,9 @@ def load_library(path: str = LIB_PATH):
             "anima_patchify": [vp, vp, i, i, i, vp], "anima_unpatchify": [vp, vp, i, i, i, vp],
             "anima_timestep_embedding": [vp, vp, i, vp],
             "anima_euler_step": [vp, vp, vp, vp, f, f, f, ll, vp],
+            "anima_ipc_alloc": [vp, sz, C.POINTER(vp), C.c_char_p], "anima_ipc_open": [vp, C.c_char_p, C.POINTER(vp)],
+            "anima_ipc_close": [vp, vp], "anima_ipc_free": [vp, vp],
+            "anima_peer_barrier": [vp, C.POINTER(PeerGroup)],
         }
         for name, args in sig.items():
             fn = getattr(lib, name)
@@ -141,7 +152,8 @@ def check(status: int):
 LAUNCHING = set(EXPORTS) - {"anima_ctx_create", "anima_ctx_destroy", "anima_ctx_set_stream", "anima_sync",
                             "anima_last_error", "anima_alloc", "anima_free", "anima_upload", "anima_download",
                             "anima_profile_report", "anima_version", "anima_zero", "anima_selftest_wait_timeout",
-                            "anima_ctx_set_attention_split"}
+                            "anima_ctx_set_attention_split", "anima_ipc_alloc", "anima_ipc_open", "anima_ipc_close",
+                            "anima_ipc_free"}
 
 
 class KernelTimer:

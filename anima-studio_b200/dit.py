@@ -102,6 +102,8 @@ class AnimaDiT:
         if precision not in ("a16", "a8"):
             raise ValueError("precision must be 'a16' (two int8 planes) or 'a8' (W8A8)")
         self.seq = seq if seq is not None and seq.world > 1 else None
+        self.seq_exchange = "peer"
+        self._exchanges = []
         self.device = torch.device(device)
         self.planes = 2 if precision == "a16" else 1
         self.precision = precision
@@ -148,12 +150,21 @@ class AnimaDiT:
         self._rope = {}
         self._bufs = {}
 
-    def set_seq(self, seq) -> None:
+    def set_seq(self, seq, exchange: str = "peer") -> None:
         """Switch sequence parallelism on (a sharding.SeqGroup with world > 1) or off (None) for
-        later forwards; the weights are the same either way."""
+        later forwards; the weights are the same either way. exchange: how self-attention's k|v
+        reach the other ranks: "peer" (the qkv GEMM stores them into every rank's buffer over
+        NVLink, then a device barrier) or "nccl" (a copy and an NCCL all-gather). Collective."""
+        self._close_exchanges()
         self.seq = seq if seq is not None and seq.world > 1 else None
+        self.seq_exchange = exchange
         self._bufs = {}
         self._rope = {}
+
+    def _close_exchanges(self):
+        for x in getattr(self, "_exchanges", []):
+            x.close()
+        self._exchanges = []
 
     @classmethod
     def from_file(cls, path: str, device="cuda", prefix: str = "model.diffusion_model.", **kw) -> "AnimaDiT":
@@ -247,9 +258,17 @@ class AnimaDiT:
             }
             if self.seq:
                 Lr = M // B
-                # this rank's k|v rows, then every rank's, per image: [B, world * Lr, 4096]
-                b["kv_mine"] = torch.empty(B, Lr, 2 * D, dtype=self.attn_dtype, device=dv)
-                b["kv_all"] = torch.empty(B, self.seq.world * Lr, 2 * D, dtype=self.attn_dtype, device=dv)
+                if self.seq_exchange == "peer":
+                    # every rank's k|v rows land in this rank's IPC-shared buffer [B, world * Lr, 4096];
+                    # kept until set_seq (graphs captured on it may still be replayed)
+                    from .sharding import KVExchange
+                    x = KVExchange(self.seq, B, Lr, self.attn_dtype, dv)
+                    self._exchanges.append(x)
+                    b["kvx"], b["kv_all"] = x, x.kv
+                else:
+                    # this rank's k|v rows, then every rank's, per image: [B, world * Lr, 4096]
+                    b["kv_mine"] = torch.empty(B, Lr, 2 * D, dtype=self.attn_dtype, device=dv)
+                    b["kv_all"] = torch.empty(B, self.seq.world * Lr, 2 * D, dtype=self.attn_dtype, device=dv)
             self._bufs = {(M, B): b}
         return b
 
@@ -263,10 +282,15 @@ class AnimaDiT:
         qa, qh = bufs["qa"], bufs["qh"]
         # self-attention
         ops.layernorm_mod_quant(x, m_self, 0, D, D, out=qa)
+        kvx = bufs.get("kvx")
         qkv = ops.linear(qa, blk["qkv"], out=bufs["qkv"], mode="qkv", qk=(blk["self_qn"], blk["self_kn"]),
-                         rope_cs=cs, n_q=D, name="dit.self.qkv")
+                         rope_cs=cs, n_q=D, name="dit.self.qkv", peer=kvx.peer_args() if kvx else None)
         if self.seq:
-            kv = self._gather_kv(qkv, B, L, bufs)
+            if kvx:
+                kvx.barrier()        # every rank's k|v tiles have landed in bufs["kv_all"]
+                kv = bufs["kv_all"]
+            else:
+                kv = self._gather_kv(qkv, B, L, bufs)
             Lk = kv.shape[1]
             a = ops.attention(qkv, kv, kv, Lq=L, Lk=Lk, H=HEADS, D=HD, ldq=3 * D, ldk=2 * D, ldv=2 * D, q_off=0,
                               k_off=0, v_off=D, batch=B, q_bstride=L * 3 * D, k_bstride=Lk * 2 * D,

@@ -163,7 +163,7 @@ def zero(t: torch.Tensor):
 def linear(x, W, *, out: torch.Tensor | None = None, resid: bool = False, gate: torch.Tensor | None = None,
            g_off: int = 0, act: str | None = None, add: torch.Tensor | None = None, out_dtype=torch.float32,
            mode: str = "store", qk=None, rope_cs: torch.Tensor | None = None, n_q: int = 0, eps: float = 1e-6,
-           planes: int = 2, name: str | None = None) -> torch.Tensor:
+           planes: int = 2, name: str | None = None, peer=None) -> torch.Tensor:
     """y = x @ W^T (+ bias) (+ add) (act); or out += gate[g_off + n] * y when resid (ops.js:48-66).
 
     x: QuantRows (rotated, quantized) for ConvRot weights, or an fp32 tensor (rotated and quantized
@@ -171,6 +171,9 @@ def linear(x, W, *, out: torch.Tensor | None = None, resid: bool = False, gate: 
     before the activation, as the reference does (ops.js:55-57).
     mode: "store" | "qkv" (per-head RMSNorm + RoPE on q/k heads, qk = (qn, kn)) |
           "head_norm" (per-head RMSNorm with qk[0]).
+    peer (mode "qkv"): {"kv": [device addresses of every rank's gathered k|v buffer], "row0", "rows",
+          "item_rows"}: the k|v columns go to those buffers over NVLink instead of to `out`
+          (sharding.KVExchange; anima_linear_opts.peer_*).
     """
     from .lora import lora_delta, lora_epilogue
 
@@ -208,6 +211,11 @@ def linear(x, W, *, out: torch.Tensor | None = None, resid: bool = False, gate: 
         o.rope_rows = rope_cs.numel() // 128
     o.n_q = n_q
     o.eps = eps
+    if peer is not None:
+        o.peer_count = len(peer["kv"])
+        for r, a in enumerate(peer["kv"]):
+            o.peer_kv[r] = a
+        o.peer_row0, o.peer_rows, o.peer_item_rows = peer["row0"], peer["rows"], peer["item_rows"]
     qa = x.c()
     w = W.c()
     ctx_for(x.hi).call("anima_linear", C.byref(qa), C.byref(w), C.byref(o), tag=name, work=2.0 * M * W.N * W.K,

@@ -73,3 +73,85 @@ class SeqGroup:
 
         dist.all_gather_into_tensor(out, inp, group=self.group)
         return out
+
+
+class _DeviceArray:
+    """__cuda_array_interface__ over a raw device allocation, for a torch view of it."""
+
+    def __init__(self, addr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (addr, False),
+                                         "version": 3, "strides": None}
+
+
+class KVExchange:
+    """The k|v exchange of sequence parallelism over peer memory, for images of `rows` local token
+    rows: every rank owns a gathered k|v buffer [B, world * rows, 4096] and a flag array, shared
+    with the other ranks by CUDA IPC. The qkv GEMM of each rank stores its k|v tiles into every
+    rank's buffer through its mappings (ops.linear(..., peer=self.peer_args())), then barrier()
+    (anima_peer_barrier) orders those writes before any rank's attention reads `self.kv`.
+    Construction and close() are collective: every rank of the group calls them in the same order."""
+
+    def __init__(self, seq: SeqGroup, B: int, rows: int, dtype: torch.dtype, device):
+        import ctypes as C
+
+        import torch.distributed as dist
+
+        from . import device as dev
+
+        self.seq, self.B, self.rows = seq, B, rows
+        index = torch.device(device).index
+        self.ctx = dev.Context.get(torch.cuda.current_device() if index is None else index)
+        esz = torch.tensor([], dtype=dtype).element_size()
+        nbytes = B * seq.world * rows * 4096 * esz
+        mine, handles = [], []
+        for size in (nbytes, 64):  # the k|v buffer, then the barrier flags (world <= 8 words)
+            addr, h = C.c_void_p(), C.create_string_buffer(64)
+            self.ctx.call("anima_ipc_alloc", size, C.byref(addr), h)
+            mine.append(addr.value)
+            handles.append(h.raw)
+        everyone = [None] * seq.world
+        dist.all_gather_object(everyone, handles, group=seq.group)
+        self.kv_addr, self.flag_addr, self.opened = [], [], []
+        for r, (hk, hf) in enumerate(everyone):
+            if r == seq.rank:
+                self.kv_addr.append(mine[0])
+                self.flag_addr.append(mine[1])
+                continue
+            for h, dst in ((hk, self.kv_addr), (hf, self.flag_addr)):
+                addr = C.c_void_p()
+                self.ctx.call("anima_ipc_open", h, C.byref(addr))
+                dst.append(addr.value)
+                self.opened.append(addr.value)
+        self.own = mine
+        self.counter = torch.zeros(1, dtype=torch.int32, device=device)
+        typestr = "<f2" if dtype == torch.float16 else "<i2"
+        kv = torch.as_tensor(_DeviceArray(mine[0], (B, seq.world * rows, 4096), typestr), device=device)
+        self.kv = kv if dtype == torch.float16 else kv.view(dtype)
+        g = dev.PeerGroup()
+        g.rank, g.world, g.timeout_us = seq.rank, seq.world, 0
+        for r in range(seq.world):
+            g.flags[r] = self.flag_addr[r]
+        g.counter = self.counter.data_ptr()
+        self._group = g
+
+    def peer_args(self) -> dict:
+        lo, _ = self.seq.span(self.seq.world * self.rows)
+        return {"kv": list(self.kv_addr), "row0": lo, "rows": self.rows, "item_rows": self.seq.world * self.rows}
+
+    def barrier(self):
+        import ctypes as C
+
+        self.ctx.call("anima_peer_barrier", C.byref(self._group))
+
+    def close(self):
+        """Unmap the other ranks' buffers, then free this rank's (collective)."""
+        import torch.distributed as dist
+
+        torch.cuda.synchronize()
+        dist.barrier(group=self.seq.group)
+        for a in self.opened:
+            self.ctx.call("anima_ipc_close", a)
+        dist.barrier(group=self.seq.group)
+        for a in self.own:
+            self.ctx.call("anima_ipc_free", a)
+        self.opened, self.own = [], []

@@ -412,14 +412,14 @@ def measure_cfg(dit, seed, res, cfg, steps, warmup, world, rank, peaks, int8_pea
             f"{steps} timed steps per rank", "per_op": prof}
 
 
-def measure_seq(dit, seed, steps, warmup, world, rank):
+def measure_seq(dit, seed, steps, warmup, world, rank, exchange="peer"):
     """One image denoised by all ranks together: its 4096 token rows split over the ranks
     (sequence parallelism, one k|v all-gather per block), Euler 8-step schedule, CUDA graph per
     step with the all-gathers captured in it. Returns the single-image rate."""
     import torch
 
     syn, pl, sh = pkg("synthetic"), pkg("pipeline"), pkg("sharding")
-    dit.set_seq(sh.SeqGroup(rank, world, None))
+    dit.set_seq(sh.SeqGroup(rank, world, None), exchange)
     try:
         cond = dit.prepare_context(torch.cat([syn.randn(seed, "ctx", (256, 1024)), torch.zeros(256, 1024)]).cuda())
         noise = syn.randn(seed, "noise", (1, 16, 128, 128)).cuda()   # the same image on every rank
@@ -428,8 +428,11 @@ def measure_seq(dit, seed, steps, warmup, world, rank):
         del gs
     finally:
         dit.set_seq(None)
-    return {"workload": "one 1024x1024 image, 28 INT8 ConvRot blocks, token rows split over the ranks, one "
-                        "all-gather of k|v (fp16, 16 MiB) per block, CUDA graph per step", "n_gpus": world,
+    how = ("the qkv GEMM stores its k|v tiles into every rank's buffer over NVLink, then a device barrier"
+           if exchange == "peer" else "a copy and an NCCL all-gather")
+    return {"workload": "one 1024x1024 image, 28 INT8 ConvRot blocks, token rows split over the ranks; k|v of all "
+                        f"rows (fp16, 16 MiB) exchanged once per block: {how}; CUDA graph per step",
+            "exchange": exchange, "n_gpus": world,
             "steps_per_s": steps / (ms * 1e-3), "ms_per_step": ms / steps, "steps": steps, "scaling": "strong"}
 
 
@@ -697,6 +700,7 @@ def main():
                        for res, n in ((1024, 12), (1536, 6))]
         if world > 1:
             subs["tp"] = measure_seq(dit, seed, 16, 3, world, rank)
+            subs["tp"]["nccl_exchange"] = measure_seq(dit, seed, 16, 3, world, rank, "nccl")
     int8_peak = measure_int8_peak(torch) if rank == 0 else None
     dist.destroy_process_group() if world > 1 else None
     if rank != 0:

@@ -107,6 +107,16 @@ typedef struct {
   int ld_bt;
   int lora_count;
   int lora_off[4], lora_n[4], lora_r0[4], lora_r[4];
+  /* Sequence-parallel k|v exchange (QKV_NORM_ROPE only; no reference counterpart): when
+     peer_count > 0 the k and v columns [n_q, N) do not go to out; every 32-row piece of them is
+     stored instead into peer_kv[0..peer_count), each rank's gathered k|v buffer
+     [items, peer_item_rows, N - n_q] (dtype out_dtype, 16-byte aligned) as mapped in this process
+     (anima_ipc_open; this rank's own buffer included), at row peer_row0 + m % peer_rows of item
+     m / peer_rows. peer_rows is a multiple of 32 dividing M; follow with anima_peer_barrier before
+     any rank reads its buffer. Only TMA stores touch peer memory. */
+  int peer_count;
+  void* peer_kv[8];
+  int peer_row0, peer_rows, peer_item_rows;
 } anima_linear_opts;
 
 typedef struct {
@@ -253,6 +263,39 @@ int anima_selftest_wait_timeout(anima_ctx* ctx, unsigned timeout_us, int* result
  * A NULL x_k drops its term; y may be any of the x_k (elementwise, in place). */
 int anima_lincomb(anima_ctx* ctx, float* y, long long n, const float* x0, const float* x1, const float* x2,
                   const float* x3, const float* c);
+
+/* ---------------------------------------------------------------- several GPUs of one node */
+/* Peer memory for the sequence-parallel mode, where the ranks of one node split an image's token
+ * rows and exchange self-attention keys/values (no reference counterpart: the reference runs on
+ * one GPU). One process per GPU; buffers are shared with CUDA IPC, written by kernels over NVLink.
+ *
+ * anima_ipc_alloc: a plain device allocation of `bytes` on the context's device, zero-filled,
+ *   and its 64-byte IPC handle (to hand to the other ranks, e.g. through torch.distributed).
+ * anima_ipc_open: map another process's handle into this one (peer access enabled); returns the
+ *   device address to use in this process. anima_ipc_close unmaps it; anima_ipc_free frees an
+ *   anima_ipc_alloc allocation (after every other rank closed its mapping). */
+int anima_ipc_alloc(anima_ctx* ctx, size_t bytes, void** ptr, unsigned char handle[64]);
+int anima_ipc_open(anima_ctx* ctx, const unsigned char handle[64], void** ptr);
+int anima_ipc_close(anima_ctx* ctx, void* ptr);
+int anima_ipc_free(anima_ctx* ctx, void* ptr);
+
+/* The ranks of one node, for anima_peer_barrier. flags[r] is rank r's flag array (world unsigned,
+ * from anima_ipc_alloc, zeroed) as mapped in this process (this rank's own at flags[rank]);
+ * counter is this rank's private barrier count (device memory, zero at start). */
+typedef struct {
+  int rank, world;         /* world <= 8 */
+  unsigned* flags[8];
+  unsigned* counter;
+  unsigned timeout_us;     /* 0 = 2 s */
+} anima_peer_group;
+
+/* Device-side barrier of all ranks, in stream order: the kernel raises this rank's next epoch in
+ * every rank's flags (system-scope release after a system fence, so this rank's earlier kernels'
+ * writes to peer memory are visible first) and waits (acquire) until every rank has raised it.
+ * Every rank must call it the same number of times. A wait that runs past the timeout records
+ * "cross-GPU barrier timed out" in the device error word (reported by anima_sync) and returns;
+ * nothing hangs. Safe inside CUDA graphs: the epoch lives in device memory. */
+int anima_peer_barrier(anima_ctx* ctx, const anima_peer_group* g);
 
 #ifdef __cplusplus
 }

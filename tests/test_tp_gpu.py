@@ -1,7 +1,9 @@
-"""Sequence parallelism on 2 GPUs (NCCL): one image's token rows split over the ranks, k|v gathered
-for self-attention. The split forward must match the one-GPU forward of the same weights (the
-same kernels on fewer rows; only the GEMM tiling of the row slices differs) and the reference's
-own 28-block forward + 2 Euler steps at a 16x16 latent (tests/golden/forward_int8_16x16.npz)."""
+"""Sequence parallelism on 2 GPUs: one image's token rows split over the ranks, k|v of all rows
+exchanged for self-attention, either by the qkv GEMM storing its k|v tiles into every rank's buffer
+over NVLink (peer memory, device barrier) or by an NCCL all-gather; both must deliver the same
+k|v. The split forward must match the one-GPU forward of the same weights (the same kernels on
+fewer rows) and the reference's own 28-block forward + 2 Euler steps at a 16x16 latent
+(tests/golden/forward_int8_16x16.npz)."""
 
 import os
 import socket
@@ -38,24 +40,30 @@ def _worker(rank, world, port, out_path):
     tensors = syn.dit_tensors(seed, "int8", 28, direct=True)
     ctx = torch.cat([syn.randn(seed, "golden.ctx", (256, 1024)), torch.zeros(256, 1024)]).cuda()
     noise = torch.from_numpy(g["noise"])[None].cuda()
-    dit = ditm.AnimaDiT(tensors, "cuda", seq=sh.SeqGroup(rank, world, None))
+    seq = sh.SeqGroup(rank, world, None)
+    dit = ditm.AnimaDiT(tensors, "cuda", seq=seq)       # k|v exchanged over peer memory
     cond = dit.prepare_context(ctx)
     sig = pl.sigmas_simple(2, 3.0)
     x0 = (noise * np.float32(sig[0])).contiguous()
     v_sp = dit.forward(x0, cond, dit.time_cond(sig[0]))
     lat_sp = pl.denoise_loop(dit, noise, cond, 2)
-    # the graphed sampler with the all-gathers captured in its graphs
+    # the graphed sampler with the qkv GEMMs' peer stores and the device barriers captured
     gs = pl.GraphedSampler(dit, cond, 2, 1, 16, 16)
     lat_graph = gs.run(noise).clone()
+    lat_graph2 = gs.run(noise).clone()   # replays are repeatable (the barrier epochs live on the device)
     del gs
+    dit.set_seq(seq, "nccl")                             # the same exchange through NCCL
+    v_nccl = dit.forward(x0, cond, dit.time_cond(sig[0]))
     torch.cuda.synchronize()
+    pkg("device").Context.get(rank).sync()
+    dit.set_seq(None)
     if rank == 0:
-        dit.set_seq(None)
         cref = dit.prepare_context(ctx)
         v_1 = dit.forward(x0, cref, dit.time_cond(sig[0]))
         lat_1 = pl.denoise_loop(dit, noise, cref, 2)
         np.savez(out_path, v_sp=v_sp.cpu().numpy(), v_1=v_1.cpu().numpy(), lat_sp=lat_sp.cpu().numpy(),
-                 lat_1=lat_1.cpu().numpy(), lat_graph=lat_graph.cpu().numpy())
+                 lat_1=lat_1.cpu().numpy(), lat_graph=lat_graph.cpu().numpy(), lat_graph2=lat_graph2.cpu().numpy(),
+                 v_nccl=v_nccl.cpu().numpy())
     dist.barrier()
     dist.destroy_process_group()
 
@@ -72,5 +80,7 @@ def test_sequence_parallel_matches_single_gpu_and_reference(tmp_path):
     assert rel(r["v_sp"], r["v_1"]) < 1e-4
     assert rel(r["lat_sp"], r["lat_1"]) < 1e-4
     assert rel(r["lat_graph"], r["lat_sp"]) < 1e-6
+    assert np.array_equal(r["lat_graph2"], r["lat_graph"])
+    assert np.array_equal(r["v_nccl"], r["v_sp"])       # both exchanges deliver the same k|v
     assert rel(r["v_sp"][0], g["velocity0"]) < 3e-3
     assert rel(r["lat_sp"][0], g["latent_final"]) < 3e-3
