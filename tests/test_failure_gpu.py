@@ -28,3 +28,35 @@ def test_bounded_wait_times_out_and_the_context_survives():
     z = ops.rotate(y)  # the Hadamard is its own inverse
     assert rel_l2(z.cpu().numpy(), x.cpu().numpy()) < 1e-6
     ctx.sync()
+
+
+def test_peer_barrier_without_the_other_rank_times_out():
+    """The sequence-parallel barrier as rank 0 of a two-rank group whose second rank never
+    arrives (its flag words are a second local array that nothing writes): after the 50 ms limit
+    the kernel records the timeout and returns; a one-rank barrier completes."""
+    dev = pkg("device")
+    ctx = dev.Context.get(0)
+    addrs = []
+    for _ in range(2):
+        a, h = C.c_void_p(), C.create_string_buffer(64)
+        ctx.call("anima_ipc_alloc", 64, C.byref(a), h)
+        addrs.append(a.value)
+    counter = torch.zeros(1, dtype=torch.int32, device="cuda")
+    try:
+        g = dev.PeerGroup()
+        g.rank, g.world, g.timeout_us = 0, 1, 50000
+        g.flags[0] = addrs[0]
+        g.counter = counter.data_ptr()
+        ctx.call("anima_peer_barrier", C.byref(g))
+        ctx.sync()                       # alone, every rank has arrived
+        assert int(counter.item()) == 1
+        g.world = 2
+        g.flags[1] = addrs[1]            # "rank 1": its own flags get this rank's epoch, its word in ours never
+        ctx.call("anima_peer_barrier", C.byref(g))
+        with pytest.raises(dev.AnimaError, match="cross-GPU barrier timed out"):
+            ctx.sync()
+        ctx.sync()
+        assert int(counter.item()) == 2
+    finally:
+        for a in addrs:
+            ctx.call("anima_ipc_free", a)
