@@ -730,21 +730,214 @@ int static_scratch(anima_ctx* ctx) {
 }  // namespace attn
 }  // namespace anima
 
+// ------------------------------------------------------------------ text-model attention
+// The Qwen3 text encoder (causal, 16 q heads over 8 k/v heads, d = 128) and the LLM adapter
+// (d = 64, self and cross) attend over a few hundred tokens once per prompt; the reference runs
+// them through the same flashAttentionShader with `group` and `causal` (kernels.js:147-299).
+// Here a CUDA-core kernel: a CTA takes 16 queries of one head (4 per warp), streams the keys and
+// values in 32-key tiles through shared memory (fp32), each lane scores one key of the tile for
+// the warp's 4 queries, and the online softmax (running max and sum, exp2 domain) accumulates
+// D / 32 output dimensions per lane.
+namespace tattn {
+
+constexpr int KT = 32;
+constexpr int QPW = 4;
+constexpr int WARPS = 4;
+constexpr int QPC = QPW * WARPS;
+
+struct Args {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* out;
+  long long ldq, ldk, ldv, ldo, q_bs, k_bs, v_bs, o_bs;
+  int q_off, k_off, v_off;
+  int Lq, Lk, group, causal, kv_bcast;
+  const int* key_len;
+  float scale_log2;
+};
+
+__device__ __forceinline__ float cvt_in(float v) { return v; }
+__device__ __forceinline__ float cvt_in(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ float cvt_in(__half v) { return __half2float(v); }
+template <typename T>
+__device__ __forceinline__ T cvt_out(float v);
+template <>
+__device__ __forceinline__ float cvt_out<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 cvt_out<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+template <>
+__device__ __forceinline__ __half cvt_out<__half>(float v) { return __float2half_rn(v); }
+
+template <typename TI, typename TO, int D>
+__global__ void __launch_bounds__(WARPS * 32) text_attention_kernel(const Args a) {
+  __shared__ float ks[KT][D + 1];  // +1: lane j reads row j, so the column walk is conflict-free
+  __shared__ float vs[KT][D];
+  __shared__ float qs[QPC][D];
+  constexpr int DPL = D / 32;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.z, h = blockIdx.y, q0 = blockIdx.x * QPC;
+  const int hk = h / a.group;
+  const int kb = a.kv_bcast ? 0 : b;
+  const TI* Q = static_cast<const TI*>(a.q) + b * a.q_bs + a.q_off + static_cast<long long>(h) * D;
+  const TI* K = static_cast<const TI*>(a.k) + kb * a.k_bs + a.k_off + static_cast<long long>(hk) * D;
+  const TI* V = static_cast<const TI*>(a.v) + kb * a.v_bs + a.v_off + static_cast<long long>(hk) * D;
+  int kend = a.Lk;
+  if (a.key_len) kend = min(kend, a.key_len[kb]);
+  if (a.causal) kend = min(kend, min(q0 + QPC, a.Lq));  // keys past the CTA's last query stay hidden
+  for (int i = threadIdx.x; i < QPC * D; i += WARPS * 32) {
+    const int r = i / D, c = i % D, qi = q0 + r;
+    qs[r][c] = qi < a.Lq ? cvt_in(Q[qi * a.ldq + c]) * a.scale_log2 : 0.f;
+  }
+  float m[QPW], l[QPW], o[QPW][DPL];
+#pragma unroll
+  for (int u = 0; u < QPW; ++u) {
+    m[u] = -INFINITY;
+    l[u] = 0.f;
+#pragma unroll
+    for (int d = 0; d < DPL; ++d) o[u][d] = 0.f;
+  }
+  for (int k0 = 0; k0 < kend; k0 += KT) {
+    __syncthreads();  // the previous tile is consumed (and the queries are in place)
+    for (int i = threadIdx.x; i < KT * D; i += WARPS * 32) {
+      const int r = i / D, c = i % D, kj = k0 + r;
+      const bool in = kj < kend;
+      ks[r][c] = in ? cvt_in(K[kj * a.ldk + c]) : 0.f;
+      vs[r][c] = in ? cvt_in(V[kj * a.ldv + c]) : 0.f;
+    }
+    __syncthreads();
+    const int kj = k0 + lane;
+    float sc[QPW];
+#pragma unroll
+    for (int u = 0; u < QPW; ++u) sc[u] = 0.f;
+#pragma unroll 8
+    for (int c = 0; c < D; ++c) {
+      const float kc = ks[lane][c];
+#pragma unroll
+      for (int u = 0; u < QPW; ++u) sc[u] = fmaf(qs[warp * QPW + u][c], kc, sc[u]);
+    }
+#pragma unroll
+    for (int u = 0; u < QPW; ++u) {
+      const int qi = q0 + warp * QPW + u;
+      const bool ok = kj < kend && (!a.causal || kj <= qi);
+      float mx = ok ? sc[u] : -INFINITY;
+#pragma unroll
+      for (int s = 16; s > 0; s >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, s));
+      const float mnew = fmaxf(m[u], mx);
+      if (mnew == -INFINITY) continue;  // nothing visible to this query yet (warp-uniform)
+      const float corr = exp2f(m[u] - mnew);  // 0 on the first visible tile (m = -inf)
+      const float p = ok ? exp2f(sc[u] - mnew) : 0.f;
+      float ps = p;
+#pragma unroll
+      for (int s = 16; s > 0; s >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, s);
+      l[u] = l[u] * corr + ps;
+#pragma unroll
+      for (int d = 0; d < DPL; ++d) o[u][d] *= corr;
+#pragma unroll 8
+      for (int j = 0; j < KT; ++j) {
+        const float pj = __shfl_sync(0xffffffffu, p, j);
+#pragma unroll
+        for (int d = 0; d < DPL; ++d) o[u][d] = fmaf(pj, vs[j][lane + 32 * d], o[u][d]);
+      }
+      m[u] = mnew;
+    }
+  }
+  TO* out = static_cast<TO*>(a.out) + b * a.o_bs + static_cast<long long>(h) * D;
+#pragma unroll
+  for (int u = 0; u < QPW; ++u) {
+    const int qi = q0 + warp * QPW + u;
+    if (qi >= a.Lq) continue;
+    const float inv = l[u] > 0.f ? 1.0f / l[u] : 0.f;  // no visible key (key_len 0): zeros
+#pragma unroll
+    for (int d = 0; d < DPL; ++d) out[qi * a.ldo + lane + 32 * d] = cvt_out<TO>(o[u][d] * inv);
+  }
+}
+
+template <typename TI, int D>
+void launch_out(const Args& a, int out_dtype, dim3 grid, cudaStream_t st) {
+  if (out_dtype == ANIMA_F32)
+    text_attention_kernel<TI, float, D><<<grid, WARPS * 32, 0, st>>>(a);
+  else if (out_dtype == ANIMA_BF16)
+    text_attention_kernel<TI, __nv_bfloat16, D><<<grid, WARPS * 32, 0, st>>>(a);
+  else
+    text_attention_kernel<TI, __half, D><<<grid, WARPS * 32, 0, st>>>(a);
+}
+
+template <int D>
+void launch_in(const Args& a, int in_dtype, int out_dtype, dim3 grid, cudaStream_t st) {
+  if (in_dtype == ANIMA_F32)
+    launch_out<float, D>(a, out_dtype, grid, st);
+  else if (in_dtype == ANIMA_BF16)
+    launch_out<__nv_bfloat16, D>(a, out_dtype, grid, st);
+  else
+    launch_out<__half, D>(a, out_dtype, grid, st);
+}
+
+}  // namespace tattn
+
 using namespace anima;
 
 namespace {
+
+int text_attention(anima_ctx* ctx, const anima_attention_args* a, int group) {
+  ANIMA_REQUIRE(a->head_dim == 64 || a->head_dim == 128, "anima_attention: head_dim %d (64 or 128)", a->head_dim);
+  ANIMA_REQUIRE(a->heads % group == 0, "anima_attention: %d heads do not form groups of %d", a->heads, group);
+  const long long hd = a->head_dim;
+  const long long kv_cols = static_cast<long long>(a->heads / group) * hd;
+  ANIMA_REQUIRE(a->ldq >= a->q_off + a->heads * hd && a->ldk >= a->k_off + kv_cols && a->ldv >= a->v_off + kv_cols &&
+                    a->ldo >= a->heads * hd && a->q_off >= 0 && a->k_off >= 0 && a->v_off >= 0,
+                "anima_attention: row strides too small for %d heads (%lld k/v columns)", a->heads, kv_cols);
+  const bool kv_bcast = a->batch > 1 && a->k_bstride == 0 && a->v_bstride == 0;
+  tattn::Args t{};
+  t.q = a->q;
+  t.k = a->k;
+  t.v = a->v;
+  t.out = a->out;
+  t.ldq = a->ldq;
+  t.ldk = a->ldk;
+  t.ldv = a->ldv;
+  t.ldo = a->ldo;
+  t.q_bs = a->batch > 1 ? a->q_bstride : 0;
+  t.k_bs = a->batch > 1 ? a->k_bstride : 0;
+  t.v_bs = a->batch > 1 ? a->v_bstride : 0;
+  t.o_bs = a->batch > 1 ? a->o_bstride : 0;
+  t.q_off = a->q_off;
+  t.k_off = a->k_off;
+  t.v_off = a->v_off;
+  t.Lq = a->Lq;
+  t.Lk = a->Lk;
+  t.group = group;
+  t.causal = a->causal ? 1 : 0;
+  t.kv_bcast = kv_bcast ? 1 : 0;
+  t.key_len = a->key_len;
+  const float scale = a->scale > 0.f ? a->scale : 1.0f / sqrtf(static_cast<float>(a->head_dim));
+  t.scale_log2 = scale * 1.4426950408889634f;
+  const dim3 grid((a->Lq + tattn::QPC - 1) / tattn::QPC, a->heads, a->batch);
+  ANIMA_REQUIRE(grid.y <= 65535 && grid.z <= 65535, "anima_attention: too many heads or batch items");
+  ProfScope prof(ctx, "attn.text", 4.0 * a->batch * a->heads * static_cast<double>(a->Lq) * a->Lk * a->head_dim, 0);
+  if (a->head_dim == 128)
+    tattn::launch_in<128>(t, a->dtype, a->out_dtype, grid, ctx->stream);
+  else
+    tattn::launch_in<64>(t, a->dtype, a->out_dtype, grid, ctx->stream);
+  return check_launch("text_attention_kernel");
+}
 
 // static_ws: the stream-K workspace comes from the module's static device array (no allocation)
 // instead of the context's lazily allocated one.
 int attention_launch(anima_ctx* ctx, const anima_attention_args* a, bool static_ws) {
   ANIMA_REQUIRE(ctx && a, "anima_attention: NULL argument");
   ANIMA_ON_DEVICE(ctx);
-  ANIMA_REQUIRE(a->head_dim == attn::HD, "anima_attention: head_dim %d (only 128)", a->head_dim);
-  ANIMA_REQUIRE(a->dtype == ANIMA_BF16 || a->dtype == ANIMA_F16, "anima_attention: q/k/v dtype must be bf16 or f16");
   ANIMA_REQUIRE(a->out_dtype == ANIMA_F32 || a->out_dtype == ANIMA_BF16 || a->out_dtype == ANIMA_F16,
                 "anima_attention: out_dtype %d", a->out_dtype);
   ANIMA_REQUIRE(a->batch > 0 && a->heads > 0 && a->Lq > 0 && a->Lk > 0, "anima_attention: empty problem");
   ANIMA_REQUIRE(a->q && a->k && a->v && a->out, "anima_attention: NULL data pointer");
+  const int group = a->group > 1 ? a->group : 1;
+  if (group > 1 || a->causal || a->head_dim != attn::HD || a->dtype == ANIMA_F32) {
+    ANIMA_REQUIRE(a->dtype == ANIMA_F32 || a->dtype == ANIMA_BF16 || a->dtype == ANIMA_F16,
+                  "anima_attention: q/k/v dtype %d", a->dtype);
+    return text_attention(ctx, a, group);  // no workspace either way
+  }
+  ANIMA_REQUIRE(a->dtype == ANIMA_BF16 || a->dtype == ANIMA_F16, "anima_attention: q/k/v dtype must be bf16 or f16");
   const long long cols_q = a->q_off + static_cast<long long>(a->heads) * a->head_dim;
   const long long cols_k = a->k_off + static_cast<long long>(a->heads) * a->head_dim;
   const long long cols_v = a->v_off + static_cast<long long>(a->heads) * a->head_dim;

@@ -260,7 +260,7 @@ template <int COLS>
 struct RowGeom {
   static constexpr int NG = COLS / 256;
   static constexpr bool HALF = NG == 1;
-  static constexpr int G2 = NG >= 4 ? 2 : 1;
+  static constexpr int G2 = NG % 3 == 0 ? 3 : (NG >= 4 ? 2 : 1);  // 3072 (Qwen3's MLP): 3 passes, 2 warps
   static constexpr int WPR = HALF ? 1 : NG / (2 * G2);
   static constexpr int RPC = HALF ? 16 : 8 / WPR;  // rows per 256-thread CTA
   static_assert(COLS % 256 == 0 && NG <= 64 && (HALF || NG % (2 * G2) == 0) && WPR <= 8, "unsupported row width");
@@ -823,10 +823,11 @@ int launch_rows(anima_ctx* ctx, const TIn* x, int rows, int cols, int ldx, const
     ROWS_CASE(512)
     ROWS_CASE(1024)
     ROWS_CASE(2048)
+    ROWS_CASE(3072)
     ROWS_CASE(4096)
     ROWS_CASE(8192)
     default:
-      return set_error(ANIMA_ERR_UNSUPPORTED, "row kernel: cols=%d (supported: 256, 512, 1024, 2048, 4096, 8192)", cols);
+      return set_error(ANIMA_ERR_UNSUPPORTED, "row kernel: cols=%d (supported: 256, 512, 1024, 2048, 3072, 4096, 8192)", cols);
   }
 #undef ROWS_CASE
   return check_launch("rows_kernel");

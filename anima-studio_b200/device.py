@@ -80,7 +80,7 @@ class AttentionArgs(C.Structure):
                 ("k", C.c_void_p), ("ldk", C.c_longlong), ("k_bstride", C.c_longlong), ("k_off", C.c_int),
                 ("v", C.c_void_p), ("ldv", C.c_longlong), ("v_bstride", C.c_longlong), ("v_off", C.c_int),
                 ("out", C.c_void_p), ("ldo", C.c_longlong), ("o_bstride", C.c_longlong), ("out_dtype", C.c_int),
-                ("key_len", C.c_void_p), ("scale", C.c_float)]
+                ("key_len", C.c_void_p), ("scale", C.c_float), ("group", C.c_int), ("causal", C.c_int)]
 
 
 _lib = None

@@ -246,14 +246,16 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, Lq: int, Lk:
               k_off: int = 0, v_off: int = 0, batch: int = 1, q_bstride: int = 0, k_bstride: int = 0,
               v_bstride: int = 0, key_len: torch.Tensor | None = None, out: torch.Tensor | None = None,
               out_dtype=None, o_bstride: int | None = None, scale: float | None = None,
-              name: str | None = None, noalloc: bool = False) -> torch.Tensor:
+              name: str | None = None, noalloc: bool = False, group: int = 1, causal: bool = False) -> torch.Tensor:
     """Non-causal multi-head attention (ops.js:166-208): q [.., ldq] with head h at q_off + h D,
     k/v likewise; output [batch * Lq, H D]. q/k/v are bf16 or fp16; key_len (int32 [batch]) masks
     keys past each item's text length. noalloc: the entry point whose stream-K workspace is the
-    library's static device array (no allocation; calls must not overlap)."""
+    library's static device array (no allocation; calls must not overlap). group: q heads per k/v
+    head (GQA); causal: query i sees keys j <= i; with either, or D = 64, or fp32 q/k/v, the
+    text-model kernel runs (ops.js:166-208 takes the same `group` and `causal`)."""
     ldq = ldq or H * D
-    ldk = ldk or H * D
-    ldv = ldv or H * D
+    ldk = ldk or (H // max(group, 1)) * D
+    ldv = ldv or (H // max(group, 1)) * D
     if out is None:
         out = torch.empty(batch * Lq, H * D, dtype=out_dtype or q.dtype, device=q.device)
     a = dev.AttentionArgs()
@@ -267,6 +269,7 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, Lq: int, Lk:
     a.out_dtype = _dt(out)
     a.key_len = key_len.data_ptr() if key_len is not None else 0
     a.scale = scale if scale is not None else 1.0 / math.sqrt(D)
+    a.group, a.causal = int(group), 1 if causal else 0
     ctx_for(q).call("anima_attention_noalloc" if noalloc else "anima_attention", C.byref(a), tag=name,
                     work=4.0 * batch * Lq * Lk * D * H)
     return out

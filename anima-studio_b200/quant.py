@@ -63,6 +63,18 @@ def quantize_int8_convrot(weight: torch.Tensor) -> dict:
     }
 
 
+def quantize_int8_rows(weight: torch.Tensor) -> dict:
+    """Per-row int8 without rotation, the layout of embedding tables (rows are gathered, never
+    multiplied; quant.py:70-78): scale = amax_row / 127, q = clamp(rne(w / scale), -128, 127)."""
+    w = weight.float()
+    scale = (w.abs().amax(dim=1, keepdim=True) / 127.0).clamp(min=1e-30)
+    return {
+        "weight": (w / scale).round().clamp(-128, 127).to(torch.int8).contiguous(),
+        "weight_scale": scale.contiguous(),
+        "comfy_quant": comfy_meta("int8_tensorwise"),
+    }
+
+
 def _nearest_level(x: torch.Tensor, levels: torch.Tensor) -> torch.Tensor:
     """Index of the nearest sorted level; ties go to the lower one (quant.py:88-95)."""
     last = levels.numel() - 1

@@ -159,3 +159,70 @@ def lora_tensors(seed: int, targets, rank: int = 32, std: float = 0.01, n_blocks
             if alpha is not None:
                 out[mod + ".alpha"] = torch.tensor(float(alpha))
     return out
+
+
+# ----------------------------------------------------------------------------- text models
+# Qwen3-0.6B (app/models/qwen3.js:7) and the LLM adapter (tools/reference.py:139-169). The
+# published files keep Qwen3's attention and MLP linears quantized (int8 ConvRot or W4A8), its
+# embedding table as per-row int8, and the adapter in bf16 (tools/build_assets.py:66-69, 130-157).
+QWEN3 = {"layers": 28, "hidden": 1024, "heads": 16, "kv_heads": 8, "head_dim": 128, "mlp": 3072, "vocab": 151936,
+         "theta": 1e6}
+ADAPTER = {"blocks": 6, "hidden": 1024, "heads": 16, "head_dim": 64, "mlp": 4096, "vocab": 32128, "theta": 1e4}
+
+
+def te_tensors(seed: int, n_layers: int = QWEN3["layers"], vocab: int = QWEN3["vocab"], fmt: str = "int8",
+               device="cpu", direct: bool = False) -> dict:
+    """A synthetic Qwen3 text-encoder file (names as the reference's te asset): linears N(0, 0.02)
+    quantized with the ConvRot quantizers (direct=True: drawn in the stored format, see
+    direct_linear), the embedding N(0, 1) as per-row int8, norm weights 1 + N(0, 0.02) in bf16.
+    vocab may be cut down for tests (ids must stay below it)."""
+    D, HD = QWEN3["hidden"], QWEN3["head_dim"]
+    shapes = {"self_attn.q_proj": (QWEN3["heads"] * HD, D), "self_attn.k_proj": (QWEN3["kv_heads"] * HD, D),
+              "self_attn.v_proj": (QWEN3["kv_heads"] * HD, D), "self_attn.o_proj": (D, QWEN3["heads"] * HD),
+              "mlp.gate_proj": (QWEN3["mlp"], D), "mlp.up_proj": (QWEN3["mlp"], D), "mlp.down_proj": (D, QWEN3["mlp"])}
+    out = {}
+    for k, v in quant.quantize_int8_rows(randn(seed, "te.embed", (vocab, D), device)).items():
+        out["model.embed_tokens." + k] = v
+    for i in range(n_layers):
+        p = f"model.layers.{i}."
+        for mod, shape in shapes.items():
+            make = direct_linear if direct else quantized_linear
+            for k, v in make(seed, p + mod, shape, fmt if fmt == "int8" else "w4a8", device).items():
+                out[p + mod + "." + k] = v
+        for n, size in (("input_layernorm", D), ("post_attention_layernorm", D), ("self_attn.q_norm", HD),
+                        ("self_attn.k_norm", HD)):
+            name = p + n + ".weight"
+            out[name] = (1 + randn(seed, name, (size,), device, 0.02)).to(torch.bfloat16)
+    out["model.norm.weight"] = (1 + randn(seed, "model.norm.weight", (D,), device, 0.02)).to(torch.bfloat16)
+    return out
+
+
+def adapter_tensors(seed: int, n_blocks: int = ADAPTER["blocks"], vocab: int = ADAPTER["vocab"], device="cpu") -> dict:
+    """A synthetic LLM adapter (the "llm_adapter." tensors of the DiT file), all bf16: linears
+    N(0, 0.02), biases N(0, 0.02), the T5-vocabulary embedding N(0, 1), norms 1 + N(0, 0.02)."""
+    D, HD, F = ADAPTER["hidden"], ADAPTER["head_dim"], ADAPTER["mlp"]
+    out = {}
+
+    def bf(name, shape, std=0.02, one=False):
+        t = randn(seed, name, shape, device, std)
+        out[name] = (t + 1 if one else t).to(torch.bfloat16)
+
+    p0 = "llm_adapter."
+    bf(p0 + "embed.weight", (vocab, D), 1.0)
+    for i in range(n_blocks):
+        p = f"{p0}blocks.{i}."
+        for a in ("self_attn", "cross_attn"):
+            for n in ("q_proj", "k_proj", "v_proj", "o_proj"):
+                bf(f"{p}{a}.{n}.weight", (D, D))
+            bf(f"{p}{a}.q_norm.weight", (HD,), one=True)
+            bf(f"{p}{a}.k_norm.weight", (HD,), one=True)
+        for n in ("norm_self_attn", "norm_cross_attn", "norm_mlp"):
+            bf(f"{p}{n}.weight", (D,), one=True)
+        bf(p + "mlp.0.weight", (F, D))
+        bf(p + "mlp.0.bias", (F,))
+        bf(p + "mlp.2.weight", (D, F))
+        bf(p + "mlp.2.bias", (D,))
+    bf(p0 + "out_proj.weight", (D, D))
+    bf(p0 + "out_proj.bias", (D,))
+    bf(p0 + "norm.weight", (D,), one=True)
+    return out

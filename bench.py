@@ -436,6 +436,42 @@ def measure_seq(dit, seed, steps, warmup, world, rank, exchange="peer"):
             "steps_per_s": steps / (ms * 1e-3), "ms_per_step": ms / steps, "steps": steps, "scaling": "strong"}
 
 
+def one_plane_probe(dit, cond, tc):
+    """The one-plane (W8A8, precision "a8") form of the 2048->8192 linear, where the north star's
+    int8 tensor-core fraction is defined, and what that precision does to one DiT block at
+    L = 4096: the block output's relative L2 distance from the default two-plane path (itself
+    within ~3e-4 of the reference at this size)."""
+    import torch
+
+    ops, syn = pkg("ops"), pkg("synthetic")
+    M, K = 4096, 2048
+    w = dit.blocks[0]["l1"]
+    x = syn.randn(7, "probe.x", (M, K)).cuda()
+    q1 = ops.rotate_quant(x, 1)
+    out = torch.empty(M, w.N, dtype=torch.float16, device="cuda")
+    for _ in range(3):
+        ops.linear(q1, w, out=out)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(20):
+        ops.linear(q1, w, out=out)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / 20
+    res = {}
+    xb = syn.randn(7, "probe.block", (M, 2048)).cuda()
+    cs = dit.rope(64, 64)
+    for planes in (2, 1):
+        dit.planes, dit._bufs = planes, {}
+        y = xb.clone()
+        dit.block(0, y, cond, tc, 1, M, cs, dit._buffers(M))
+        res[planes] = y
+    dit.planes, dit._bufs = 2, {}
+    err = float((res[1] - res[2]).norm() / res[2].norm())
+    return {"launch_ms": ms, "achieved": 2.0 * M * w.N * K / (ms * 1e-3) / 1e12, "block_rel_l2_vs_a16": err}
+
+
 def load_model(args, seed, fmt="int8"):
     import torch
 
@@ -701,6 +737,7 @@ def main():
         if world > 1:
             subs["tp"] = measure_seq(dit, seed, 16, 3, world, rank)
             subs["tp"]["nccl_exchange"] = measure_seq(dit, seed, 16, 3, world, rank, "nccl")
+    a8 = one_plane_probe(dit, cond, tcs[0]) if rank == 0 and headline and args.precision == "a16" else None
     int8_peak = measure_int8_peak(torch) if rank == 0 else None
     dist.destroy_process_group() if world > 1 else None
     if rank != 0:
@@ -744,10 +781,13 @@ def main():
                           if att_ms and peaks.get("bf16_tflops") else None},
             "per_op_ms_per_step": {f"{k[0].replace('anima_', '')}:{k[1]}": round(v[1] / replay_steps, 3)
                                    for k, v in sorted(summ.items(), key=lambda kv: -kv[1][1])},
+            "one_plane": dict(a8, frac=a8["achieved"] / int8_peak if int8_peak else None) if a8 else None,
             "note": "achieved = algorithmic 2MNK ops per launch / CUDA-event time per launch, measured on the "
                     "launching stream in an instrumented replay of the timed steps; a16 runs two int8 MMAs per "
-                    "product, so hw_ops_frac = planes x frac; traffic = DRAM bytes per launch from the ncu capture "
-                    "in profiles/gemm_i8_mlp1_L4096.md"}
+                    "product, so its frac is capped at 0.5 by construction and hw_ops_frac = planes x frac; "
+                    "one_plane = the same linear with one int8 activation plane (W8A8, the north star's int8 "
+                    "figure), timed alone, with its DiT-block error against the a16 path; traffic = DRAM bytes per "
+                    "launch from the ncu capture in profiles/gemm_i8_mlp1_L4096.md"}
     metric, workload = METRIC, WORKLOAD
     if not headline:
         metric = ("DiT denoise steps/sec at 1024^2 (4096 tokens), 28-block W4A8-mixed ConvRot DiT"

@@ -121,7 +121,8 @@ typedef struct {
 
 typedef struct {
   int batch, heads, head_dim, Lq, Lk;
-  int dtype;               /* ANIMA_BF16 or ANIMA_F16 for q/k/v */
+  int dtype;               /* ANIMA_BF16 or ANIMA_F16 for q/k/v (ANIMA_F32 too when group > 1,
+                              causal or head_dim 64: the text models' path) */
   const void* q; long long ldq, q_bstride; int q_off;
   const void* k; long long ldk, k_bstride; int k_off;
   const void* v; long long ldv, v_bstride; int v_off;
@@ -129,6 +130,8 @@ typedef struct {
   const int* key_len;      /* [batch] keys >= key_len[b] are masked; NULL = all Lk keys.
                               k_bstride == v_bstride == 0 with batch > 1 shares one K/V and key_len[0]. */
   float scale;             /* softmax scale, 1/sqrt(head_dim) in the reference */
+  int group;               /* q heads per k/v head (GQA, ops.js:166 `group`); 0 or 1 = none */
+  int causal;              /* key j visible to query i only when j <= i (ops.js:166 `causal`) */
 } anima_attention_args;
 
 /* ---------------------------------------------------------------- runtime (device.js GPU) */
@@ -211,8 +214,11 @@ int anima_qk_norm_rope(anima_ctx* ctx, void* qkv, int dtype, int L, int H, int D
 /* ops.rope (ops.js:148-152, kernels.js:336-357), in place on x viewed as [L, H, D] at colOff. */
 int anima_rope(anima_ctx* ctx, void* x, int dtype, int L, int H, int D, int row_stride, int col_off,
                const float* rope, int rope_rows);
-/* ops.attention (ops.js:166-208, kernels.js:147-299): non-causal multi-head attention, tcgen05
- * flash kernel, fp32 softmax. head_dim must be 128.
+/* ops.attention (ops.js:166-208, kernels.js:147-299): multi-head attention with fp32 softmax.
+ * Non-causal, head_dim 128, one k/v head per q head (the DiT's attentions): the tcgen05 flash
+ * kernel. Causal, grouped k/v heads or head_dim 64 (the Qwen3 text encoder and the LLM adapter,
+ * a few hundred tokens): a CUDA-core kernel over 32-key tiles in shared memory, which also takes
+ * fp32 q/k/v.
  * The stream-K schedule (see anima_ctx_set_attention_split) launches one CTA per SM and lets a CTA
  * wait, bounded at 2 s, for a partial result written by a lower-numbered CTA; it therefore needs
  * all of the device's SMs to be available to this kernel at once. Where other work can hold SMs

@@ -176,11 +176,32 @@ def full_size_fixtures(quant, R, syn):
     print("mixed + LoRA done", flush=True)
 
 
+def text_fixtures(quant, R, syn):
+    """The text conditioning through the reference's own qwen3 and llm_adapter
+    (tools/reference.py:116-169): a 28-layer INT8 ConvRot Qwen3 and the 6-block bf16 adapter with
+    synthetic weights (vocabularies cut to 4096 rows: the ids stay below), 77 Qwen3 tokens and 60
+    T5 tokens drawn from a seeded generator. Keeps the ids, the Qwen3 hidden states and the
+    adapter's first 60 rows (the rest is zero padding to 512)."""
+    seed, vocab = 51, 4096
+    g = torch.Generator().manual_seed(seed)
+    qids = torch.randint(0, vocab, (77,), generator=g).tolist()
+    tids = torch.randint(0, vocab, (60,), generator=g).tolist()
+    Wte = RefWeights(quant, lambda i: {}, syn.te_tensors(seed, 28, vocab, direct=True))
+    hs = R.qwen3(Wte, qids)
+    Wad = RefWeights(quant, lambda i: {}, syn.adapter_tensors(seed, 6, vocab))
+    ctx = R.llm_adapter(Wad, hs, tids)
+    assert ctx.shape == (512, 1024) and float(ctx[60:].abs().max()) == 0.0
+    np.savez_compressed(os.path.join(HERE, "text_1024.npz"), seed=seed, vocab=vocab, qwen_ids=np.array(qids),
+                        t5_ids=np.array(tids), hidden=hs.numpy(), ctx60=ctx[:60].numpy())
+    print("text done", flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("ANIMA_REFERENCE"))
-    ap.add_argument("--only", choices=["small", "full"], default=None,
-                    help="small: sections 1-5 (L = 64 and the quantizers); full: the 1024^2 fixtures")
+    ap.add_argument("--only", choices=["small", "full", "text"], default=None,
+                    help="small: sections 1-5 (L = 64 and the quantizers); full: the 1024^2 fixtures; "
+                         "text: the Qwen3 + LLM adapter fixture")
     args = ap.parse_args()
     if not args.ref:
         ap.error("give the reference checkout with --ref or ANIMA_REFERENCE")
@@ -190,6 +211,9 @@ def main():
     torch.set_grad_enabled(False)
     if args.only == "full":
         full_size_fixtures(quant, R, syn)
+        return
+    if args.only == "text":
+        text_fixtures(quant, R, syn)
         return
 
     # 1. int8 ConvRot quantizer + dequantizer (tools/quant.py:59-67, 81-83)
@@ -298,6 +322,7 @@ def main():
         print("forward", fmt, "done", flush=True)
     if args.only is None:
         full_size_fixtures(quant, R, syn)
+        text_fixtures(quant, R, syn)
     print("golden fixtures written to", HERE)
 
 

@@ -125,3 +125,19 @@ def test_beta_scheduler_matches_reference_algorithm():
     for steps in (1, 3, 4, 8, 12, 20, 30, 50):
         for shift in (1.0, 3.0, 6.0):
             assert pl.sigmas_beta(steps, shift) == samplers_np.sigmas_beta(steps, shift)
+
+
+def test_text_oracle_matches_reference_fixture():
+    """The numpy Qwen3 + LLM adapter (oracle/text_np.py) against tools/reference.py's qwen3 and
+    llm_adapter on the same synthetic weights (tests/golden/text_1024.npz)."""
+    from oracle import text_np
+
+    g = load("text_1024.npz")
+    seed, vocab = int(g["seed"]), int(g["vocab"])
+    syn = pkg("synthetic")
+    W = oracle.DequantWeights(oracle.to_numpy(syn.te_tensors(seed, 28, vocab, direct=True)))
+    hs = text_np.qwen3(W, g["qwen_ids"])
+    assert rel_l2(hs, g["hidden"]) < 1e-5
+    Wa = oracle.DequantWeights(oracle.to_numpy(syn.adapter_tensors(seed, 6, vocab)))
+    ctx = text_np.llm_adapter(Wa, g["hidden"], g["t5_ids"])
+    assert rel_l2(ctx[:60], g["ctx60"]) < 1e-5 and not ctx[60:].any()
