@@ -10,7 +10,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libanima_b200.so")
-SOURCES = ["anima_b200.cu", "runtime.cu", "rowops.cu", "gemm_i8.cu", "attention.cu", "peer.cu", "sm100.cuh", "internal.h"]
+SOURCES = ["anima_b200.cu", "runtime.cu", "rowops.cu", "gemm_i8.cu", "attention.cu", "peer.cu", "vae.cu", "sm100.cuh", "internal.h"]
 HEADER = os.path.join(os.path.dirname(HERE), "include", "anima_b200.h")
 
 

@@ -5,3 +5,4 @@
 #include "gemm_i8.cu"
 #include "attention.cu"
 #include "peer.cu"
+#include "vae.cu"

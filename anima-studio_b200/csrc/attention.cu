@@ -769,11 +769,19 @@ __device__ __forceinline__ __nv_bfloat16 cvt_out<__nv_bfloat16>(float v) { retur
 template <>
 __device__ __forceinline__ __half cvt_out<__half>(float v) { return __float2half_rn(v); }
 
+// Shared memory: K tile [KT][D + 1] (+1: lane j reads row j, so the column walk is conflict-free),
+// V tile [KT][D], the CTA's queries [QPC][D]; fp32. 41 KB at D = 128, 123 KB at D = 384.
+template <int D>
+constexpr int smem_bytes() {
+  return (KT * (D + 1) + KT * D + QPC * D) * 4;
+}
+
 template <typename TI, typename TO, int D>
 __global__ void __launch_bounds__(WARPS * 32) text_attention_kernel(const Args a) {
-  __shared__ float ks[KT][D + 1];  // +1: lane j reads row j, so the column walk is conflict-free
-  __shared__ float vs[KT][D];
-  __shared__ float qs[QPC][D];
+  extern __shared__ float sm[];
+  float(*ks)[D + 1] = reinterpret_cast<float(*)[D + 1]>(sm);
+  float(*vs)[D] = reinterpret_cast<float(*)[D]>(sm + KT * (D + 1));
+  float(*qs)[D] = reinterpret_cast<float(*)[D]>(sm + KT * (D + 1) + KT * D);
   constexpr int DPL = D / 32;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.z, h = blockIdx.y, q0 = blockIdx.x * QPC;
@@ -853,24 +861,29 @@ __global__ void __launch_bounds__(WARPS * 32) text_attention_kernel(const Args a
   }
 }
 
+template <typename TI, typename TO, int D>
+int launch_typed(const Args& a, dim3 grid, cudaStream_t st) {
+  const auto fn = text_attention_kernel<TI, TO, D>;
+  if (smem_bytes<D>() > 48 * 1024) {
+    const int e = anima::set_max_dynamic_smem(reinterpret_cast<const void*>(fn), smem_bytes<D>());
+    if (e) return e;
+  }
+  fn<<<grid, WARPS * 32, smem_bytes<D>(), st>>>(a);
+  return ANIMA_OK;
+}
+
 template <typename TI, int D>
-void launch_out(const Args& a, int out_dtype, dim3 grid, cudaStream_t st) {
-  if (out_dtype == ANIMA_F32)
-    text_attention_kernel<TI, float, D><<<grid, WARPS * 32, 0, st>>>(a);
-  else if (out_dtype == ANIMA_BF16)
-    text_attention_kernel<TI, __nv_bfloat16, D><<<grid, WARPS * 32, 0, st>>>(a);
-  else
-    text_attention_kernel<TI, __half, D><<<grid, WARPS * 32, 0, st>>>(a);
+int launch_out(const Args& a, int out_dtype, dim3 grid, cudaStream_t st) {
+  if (out_dtype == ANIMA_F32) return launch_typed<TI, float, D>(a, grid, st);
+  if (out_dtype == ANIMA_BF16) return launch_typed<TI, __nv_bfloat16, D>(a, grid, st);
+  return launch_typed<TI, __half, D>(a, grid, st);
 }
 
 template <int D>
-void launch_in(const Args& a, int in_dtype, int out_dtype, dim3 grid, cudaStream_t st) {
-  if (in_dtype == ANIMA_F32)
-    launch_out<float, D>(a, out_dtype, grid, st);
-  else if (in_dtype == ANIMA_BF16)
-    launch_out<__nv_bfloat16, D>(a, out_dtype, grid, st);
-  else
-    launch_out<__half, D>(a, out_dtype, grid, st);
+int launch_in(const Args& a, int in_dtype, int out_dtype, dim3 grid, cudaStream_t st) {
+  if (in_dtype == ANIMA_F32) return launch_out<float, D>(a, out_dtype, grid, st);
+  if (in_dtype == ANIMA_BF16) return launch_out<__nv_bfloat16, D>(a, out_dtype, grid, st);
+  return launch_out<__half, D>(a, out_dtype, grid, st);
 }
 
 }  // namespace tattn
@@ -880,7 +893,8 @@ using namespace anima;
 namespace {
 
 int text_attention(anima_ctx* ctx, const anima_attention_args* a, int group) {
-  ANIMA_REQUIRE(a->head_dim == 64 || a->head_dim == 128, "anima_attention: head_dim %d (64 or 128)", a->head_dim);
+  ANIMA_REQUIRE(a->head_dim == 64 || a->head_dim == 128 || a->head_dim == 384,
+                "anima_attention: head_dim %d (64, 128 or 384)", a->head_dim);
   ANIMA_REQUIRE(a->heads % group == 0, "anima_attention: %d heads do not form groups of %d", a->heads, group);
   const long long hd = a->head_dim;
   const long long kv_cols = static_cast<long long>(a->heads / group) * hd;
@@ -915,10 +929,10 @@ int text_attention(anima_ctx* ctx, const anima_attention_args* a, int group) {
   const dim3 grid((a->Lq + tattn::QPC - 1) / tattn::QPC, a->heads, a->batch);
   ANIMA_REQUIRE(grid.y <= 65535 && grid.z <= 65535, "anima_attention: too many heads or batch items");
   ProfScope prof(ctx, "attn.text", 4.0 * a->batch * a->heads * static_cast<double>(a->Lq) * a->Lk * a->head_dim, 0);
-  if (a->head_dim == 128)
-    tattn::launch_in<128>(t, a->dtype, a->out_dtype, grid, ctx->stream);
-  else
-    tattn::launch_in<64>(t, a->dtype, a->out_dtype, grid, ctx->stream);
+  int st = a->head_dim == 128   ? tattn::launch_in<128>(t, a->dtype, a->out_dtype, grid, ctx->stream)
+           : a->head_dim == 384 ? tattn::launch_in<384>(t, a->dtype, a->out_dtype, grid, ctx->stream)
+                                : tattn::launch_in<64>(t, a->dtype, a->out_dtype, grid, ctx->stream);
+  if (st) return st;
   return check_launch("text_attention_kernel");
 }
 

@@ -34,7 +34,7 @@ EXPORTS = [
     "anima_attention", "anima_attention_noalloc", "anima_elementwise", "anima_zero", "anima_patchify", "anima_unpatchify",
     "anima_timestep_embedding", "anima_euler_step", "anima_lincomb", "anima_selftest_wait_timeout",
     "anima_ctx_set_attention_split", "anima_ipc_alloc", "anima_ipc_open", "anima_ipc_close", "anima_ipc_free",
-    "anima_peer_barrier",
+    "anima_peer_barrier", "anima_conv3x3", "anima_channel_norm",
 ]
 
 
@@ -125,6 +125,8 @@ def load_library(path: str = LIB_PATH):
             "anima_ipc_alloc": [vp, sz, C.POINTER(vp), C.c_char_p], "anima_ipc_open": [vp, C.c_char_p, C.POINTER(vp)],
             "anima_ipc_close": [vp, vp], "anima_ipc_free": [vp, vp],
             "anima_peer_barrier": [vp, C.POINTER(PeerGroup)],
+            "anima_conv3x3": [vp, vp, i, i, i, C.POINTER(Weight), i, vp, i],
+            "anima_channel_norm": [vp, vp, ll, i, vp, i, vp],
         }
         for name, args in sig.items():
             fn = getattr(lib, name)

@@ -153,6 +153,24 @@ def elementwise(op: str, a: torch.Tensor, b: torch.Tensor | None = None, out: to
     return y
 
 
+def conv3x3(x: torch.Tensor, W, h: int, w: int, up: bool = False, into: torch.Tensor | None = None) -> torch.Tensor:
+    """NHWC 3x3 convolution, pad 1, of x [h w, cin] with W (bf16 OHWI as [N, 9 cin], + bias); up:
+    nearest 2x upsample first; into: out += conv (ops.js:97-109, conv3x3 / conv3x3Into)."""
+    H, Wd = (2 * h, 2 * w) if up else (h, w)
+    out = into if into is not None else torch.empty(H * Wd, W.N, dtype=torch.float32, device=x.device)
+    wc = W.c()
+    ctx_for(x).call("anima_conv3x3", ptr(x), h, w, W.K // 9, C.byref(wc), 1 if up else 0, ptr(out),
+                    1 if into is not None else 0)
+    return out
+
+
+def channel_norm(x: torch.Tensor, gamma: torch.Tensor, cols: int, silu: bool) -> torch.Tensor:
+    """The Wan VAE's RMS_norm over channels, then SiLU (ops.js:120-126)."""
+    y = torch.empty_like(x)
+    ctx_for(x).call("anima_channel_norm", ptr(x), x.numel() // cols, cols, ptr(gamma), 1 if silu else 0, ptr(y))
+    return y
+
+
 def zero(t: torch.Tensor):
     """ops.zero (ops.js:89-93)."""
     ctx_for(t).call("anima_zero", ptr(t), t.numel() * t.element_size())

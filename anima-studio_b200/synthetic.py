@@ -16,6 +16,7 @@ checkpoint shapes); these use rank 256 and 2048 -> 2048 -> 6144.
 
 from __future__ import annotations
 
+import math
 import zlib
 
 import torch
@@ -225,4 +226,60 @@ def adapter_tensors(seed: int, n_blocks: int = ADAPTER["blocks"], vocab: int = A
     bf(p0 + "out_proj.weight", (D, D))
     bf(p0 + "out_proj.bias", (D,))
     bf(p0 + "norm.weight", (D,), one=True)
+    return out
+
+
+# ----------------------------------------------------------------------------- VAE decoder
+# The Wan-2.1 decoder as the reference's asset builder stores it (tools/build_assets.py:160-180):
+# 3x3 convs OHWI [O, 3, 3, I], 1x1 convs [O, I], RMS_norm gammas 1-D, all bf16. Stage channels
+# (384, 384, 384, 192, 96): three residual blocks per stage, a Resample (nearest 2x + conv to half
+# the channels) after each of the first three stages, 15 "upsamples" entries in all.
+VAE_DIMS = (384, 384, 384, 192, 96)
+LATENT_MEAN = [-0.7571, -0.7089, -0.9113, 0.1075, -0.1745, 0.9653, -0.1517, 1.5508, 0.4134, -0.0715, 0.5517, -0.3632,
+               -0.1922, -0.9497, 0.2503, -0.2921]
+LATENT_STD = [2.8184, 1.4541, 2.3275, 2.6558, 1.2196, 1.7708, 2.6052, 2.0743, 3.2687, 2.1526, 2.8652, 1.5579, 1.6382,
+              1.1253, 2.8251, 1.916]
+
+
+def vae_tensors(seed: int, dims=VAE_DIMS, z_dim: int = 16, device="cpu") -> dict:
+    """A synthetic Wan-2.1 VAE decoder file: conv weights N(0, 1 / fan_in) so activations keep their
+    scale through the stack, biases N(0, 0.02), gammas 1 + N(0, 0.02)."""
+    out = {}
+
+    def conv(name, o, i, k):
+        shape = (o, k, k, i) if k == 3 else (o, i)
+        out[name + ".weight"] = (randn(seed, name + ".weight", shape, device) / math.sqrt(i * k * k)).to(torch.bfloat16)
+        out[name + ".bias"] = randn(seed, name + ".bias", (o,), device, 0.02).to(torch.bfloat16)
+
+    def gamma(name, c):
+        out[name + ".gamma"] = (1 + randn(seed, name + ".gamma", (c,), device, 0.02)).to(torch.bfloat16)
+
+    def res(p, i, o):
+        gamma(p + ".residual.0", i)
+        conv(p + ".residual.2", o, i, 3)
+        gamma(p + ".residual.3", o)
+        conv(p + ".residual.6", o, o, 3)
+        if i != o:
+            conv(p + ".shortcut", o, i, 1)
+
+    conv("conv2", z_dim, z_dim, 1)
+    c = dims[0]
+    conv("decoder.conv1", c, z_dim, 3)
+    res("decoder.middle.0", c, c)
+    gamma("decoder.middle.1.norm", c)
+    conv("decoder.middle.1.to_qkv", 3 * c, c, 1)
+    conv("decoder.middle.1.proj", c, c, 1)
+    res("decoder.middle.2", c, c)
+    idx, cin = 0, dims[0]
+    for s, cout in enumerate(dims[1:]):
+        for _ in range(3):
+            res(f"decoder.upsamples.{idx}", cin, cout)
+            cin = cout
+            idx += 1
+        if s < len(dims) - 2:
+            conv(f"decoder.upsamples.{idx}.resample.1", cout // 2, cout, 3)
+            cin = cout // 2
+            idx += 1
+    gamma("decoder.head.0", cin)
+    conv("decoder.head.2", 3, cin, 3)
     return out

@@ -298,6 +298,20 @@ def kernel_case(args):
         out = torch.empty(M, N, device="cuda")
         fn = lambda: ops.matmul(a, w, out=out)  # noqa: E731
         work, unit = 2.0 * M * N * K, "TFLOP/s"
+    elif args.kernel == "vae":
+        # the Wan-2.1 decoder on a 128x128 latent -> one 1024x1024 image (once per image)
+        dec = pkg("vae").VAEDecoder(syn.vae_tensors(1), "cuda")
+        lat = torch.randn(16, 128, 128, device="cuda")
+        fn = lambda: dec.decode(lat)  # noqa: E731
+        work, unit = 1.0, "images/s"
+    elif args.kernel == "te":
+        # Qwen3-0.6B (28 int8 layers) on 512 tokens, then the LLM adapter on 512 T5 tokens
+        text = pkg("text")
+        te = text.Qwen3(syn.te_tensors(1, 28, 4096, direct=True), "cuda")
+        ad = text.LLMAdapter(syn.adapter_tensors(1, 6, 4096), "cuda")
+        ids = torch.randint(0, 4096, (512,)).tolist()
+        fn = lambda: ad(te.encode(ids), ids)  # noqa: E731
+        work, unit = 1.0, "prompts/s"
     elif args.kernel in ("gelu", "rotq"):
         K = 8192 if args.kernel == "gelu" else 2048
         h = torch.randn(M, K, device="cuda").half()
@@ -323,7 +337,7 @@ def kernel_case(args):
         ts.append(e0.elapsed_time(e1) / args.batch)
     dev.Context.get(0).sync()
     ms = statistics.median(ts)
-    rate = work / (ms * 1e-3) / (1e9 if unit == "GB/s" else 1e12)
+    rate = work / (ms * 1e-3) / {"GB/s": 1e9, "images/s": 1.0, "prompts/s": 1.0}.get(unit, 1e12)
     print(json.dumps({"kernel": args.kernel, "precision": args.precision, "attn": args.attn, "ms_median": ms,
                       "ms_min": min(ts), "rate": rate, "unit": unit, "reps": args.reps}), flush=True)
 
@@ -544,7 +558,7 @@ def run_cfg(args, world, rank, local):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--kernel", default=None, help="time one kernel case instead (mlp1|mlp2|qkv|oproj|attn|xattn|ln|gelu|rotq|xembed|final)")
+    ap.add_argument("--kernel", default=None, help="time one kernel case instead (mlp1|mlp2|qkv|oproj|attn|xattn|ln|gelu|rotq|xembed|final|vae|te)")
     ap.add_argument("--reps", type=int, default=20)
     ap.add_argument("--batch", type=int, default=10, help="kernel cases: launches per timed sample")
     ap.add_argument("--act", default="gelu", help="kernel case mlp1: epilogue activation (gelu|none)")

@@ -216,9 +216,9 @@ int anima_rope(anima_ctx* ctx, void* x, int dtype, int L, int H, int D, int row_
                const float* rope, int rope_rows);
 /* ops.attention (ops.js:166-208, kernels.js:147-299): multi-head attention with fp32 softmax.
  * Non-causal, head_dim 128, one k/v head per q head (the DiT's attentions): the tcgen05 flash
- * kernel. Causal, grouped k/v heads or head_dim 64 (the Qwen3 text encoder and the LLM adapter,
- * a few hundred tokens): a CUDA-core kernel over 32-key tiles in shared memory, which also takes
- * fp32 q/k/v.
+ * kernel. Causal, grouped k/v heads or head_dim 64 or 384 (the Qwen3 text encoder, the LLM adapter
+ * and the VAE's single-head attention, once per prompt or image): a CUDA-core kernel over 32-key
+ * tiles in shared memory, which also takes fp32 q/k/v.
  * The stream-K schedule (see anima_ctx_set_attention_split) launches one CTA per SM and lets a CTA
  * wait, bounded at 2 s, for a partial result written by a lower-numbered CTA; it therefore needs
  * all of the device's SMs to be available to this kernel at once. Where other work can hold SMs
@@ -242,6 +242,17 @@ int anima_attention_noalloc(anima_ctx* ctx, const anima_attention_args* a);
 int anima_elementwise(anima_ctx* ctx, int op, const float* a, const float* b, float* y, long long n);
 /* ops.zero (ops.js:89-93). */
 int anima_zero(anima_ctx* ctx, void* p, size_t bytes);
+
+/* ---------------------------------------------------------------- VAE decoder (vae.js) */
+/* ops.conv3x3 / conv3x3Into (ops.js:97-109, the conv3 tiles of gemm.js): NHWC 3x3 convolution,
+ * pad 1, of x fp32 [h * w, cin] with W bf16 OHWI [N, 9 cin] (+ W.bias); with up != 0 the input is
+ * first upsampled 2x (nearest, the Resample of the Wan decoder). out fp32 [H * Wd, N] (H, Wd the
+ * output size) = the result, or += it when accumulate != 0 (a residual). cin a multiple of 8. */
+int anima_conv3x3(anima_ctx* ctx, const float* x, int h, int w, int cin, const anima_weight* W, int up, float* out,
+                  int accumulate);
+/* ops.channelNorm (ops.js:120-126, the Wan decoder's RMS_norm): y = x / max(||x||_2, 1e-12) *
+ * sqrt(C) * gamma over each row of C channels, then SiLU when silu != 0; fp32. */
+int anima_channel_norm(anima_ctx* ctx, const float* x, long long rows, int C, const float* gamma, int silu, float* y);
 
 /* ---------------------------------------------------------------- model glue (dit.js, pipeline.js) */
 /* patchify (dit.js:55-65): latent [B, 16, h, w] -> patches [B, (h/2)(w/2), 68] with the zero mask channel. */

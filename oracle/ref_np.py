@@ -342,6 +342,9 @@ class DequantWeights:
             self.cache[name] = w
         return w
 
+    def has(self, name) -> bool:
+        return self.prefix + name in self.t
+
 
 class LoraMerged:
     """W(name) + sum_e scale_e * B_e @ A_e for matching linears (tools/reference.py:51-90).

@@ -196,12 +196,26 @@ def text_fixtures(quant, R, syn):
     print("text done", flush=True)
 
 
+def vae_fixtures(quant, R, syn):
+    """The reference's own vae_decode (tools/reference.py:254-295) on a synthetic Wan-2.1 decoder
+    (the published channel layout), an 8x8 latent in the model's normalised space -> a 64x64
+    image. vae_decode takes the de-normalised latent, as generate passes it (reference.py:368-370)."""
+    seed = 61
+    latent = syn.randn(seed, "golden.vae.latent", (16, 8, 8))
+    Wv = RefWeights(quant, lambda i: {}, syn.vae_tensors(seed))
+    mean = torch.tensor(R.LATENT_MEAN)[:, None, None]
+    std = torch.tensor(R.LATENT_STD)[:, None, None]
+    img = R.vae_decode(Wv, latent * std + mean)
+    np.savez_compressed(os.path.join(HERE, "vae_64.npz"), seed=seed, latent=latent.numpy(), image=img.numpy())
+    print("vae done", img.shape, flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("ANIMA_REFERENCE"))
-    ap.add_argument("--only", choices=["small", "full", "text"], default=None,
+    ap.add_argument("--only", choices=["small", "full", "text", "vae"], default=None,
                     help="small: sections 1-5 (L = 64 and the quantizers); full: the 1024^2 fixtures; "
-                         "text: the Qwen3 + LLM adapter fixture")
+                         "text: the Qwen3 + LLM adapter fixture; vae: the VAE decoder fixture")
     args = ap.parse_args()
     if not args.ref:
         ap.error("give the reference checkout with --ref or ANIMA_REFERENCE")
@@ -214,6 +228,9 @@ def main():
         return
     if args.only == "text":
         text_fixtures(quant, R, syn)
+        return
+    if args.only == "vae":
+        vae_fixtures(quant, R, syn)
         return
 
     # 1. int8 ConvRot quantizer + dequantizer (tools/quant.py:59-67, 81-83)
@@ -323,6 +340,7 @@ def main():
     if args.only is None:
         full_size_fixtures(quant, R, syn)
         text_fixtures(quant, R, syn)
+        vae_fixtures(quant, R, syn)
     print("golden fixtures written to", HERE)
 
 

@@ -141,3 +141,16 @@ def test_text_oracle_matches_reference_fixture():
     Wa = oracle.DequantWeights(oracle.to_numpy(syn.adapter_tensors(seed, 6, vocab)))
     ctx = text_np.llm_adapter(Wa, g["hidden"], g["t5_ids"])
     assert rel_l2(ctx[:60], g["ctx60"]) < 1e-5 and not ctx[60:].any()
+
+
+def test_vae_oracle_matches_reference_fixture():
+    """The numpy Wan-2.1 decoder (oracle/vae_np.py) against tools/reference.py's vae_decode on the
+    same synthetic decoder and latent (tests/golden/vae_64.npz)."""
+    from oracle import vae_np
+
+    g = load("vae_64.npz")
+    syn = pkg("synthetic")
+    W = oracle.DequantWeights(oracle.to_numpy(syn.vae_tensors(int(g["seed"]))))
+    z = g["latent"] * np.array(syn.LATENT_STD, np.float32)[:, None, None] + \
+        np.array(syn.LATENT_MEAN, np.float32)[:, None, None]
+    assert rel_l2(vae_np.vae_decode(W, z), g["image"]) < 1e-5
