@@ -12,7 +12,10 @@
 //   WG0, WG1    epilogue: tcgen05.ld of the accumulator rows (thread = row), fused epilogue, stores;
 //               WG0 takes the CTA's even tiles, WG1 the odd ones (two warps per scheduler)
 //   warp 8      TMA producer: A tile(s) 128 x 128 B and W tile BN x 128 B per stage (SWIZZLE_128B)
-//   warp 9      TMEM allocator + single-thread UMMA issuer (M = 128, N = BN, K = 32 per instruction)
+//   warp 9      TMEM allocator + single-thread UMMA issuer of the hi plane (M = 128, N = BN, K = 32)
+//   warp 10     single-thread UMMA issuer of the lo plane (two planes only): the planes have their
+//               own accumulators, so two wait -> issue -> commit chains feed the tensor core at once
+//               (one thread issuing both planes was the kernel's critical path)
 // The accumulators are double-buffered in TMEM (2 x NPLANES x BN = 512 columns), one buffer per
 // epilogue warpgroup, so the epilogues of two tiles overlap the MMAs of the next.
 
@@ -27,7 +30,7 @@ namespace gemm {
 constexpr int BM = 128;
 constexpr int BK = 128;      // bytes of K per stage (one SWIZZLE_128B row)
 constexpr int UMMA_K = 32;   // K per kind::i8 instruction
-constexpr int THREADS = 320;  // 8 epilogue warps + producer warp + MMA warp
+constexpr int THREADS = 352;  // 8 epilogue warps + producer warp + one MMA warp per activation plane
 
 struct Params {
   int M, N, K;
@@ -495,8 +498,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* empty = full + C::STAGES;
   uint64_t* acc_full = empty + C::STAGES;
   uint64_t* acc_empty = acc_full + 2;
-  uint64_t* drain = acc_empty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* drain = acc_empty + 2;  // one per MMA warp
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -505,13 +508,14 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+      mbar_init(&empty[s], NPLANES);  // a commit from each MMA warp
     }
     for (int b = 0; b < 2; ++b) {
-      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_full[b], NPLANES);
       mbar_init(&acc_empty[b], 4);  // one arrival per epilogue warp
     }
-    mbar_init(drain, 1);
+    mbar_init(&drain[0], 1);
+    mbar_init(&drain[1], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -569,7 +573,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
     }
-  } else if (warp == kMmaWarp) {
+  } else if (warp == kMmaWarp || (NPLANES == 2 && warp == kMmaWarp + 1)) {
+    const int plane = warp - kMmaWarp;
     if (lane == 0) {
       const uint32_t idesc = idesc_i8(BM, BN);
       int stage = 0;
@@ -580,8 +585,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         const uint32_t acc_phase = (t / C::ACC_BUFS) & 1;
         if (!mbar_wait(&acc_empty[buf], acc_phase ^ 1, abort_flag, kErrTimeoutAcc)) break;
         tc_fence_after();
-        const uint32_t d_hi = tmem_base + buf * C::ACC_COLS;
-        const uint32_t d_lo = d_hi + BN;
+        const uint32_t d = tmem_base + buf * C::ACC_COLS + plane * BN;  // this plane's accumulator
         bool aborted = false;
         for (int kb = 0; kb < p.num_k_blocks; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, kErrTimeoutFull)) {
@@ -589,14 +593,13 @@ __global__ void __launch_bounds__(THREADS, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t sa = smem_u32(smem + stage * C::STAGE_BYTES);
-          const uint32_t sb = sa + NPLANES * C::A_BYTES;
+          const uint32_t s0 = smem_u32(smem + stage * C::STAGE_BYTES);
+          const uint32_t sa = s0 + plane * C::A_BYTES;
+          const uint32_t sb = s0 + NPLANES * C::A_BYTES;
 #pragma unroll
           for (int k = 0; k < BK / UMMA_K; ++k) {
-            const uint64_t bdesc = sdesc_sw128(sb + k * UMMA_K, 16, 1024);
             const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
-            umma_i8(d_hi, sdesc_sw128(sa + k * UMMA_K, 16, 1024), bdesc, idesc, acc);
-            if (NPLANES == 2) umma_i8(d_lo, sdesc_sw128(sa + C::A_BYTES + k * UMMA_K, 16, 1024), bdesc, idesc, acc);
+            umma_i8(d, sdesc_sw128(sa + k * UMMA_K, 16, 1024), sdesc_sw128(sb + k * UMMA_K, 16, 1024), idesc, acc);
           }
           umma_commit(&empty[stage]);
           if (++stage == C::STAGES) {
@@ -609,9 +612,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       if (*abort_flag) {
         // MMAs already issued complete before TMEM is released.
-        umma_commit(drain);
+        umma_commit(&drain[plane]);
         const unsigned long long t0 = globaltimer();
-        while (!mbar_test(smem_u32(drain), 0)) {
+        while (!mbar_test(smem_u32(&drain[plane]), 0)) {
           if (globaltimer() - t0 > kWaitTimeoutNs) {
             flag_error(kErrTimeoutDrain);
             break;
