@@ -269,6 +269,15 @@ def kernel_case(args):
             cs = torch.from_numpy(ditm.rope_table(64, 64)).cuda()
             fn = lambda: ops.linear(qa, w, out=out, mode="qkv", qk=(nq, nk), rope_cs=cs, n_q=2048)  # noqa: E731
         work, unit = 2.0 * M * N * K, "TOPS"
+    elif args.kernel == "w4":
+        # a W4A8 2048 -> 8192 linear: the per-call decode of the packed weight, then the int8 GEMM
+        quant = pkg("quant")
+        q = quant.quantize_w4a8(torch.randn(8192, 2048, device="cuda") * 0.02)
+        w = W.linear_weights({"l." + k: v for k, v in q.items()}, "l.", "cuda")
+        qa = ops.rotate_quant(torch.randn(M, 2048, device="cuda"), planes)
+        out = torch.empty(M, 8192, dtype=torch.float16, device="cuda")
+        fn = lambda: ops.linear(qa, w, out=out)  # noqa: E731
+        work, unit = 2.0 * M * 8192 * 2048, "TOPS"
     elif args.kernel == "attn":
         dt = torch.float16 if args.attn == "f16" else torch.bfloat16
         qkv = torch.randn(M, 6144, device="cuda").to(dt)
@@ -558,7 +567,7 @@ def run_cfg(args, world, rank, local):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--kernel", default=None, help="time one kernel case instead (mlp1|mlp2|qkv|oproj|attn|xattn|ln|gelu|rotq|xembed|final|vae|te)")
+    ap.add_argument("--kernel", default=None, help="time one kernel case instead (mlp1|mlp2|qkv|oproj|w4|attn|xattn|ln|gelu|rotq|xembed|final|vae|te)")
     ap.add_argument("--reps", type=int, default=20)
     ap.add_argument("--batch", type=int, default=10, help="kernel cases: launches per timed sample")
     ap.add_argument("--act", default="gelu", help="kernel case mlp1: epilogue activation (gelu|none)")
