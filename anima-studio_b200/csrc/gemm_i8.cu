@@ -220,7 +220,14 @@ __device__ __forceinline__ void finish_cols(const Params& p, int m, int n, bool 
   if constexpr (LORA) {
     if (lt.bt_s && row_ok) lora_cols<BN, CH>(lt, col, v);
   }
-  if (apply_act && p.act != ANIMA_ACT_NONE) {
+  if (apply_act && p.act == ANIMA_ACT_GELU) {
+#pragma unroll
+    for (int j = 0; j < CH; j += 2) {
+      const f2 g = gelu2(make_float2(v[j], v[j + 1]));
+      v[j] = g.x;
+      v[j + 1] = g.y;
+    }
+  } else if (apply_act && p.act != ANIMA_ACT_NONE) {
 #pragma unroll
     for (int j = 0; j < CH; ++j) v[j] = act_fn(v[j], p.act);
   }

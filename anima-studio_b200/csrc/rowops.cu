@@ -75,88 +75,57 @@ __device__ __forceinline__ float warp_max(float v) {
 // ------------------------------------------------------------------ packed fp32 pairs
 // The row kernels keep their data as float2 pairs of neighbouring elements so the bulk of the
 // arithmetic uses the paired fp32 instructions (f2 helpers in sm100.cuh).
+//
+// Lane order: a half-warp holds one group of 256 elements, lane t (0..15) the 16 elements
+// 4t + 64k + e (k, e = 0..3) as register a = e + 4k, i.e. pairs P[2k] = (e 0, 1), P[2k+1] =
+// (e 2, 3). Each k is one 16-byte (fp32) or 8-byte (16-bit) access, and the 16 lanes of a
+// half-warp read 256 (fp32) or 128 (16-bit) contiguous bytes per access, so every sector an
+// access touches is fully used. p points at element 4t of the lane's group.
 
 template <typename T>
-__device__ __forceinline__ void load16p(const T* p, f2 (&x)[8]) {
-  if constexpr (sizeof(T) == 4) {
+__device__ __forceinline__ f2 to_f2(uint32_t w) {
+  if constexpr (std::is_same<T, __half>::value)
+    return __half22float2(*reinterpret_cast<const __half2*>(&w));
+  else
+    return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w));
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t from_f2(f2 v) {
+  if constexpr (std::is_same<T, __half>::value) {
+    const __half2 h = __floats2half2_rn(v.x, v.y);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  } else {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(v.x, v.y);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void load_lane16(const T* p, f2 (&x)[8]) {
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const float4 a = reinterpret_cast<const float4*>(p)[k];
+  for (int k = 0; k < 4; ++k) {
+    if constexpr (sizeof(T) == 4) {
+      const float4 a = *reinterpret_cast<const float4*>(p + 64 * k);
       x[2 * k] = make_float2(a.x, a.y);
       x[2 * k + 1] = make_float2(a.z, a.w);
-    }
-  } else {
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      const uint4 u = reinterpret_cast<const uint4*>(p)[k];
-      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        if constexpr (std::is_same<T, __half>::value)
-          x[4 * k + i] = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
-        else
-          x[4 * k + i] = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
-      }
+    } else {
+      const uint2 u = *reinterpret_cast<const uint2*>(p + 64 * k);
+      x[2 * k] = to_f2<T>(u.x);
+      x[2 * k + 1] = to_f2<T>(u.y);
     }
   }
 }
 
 template <typename T>
-__device__ __forceinline__ void store16p(T* p, const f2 (&x)[8]) {
-  if constexpr (sizeof(T) == 4) {
+__device__ __forceinline__ void store_lane16(T* p, const f2 (&x)[8]) {
 #pragma unroll
-    for (int k = 0; k < 4; ++k)
-      reinterpret_cast<float4*>(p)[k] = make_float4(x[2 * k].x, x[2 * k].y, x[2 * k + 1].x, x[2 * k + 1].y);
-  } else {
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      uint32_t w[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        if constexpr (std::is_same<T, __half>::value) {
-          const __half2 h = __floats2half2_rn(x[4 * k + i].x, x[4 * k + i].y);
-          w[i] = *reinterpret_cast<const uint32_t*>(&h);
-        } else {
-          const __nv_bfloat162 h = __floats2bfloat162_rn(x[4 * k + i].x, x[4 * k + i].y);
-          w[i] = *reinterpret_cast<const uint32_t*>(&h);
-        }
-      }
-      reinterpret_cast<uint4*>(p)[k] = make_uint4(w[0], w[1], w[2], w[3]);
-    }
+  for (int k = 0; k < 4; ++k) {
+    if constexpr (sizeof(T) == 4)
+      *reinterpret_cast<float4*>(p + 64 * k) = make_float4(x[2 * k].x, x[2 * k].y, x[2 * k + 1].x, x[2 * k + 1].y);
+    else
+      *reinterpret_cast<uint2*>(p + 64 * k) = make_uint2(from_f2<T>(x[2 * k]), from_f2<T>(x[2 * k + 1]));
   }
-}
-
-__device__ __forceinline__ float rcp_approx(float x) {
-  float r;
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
-  return r;
-}
-__device__ __forceinline__ float ex2_approx(float x) {
-  float r;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
-  return r;
-}
-
-// GELU(x) = x Phi(x) on a pair, with erf from Abramowitz & Stegun 7.1.26 (|error| <= 1.5e-7):
-// erf(a) = 1 - t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) exp(-a^2), t = 1 / (1 + p a)
-__device__ __forceinline__ f2 gelu2(f2 x) {
-  const f2 z = mul2(x, dup2(0.70710678118654752f));
-  const f2 a = make_float2(fabsf(z.x), fabsf(z.y));
-  const f2 d = fma2(a, dup2(0.3275911f), dup2(1.0f));
-  const f2 t = make_float2(rcp_approx(d.x), rcp_approx(d.y));
-  f2 q = fma2(dup2(1.061405429f), t, dup2(-1.453152027f));
-  q = fma2(q, t, dup2(1.421413741f));
-  q = fma2(q, t, dup2(-0.284496736f));
-  q = fma2(q, t, dup2(0.254829592f));
-  q = mul2(q, t);
-  const f2 n = mul2(a, mul2(a, dup2(-1.4426950408889634f)));  // -a^2 log2(e)
-  const f2 e = make_float2(ex2_approx(n.x), ex2_approx(n.y));
-  const f2 r = fma2(q, e, dup2(-1.0f));  // -erf(|z|)
-  // w = sign(z) erf(|z|): flip r unless z is negative
-  const f2 w = make_float2(__uint_as_float(__float_as_uint(r.x) ^ (~__float_as_uint(z.x) & 0x80000000u)),
-                           __uint_as_float(__float_as_uint(r.y) ^ (~__float_as_uint(z.y) & 0x80000000u)));
-  const f2 h = mul2(x, dup2(0.5f));
-  return fma2(h, w, h);
 }
 
 // ------------------------------------------------------------------ ConvRot Hadamard (256-point)
@@ -172,11 +141,13 @@ __device__ __forceinline__ f2 gelu2(f2 x) {
 // every digit. sigma on the input is folded into the first butterfly stage, swap() into the
 // shared-memory addressing, sigma on the output into the caller's per-element multiplier.
 //
-// A half-warp holds one group, lane t the 16 consecutive elements 16t..16t+15 as 8 float2 pairs,
-// so index bits 0-3 are in the thread (bit 0 within a pair) and bits 4-7 pick the lane. The
-// transform runs bits 0-3 in registers, transposes the 16 x 16 tile through shared memory
-// (lane c then holds elements c + 16 b, b = 0..15, pairs (b, b+1)), runs bits 4-7, and
-// transposes back with swap() applied, leaving lane t with y[16t .. 16t+15] up to sigma and 1/16.
+// In the lane order of load_lane16, register a = e + 4k of lane t holds element (a & 3) + 4t +
+// 64 (a >> 2): the register index is the digit pair (d0, d3) and the lane the pair (d1, d2), so
+// sigma and swap() split into a register part and a lane part (sgn4 and swap4 below). The
+// transform runs the register bits (d0, d3) first, transposes the 16 x 16 tile through shared
+// memory (lane c then holds register index c of lanes b = 0..15, pairs (b, b+1)), runs the lane
+// bits (d1, d2), and transposes back with swap() applied, leaving every lane with the output
+// positions of its input positions, up to sigma and 1/16.
 
 // sigma over a 4-bit index (two base-4 digits)
 __host__ __device__ constexpr float sgn4(int a) { return ((a & 3) == 3) != ((a >> 2) == 3) ? -1.f : 1.f; }
@@ -208,36 +179,60 @@ constexpr int kTileStride = 20;
 constexpr int kTileHalf = 336;
 constexpr int kTileWords = kTileHalf + 16 * kTileStride;  // per warp
 
-// P: lane t's 16 consecutive elements of a group. Returns them transformed (unscaled, without the
-// output sigma), still lane t's 16 consecutive output positions.
-__device__ __forceinline__ void hadamard256(float* tb, int t, f2 (&P)[8]) {
-  wht16(P);  // bits 0-3
+// V[p]: lane t's 16 elements of a group (lane order of load_lane16). Transforms V[p0 .. p0 + NP - 1]
+// in place (unscaled, without the output sigma; lane t keeps the same 16 positions), NP groups per
+// half-warp at once in NP tiles kTileWords apart (tb: the first), so the shared-memory round trips
+// of the NP transposes overlap.
+template <int NP, int NV>
+__device__ __forceinline__ void hadamard256_n(float* tb, int t, f2 (&V)[NV][8], int p0) {
 #pragma unroll
-  for (int k = 0; k < 4; ++k)
-    *reinterpret_cast<float4*>(tb + t * kTileStride + 4 * k) = make_float4(P[2 * k].x, P[2 * k].y, P[2 * k + 1].x, P[2 * k + 1].y);
-  __syncwarp();
+  for (int i = 0; i < NP; ++i) {
+    f2 (&P)[8] = V[p0 + i];
+    float* b = tb + i * kTileWords;
+    wht16(P);  // register bits (d0, d3)
 #pragma unroll
-  for (int j = 0; j < 8; ++j) P[j] = make_float2(tb[(2 * j) * kTileStride + t], tb[(2 * j + 1) * kTileStride + t]);
+    for (int k = 0; k < 4; ++k)
+      *reinterpret_cast<float4*>(b + t * kTileStride + 4 * k) = make_float4(P[2 * k].x, P[2 * k].y, P[2 * k + 1].x, P[2 * k + 1].y);
+  }
   __syncwarp();
-  wht16(P);  // bits 4-7; P[j] = u[t + 16 (2j)], u[t + 16 (2j + 1)]
   const int ct = swap4(t);
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    tb[swap4(2 * j) * kTileStride + ct] = P[j].x;
-    tb[swap4(2 * j + 1) * kTileStride + ct] = P[j].y;
+  for (int i = 0; i < NP; ++i) {
+    f2 (&P)[8] = V[p0 + i];
+    const float* b = tb + i * kTileWords;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) P[j] = make_float2(b[(2 * j) * kTileStride + t], b[(2 * j + 1) * kTileStride + t]);
   }
   __syncwarp();
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const float4 q = *reinterpret_cast<const float4*>(tb + t * kTileStride + 4 * k);
-    P[2 * k] = make_float2(q.x, q.y);
-    P[2 * k + 1] = make_float2(q.z, q.w);
+  for (int i = 0; i < NP; ++i) {
+    f2 (&P)[8] = V[p0 + i];
+    float* b = tb + i * kTileWords;
+    wht16(P);  // lane bits (d1, d2); P[j] = register t of lanes 2j, 2j + 1
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      b[swap4(2 * j) * kTileStride + ct] = P[j].x;
+      b[swap4(2 * j + 1) * kTileStride + ct] = P[j].y;
+    }
+  }
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < NP; ++i) {
+    f2 (&P)[8] = V[p0 + i];
+    const float* b = tb + i * kTileWords;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float4 q = *reinterpret_cast<const float4*>(b + t * kTileStride + 4 * k);
+      P[2 * k] = make_float2(q.x, q.y);
+      P[2 * k + 1] = make_float2(q.z, q.w);
+    }
   }
   __syncwarp();
 }
 
-// Per-pair multipliers that apply the output sigma: sigma(16 t + a) = sgn4(t) sgn4(a), and over
-// the pair (a, a + 1) = (2j, 2j + 1) sgn4 takes the patterns (+,+), (+,-), (-,-), (-,+).
+// Per-pair multipliers that apply the output sigma: sigma of register a of lane t is
+// sgn4(t) sgn4(a), and over the pair (a, a + 1) = (2j, 2j + 1) sgn4 takes the patterns (+,+),
+// (+,-), (-,-), (-,+).
 struct PairScale {
   f2 pp, pm, mm, mp;
   __device__ __forceinline__ PairScale(float w, bool signed_out) {
@@ -252,10 +247,62 @@ struct PairScale {
   }
 };
 
+// ------------------------------------------------------------------ per-lane pieces of the row kernels
+//   LN      y = LN(x) * (1 + mod[scale_off + c]) + mod[shift_off + c]  (fp32 two-pass mean/var,
+//           biased variance, eps: tools/reference.py:190-191, kernels.js:95-145)
+//   act     y <- GELU(y) (the MLP's activation, applied here when the layer1 GEMM stored its
+//           pre-activation)
+//   rotate  y <- y H per 256 group (tools/quant.py:30-45)
+//   quant   s = amax / 127; a = y * (127 / amax); hi = rne(a); lo = rne((a - hi) * 254)
+//           (|a| <= 127 and |a - hi| <= 1/2, so neither needs clamping)
+
+// c * (rstd * (1 + scale)) + shift on lane t's 16 centred values c = x - mean; sc/sh point at the
+// lane's first column of the scale and shift vectors (lane order).
+__device__ __forceinline__ void ln_apply16(f2 (&v)[8], f2 rs, const float* sc, const float* sh) {
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float4 c = *reinterpret_cast<const float4*>(sc + 64 * k);
+    const float4 d = *reinterpret_cast<const float4*>(sh + 64 * k);
+    v[2 * k] = fma2(v[2 * k], fma2(rs, make_float2(c.x, c.y), rs), make_float2(d.x, d.y));
+    v[2 * k + 1] = fma2(v[2 * k + 1], fma2(rs, make_float2(c.z, c.w), rs), make_float2(d.z, d.w));
+  }
+}
+
+// Quantize lane t's 16 values, a = v * ps (ps carries 127 / amax and the Hadamard's output sigma),
+// into the two int8 planes: register a = e + 4k goes to byte e of the 32-bit word at hi / lo + 64 k.
+// hi = rne(a) through the 1.5 * 2^23 magic number, with the product kept exact inside the fma:
+// the float's low byte is then the two's-complement int8 of hi (|a| <= 127). lo = rne((a - hi) *
+// 254) the same way, a - hi again from the exact product (|a - hi| <= 1/2, so |lo| <= 127).
+__device__ __forceinline__ void quant_store16(const f2 (&v)[8], const PairScale& ps, int8_t* hi, int8_t* lo) {
+  const f2 magic = dup2(12582912.0f), c254 = dup2(254.0f), m1 = dup2(-1.0f);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    uint32_t hb[4], lb[4];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int j = 2 * k + i;
+      const f2 m = fma2(v[j], ps.of(j), magic);        // magic + hi
+      const f2 rem = fma2(v[j], ps.of(j), fma2(m, m1, magic));  // a - hi
+      const f2 l = fma2(rem, c254, magic);
+      hb[2 * i] = __float_as_uint(m.x);
+      hb[2 * i + 1] = __float_as_uint(m.y);
+      lb[2 * i] = __float_as_uint(l.x);
+      lb[2 * i + 1] = __float_as_uint(l.y);
+    }
+    reinterpret_cast<uint32_t*>(hi)[16 * k] = __byte_perm(__byte_perm(hb[0], hb[1], 0x0040), __byte_perm(hb[2], hb[3], 0x0040), 0x5410);
+    if (lo) reinterpret_cast<uint32_t*>(lo)[16 * k] = __byte_perm(__byte_perm(lb[0], lb[1], 0x0040), __byte_perm(lb[2], lb[3], 0x0040), 0x5410);
+  }
+}
+
+__device__ __forceinline__ float amax16(const f2 (&v)[8], float m) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) m = fmax3(m, fabsf(v[j].x), fabsf(v[j].y));
+  return m;
+}
+
 // ------------------------------------------------------------------ row kernel: LN + adaLN, ConvRot, quant
 // Geometry: a warp pass covers two groups of 256 columns, one per half-warp; a warp makes G2
 // passes and WPR warps share a row. Rows of a single group are handled by one half-warp each.
-// Every warp access is a contiguous 1 KB (fp32) or 512 B (16-bit) segment.
 template <int COLS>
 struct RowGeom {
   static constexpr int NG = COLS / 256;
@@ -290,13 +337,7 @@ __device__ __forceinline__ float row_reduce(float v, float* red) {
   }
 }
 
-//   LN      y = LN(x) * (1 + mod[scale_off + c]) + mod[shift_off + c]  (fp32 two-pass mean/var,
-//           biased variance, eps: tools/reference.py:190-191, kernels.js:95-145)
-//   act     y <- GELU(y) (the MLP's activation, applied here when the layer1 GEMM stored its
-//           pre-activation)
-//   rotate  y <- y H per 256 group (tools/quant.py:30-45)
-//   quant   s = amax / 127; a = y * (127 / amax); hi = rne(a); lo = rne((a - hi) * 254)
-//           (|a| <= 127 and |a - hi| <= 1/2, so neither needs clamping)
+// The general row kernel (every supported width and output), rows straight from global memory.
 template <int COLS, typename TIn, typename TOut, bool LN>
 __global__ void __launch_bounds__(256, 4) rows_kernel(const TIn* __restrict__ x, int rows, int ldx,
                                                    const float* __restrict__ mod, int shift_off, int scale_off,
@@ -314,12 +355,12 @@ __global__ void __launch_bounds__(256, 4) rows_kernel(const TIn* __restrict__ x,
   const size_t r = valid ? static_cast<size_t>(row) : 0;
   float* tb = tiles + warp * kTileWords + half * kTileHalf;
   f2 v[G2][8];
-  int col[G2];
+  int col[G2];  // the lane's first column in each pass
 #pragma unroll
   for (int p = 0; p < G2; ++p) {
-    col[p] = Gm::HALF ? 16 * t : ((wr * G2 + p) * 2 + half) * 256 + 16 * t;
+    col[p] = (Gm::HALF ? 0 : ((wr * G2 + p) * 2 + half) * 256) + 4 * t;
     if (valid) {
-      load16p(x + r * ldx + col[p], v[p]);
+      load_lane16(x + r * ldx + col[p], v[p]);
     } else {
 #pragma unroll
       for (int j = 0; j < 8; ++j) v[p][j] = dup2(0.f);
@@ -344,15 +385,7 @@ __global__ void __launch_bounds__(256, 4) rows_kernel(const TIn* __restrict__ x,
     const float var = row_reduce<COLS, false>(q2.x + q2.y, red) / static_cast<float>(COLS);
     const f2 rs = dup2(1.0f / sqrtf(var + eps));
 #pragma unroll
-    for (int p = 0; p < G2; ++p)
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const float4 sc = *reinterpret_cast<const float4*>(mod + scale_off + col[p] + 4 * k);
-        const float4 sh = *reinterpret_cast<const float4*>(mod + shift_off + col[p] + 4 * k);
-        // (x - mean) * (rstd * (1 + scale)) + shift
-        v[p][2 * k] = fma2(v[p][2 * k], fma2(rs, make_float2(sc.x, sc.y), rs), make_float2(sh.x, sh.y));
-        v[p][2 * k + 1] = fma2(v[p][2 * k + 1], fma2(rs, make_float2(sc.z, sc.w), rs), make_float2(sh.z, sh.w));
-      }
+    for (int p = 0; p < G2; ++p) ln_apply16(v[p], rs, mod + scale_off + col[p], mod + shift_off + col[p]);
   }
   if (act == ANIMA_ACT_GELU) {
 #pragma unroll
@@ -362,16 +395,14 @@ __global__ void __launch_bounds__(256, 4) rows_kernel(const TIn* __restrict__ x,
   }
   if (rotate) {
 #pragma unroll
-    for (int p = 0; p < G2; ++p) hadamard256(tb, t, v[p]);
+    for (int p = 0; p < G2; ++p) hadamard256_n<1>(tb, t, v, p);
   }
-  // the output sigma of the Hadamard for this lane's 16 positions (index bits 4-7 are t)
+  // the lane part of the Hadamard's output sigma
   const float lane_sign = rotate ? sgn4(t) : 1.0f;
   if (qhi) {
     float amax = 0.f;
 #pragma unroll
-    for (int p = 0; p < G2; ++p)
-#pragma unroll
-      for (int j = 0; j < 8; ++j) amax = fmax3(amax, fabsf(v[p][j].x), fabsf(v[p][j].y));
+    for (int p = 0; p < G2; ++p) amax = amax16(v[p], amax);
     amax = row_reduce<COLS, true>(amax, red);
     if (!valid) return;
     // a = (y / 16) * 127 / (amax / 16) = y * (127 / amax) for the unscaled y: the 1/16 is a power of
@@ -380,43 +411,251 @@ __global__ void __launch_bounds__(256, 4) rows_kernel(const TIn* __restrict__ x,
     const float inv = amax > 0.f ? 127.0f / amax : 0.f;
     if (wr == 0 && (Gm::HALF ? t : lane) == 0) qscale[r] = amax > 0.f ? (amax * post) / 127.0f : 1.0f;
     const PairScale ps(inv * lane_sign, rotate != 0);
-    const f2 magic = dup2(12582912.0f), nmagic = dup2(-12582912.0f), c254 = dup2(254.0f);
 #pragma unroll
-    for (int p = 0; p < G2; ++p) {
-      uint32_t hw[4], lw[4];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        // round to nearest even through the 1.5 * 2^23 magic number: the float's low byte is then
-        // the two's-complement int8 of the rounded value (|a| <= 127, |lo| <= 127)
-        uint32_t hb[4], lb[4];
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-          const int j = 2 * k + i;
-          const f2 a = mul2(v[p][j], ps.of(j));
-          const f2 m = add2(a, magic);
-          const f2 rem = sub2(a, add2(m, nmagic));
-          const f2 l = fma2(rem, c254, magic);
-          hb[2 * i] = __float_as_uint(m.x);
-          hb[2 * i + 1] = __float_as_uint(m.y);
-          lb[2 * i] = __float_as_uint(l.x);
-          lb[2 * i + 1] = __float_as_uint(l.y);
-        }
-        hw[k] = __byte_perm(__byte_perm(hb[0], hb[1], 0x0040), __byte_perm(hb[2], hb[3], 0x0040), 0x5410);
-        lw[k] = __byte_perm(__byte_perm(lb[0], lb[1], 0x0040), __byte_perm(lb[2], lb[3], 0x0040), 0x5410);
-      }
-      *reinterpret_cast<uint4*>(qhi + r * qld + col[p]) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-      if (qlo) *reinterpret_cast<uint4*>(qlo + r * qld + col[p]) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-    }
+    for (int p = 0; p < G2; ++p) quant_store16(v[p], ps, qhi + r * qld + col[p], qlo ? qlo + r * qld + col[p] : nullptr);
   } else if (valid) {
     const PairScale ps((rotate ? 0.0625f : 1.0f) * lane_sign, rotate != 0);
 #pragma unroll
     for (int p = 0; p < G2; ++p) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) v[p][j] = mul2(v[p][j], ps.of(j));
-      store16p(y + r * COLS + col[p], v[p]);
+      store_lane16(y + r * COLS + col[p], v[p]);
     }
   }
 }
+
+// ------------------------------------------------------------------ persistent ring row kernel
+// The block's hot rows (2048 and 8192 columns, int8 outputs): LN+adaLN+ConvRot+quant of the
+// residual stream and ConvRot+quant of the attention output and of the MLP's hidden layer. One CTA
+// per SM runs until its rows are done. A producer lane streams whole rows into a ring of
+// shared-memory stages with 1D bulk copies (cp.async.bulk, mbarrier completion), so the loads in
+// flight hold no registers and overlap the arithmetic of earlier rows. Teams of WPR consumer
+// warps take one row each at a time, every warp PASSES x 512 columns of it (two groups per pass,
+// one per half-warp); the row's sums and maximum go across the team through shared memory. Rows
+// are split this finely so that the 27-28 rows an SM gets spread evenly over many warps: at 2048
+// columns 7 teams of 4 warps take 4 rows each. CTA b takes rows b, b + grid, b + 2 grid, ... and
+// team m of it the CTA's m-th, (m + TEAMS)-th, ... row.
+namespace ring {
+
+constexpr int kSmemLimit = 232448;  // 227 KB of opt-in dynamic shared memory per CTA
+constexpr int kMaxStages = 32;
+
+template <int COLS, typename TIn, bool LN>
+struct Geom {
+  static constexpr int PASSES = COLS == 2048 ? 1 : 2;  // passes (512 columns each) per warp
+  static constexpr int WPR = COLS / (512 * PASSES);     // warps per row: 4 at 2048, 8 at 8192
+  static constexpr int CW = WPR == 4 ? 28 : 24;         // consumer warps (+ 1 producer: 29 / 25)
+  static constexpr int TEAMS = CW / WPR;                // rows in work at once: 7 / 3
+  static constexpr int THREADS = 32 * (CW + 1);
+  static constexpr int ROWB = COLS * static_cast<int>(sizeof(TIn));
+  // shared memory: ring [STAGES][ROWB] | Hadamard tiles [CW] | scale, shift [2][COLS] (LN) |
+  // reduction slots [2][CW] | full, empty mbarriers [STAGES] | abort flag
+  static constexpr int FIXED = CW * kTileWords * 4 + (LN ? 8 * COLS : 0) + 8 * CW + 16;
+  static constexpr int FIT = (kSmemLimit - FIXED) / (ROWB + 16);
+  static constexpr int STAGES = FIT < kMaxStages ? FIT : kMaxStages;
+  static constexpr int SMEM = STAGES * (ROWB + 16) + FIXED;
+  static_assert(COLS == 512 * PASSES * WPR && CW % WPR == 0 && THREADS <= 1024 && STAGES >= 4 &&
+                SMEM <= kSmemLimit, "ring geometry");
+};
+
+struct Args {
+  const void* x;
+  long long rows, ldx;
+  const float* mod;
+  int shift_off, scale_off;
+  float eps;
+  int rotate, act;
+  int8_t* qhi;
+  int8_t* qlo;
+  float* qscale;
+  long long qld;
+};
+
+// Wait for a copy in flight to land, bounded, ignoring the abort flag (used when leaving).
+__device__ __forceinline__ bool drain_wait(uint64_t* bar, uint32_t parity) {
+  const uint32_t b = smem_u32(bar);
+  const unsigned long long t0 = globaltimer();
+  while (!mbar_test_sleep(b, parity)) {
+    if (globaltimer() - t0 > kWaitTimeoutNs) {
+      flag_error(kErrTimeoutDrain);
+      return false;
+    }
+  }
+  return true;
+}
+
+// Named barrier of team m (ids 2..; 1 is the consumers' barrier, 0 __syncthreads): the WPR warps
+// of the team, every thread taking part. bar.red.and also returns whether every thread's pred was
+// true.
+__device__ __forceinline__ void team_bar(int m, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(2 + m), "r"(threads) : "memory");
+}
+__device__ __forceinline__ bool team_all(int m, int threads, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}\n"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(pred)), "r"(2 + m), "r"(threads)
+      : "memory");
+  return r != 0;
+}
+
+// Sum (MAX false) or max of v over the team's row: warp shuffles, then for WPR > 1 one exchange
+// through the slots red[phase & 1][team's warps] around the team's barrier. A slot buffer is
+// written again two reductions later, after every warp of the team has passed the barrier of
+// the reduction in between and so has read it.
+template <int WPR, int CW, bool MAX>
+__device__ __forceinline__ float team_reduce(float v, float* tred, int team, int& phase) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float w = __shfl_xor_sync(0xffffffffu, v, o);
+    v = MAX ? fmaxf(v, w) : v + w;
+  }
+  if constexpr (WPR == 1) {
+    return v;
+  } else {
+    float* buf = tred + (phase & 1) * CW;
+    ++phase;
+    if ((threadIdx.x & 31) == 0) buf[(threadIdx.x >> 5) % WPR] = v;
+    team_bar(team, 32 * WPR);
+    float r = buf[0];
+#pragma unroll
+    for (int i = 1; i < WPR; ++i) r = MAX ? fmaxf(r, buf[i]) : r + buf[i];
+    return r;
+  }
+}
+
+template <int COLS, typename TIn, bool LN>
+__global__ void __launch_bounds__(Geom<COLS, TIn, LN>::THREADS, 1) rows_ring_kernel(const Args a) {
+  using G = Geom<COLS, TIn, LN>;
+  constexpr int S = G::STAGES;
+  extern __shared__ __align__(128) uint8_t smem[];
+  TIn* ring = reinterpret_cast<TIn*>(smem);
+  float* tiles = reinterpret_cast<float*>(smem + S * G::ROWB);
+  float* modv = tiles + G::CW * kTileWords;
+  float* red = modv + (LN ? 2 * COLS : 0);
+  uint64_t* full = reinterpret_cast<uint64_t*>(red + 2 * G::CW);
+  uint64_t* empty = full + S;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + S);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp == G::CW && lane == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], G::WPR);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const long long grid = gridDim.x;
+
+  if (warp == G::CW) {  // producer
+    if (lane == 0) {
+      const TIn* x = static_cast<const TIn*>(a.x);
+      long long issued = 0;
+      for (long long u = 0;; ++u) {
+        const long long row = blockIdx.x + u * grid;
+        if (row >= a.rows) break;
+        const int s = static_cast<int>(u % S);
+        const uint32_t n = static_cast<uint32_t>(u / S);
+        if (n > 0 && !mbar_wait(&empty[s], (n - 1) & 1, abort_flag, kErrTimeoutEmpty)) break;
+        mbar_arrive_expect_tx(&full[s], G::ROWB);
+        bulk_load_1d(ring + static_cast<size_t>(s) * COLS, x + row * a.ldx, G::ROWB, &full[s]);
+        issued = u + 1;
+      }
+      // the copies of the last S rows may still be in flight after an abort: they land before the
+      // CTA's shared memory is released (on the normal path these waits return at once)
+      for (long long u = issued > S ? issued - S : 0; u < issued; ++u)
+        if (!drain_wait(&full[u % S], static_cast<uint32_t>(u / S) & 1)) break;
+    }
+    return;
+  }
+
+  // the consumers stage the modulation vectors while the producer's first copies are in flight
+  if constexpr (LN) {
+    for (int c = threadIdx.x; c < COLS; c += 32 * G::CW) {
+      modv[c] = a.mod[a.scale_off + c];
+      modv[COLS + c] = a.mod[a.shift_off + c];
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(32 * G::CW) : "memory");
+  }
+  const int team = warp / G::WPR, wr = warp % G::WPR;
+  const int half = lane >> 4, t = lane & 15;
+  float* tb = tiles + warp * kTileWords + half * kTileHalf;
+  float* tred = red + team * G::WPR;
+  int phase = 0;
+  const float lane_sign = a.rotate ? sgn4(t) : 1.0f;  // the lane part of the Hadamard's output sigma
+  const float post = a.rotate ? 0.0625f : 1.0f;
+  const int col0 = wr * (512 * G::PASSES) + half * 256 + 4 * t;  // pass p adds 512
+  for (long long u = team;; u += G::TEAMS) {
+    const long long row = blockIdx.x + u * grid;
+    if (row >= a.rows) break;
+    const int s = static_cast<int>(u % S);
+    // a wait that gave up (bounded; the abort is raised) ends the whole team together, so no warp
+    // is left at a team barrier
+    const bool ok = mbar_wait(&full[s], static_cast<uint32_t>(u / S) & 1, abort_flag, kErrTimeoutFull);
+    if constexpr (G::WPR == 1) {
+      if (!ok) return;
+    } else {
+      if (!team_all(team, 32 * G::WPR, ok)) return;
+    }
+    f2 v[G::PASSES][8];
+    const TIn* src = ring + static_cast<size_t>(s) * COLS + col0;
+#pragma unroll
+    for (int p = 0; p < G::PASSES; ++p) load_lane16(src + 512 * p, v[p]);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);  // the stage may be refilled
+    if constexpr (LN) {
+      f2 s2 = dup2(0.f);
+#pragma unroll
+      for (int p = 0; p < G::PASSES; ++p)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s2 = add2(s2, v[p][j]);
+      const float sum = team_reduce<G::WPR, G::CW, false>(s2.x + s2.y, tred, team, phase);
+      const f2 nm = dup2(-sum / static_cast<float>(COLS));
+      f2 q2 = dup2(0.f);
+#pragma unroll
+      for (int p = 0; p < G::PASSES; ++p)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          v[p][j] = add2(v[p][j], nm);
+          q2 = fma2(v[p][j], v[p][j], q2);
+        }
+      const float ss = team_reduce<G::WPR, G::CW, false>(q2.x + q2.y, tred, team, phase);
+      const f2 rs = dup2(1.0f / sqrtf(ss / static_cast<float>(COLS) + a.eps));
+#pragma unroll
+      for (int p = 0; p < G::PASSES; ++p) ln_apply16(v[p], rs, modv + col0 + 512 * p, modv + COLS + col0 + 512 * p);
+    }
+    if (a.act == ANIMA_ACT_GELU) {
+#pragma unroll
+      for (int p = 0; p < G::PASSES; ++p)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[p][j] = gelu2(v[p][j]);
+    }
+    if (a.rotate) {
+#pragma unroll
+      for (int p = 0; p < G::PASSES; ++p) hadamard256_n<1>(tb, t, v, p);
+    }
+    float amax = 0.f;
+#pragma unroll
+    for (int p = 0; p < G::PASSES; ++p) amax = amax16(v[p], amax);
+    amax = team_reduce<G::WPR, G::CW, true>(amax, tred, team, phase);
+    // quantizing the unscaled Hadamard output with 127 / amax gives the same fp32 values as
+    // quantizing y / 16 (the 1/16 is a power of two)
+    const float inv = amax > 0.f ? 127.0f / amax : 0.f;
+    if (wr == 0 && lane == 0) a.qscale[row] = amax > 0.f ? (amax * post) / 127.0f : 1.0f;
+    const PairScale ps(inv * lane_sign, a.rotate != 0);
+    int8_t* hi = a.qhi + row * a.qld + col0;
+    int8_t* lo = a.qlo ? a.qlo + row * a.qld + col0 : nullptr;
+#pragma unroll
+    for (int p = 0; p < G::PASSES; ++p) quant_store16(v[p], ps, hi + 512 * p, lo ? lo + 512 * p : nullptr);
+  }
+}
+
+}  // namespace ring
 
 // ------------------------------------------------------------------ RMSNorm (warp per row)
 template <typename TIn, typename TOut>
@@ -804,9 +1043,37 @@ void launch_simt(cudaStream_t st, int sms, int M, int N, int K, float alpha, con
 #undef SIMT
 }
 
+template <int COLS, typename TIn, bool LN>
+int launch_ring(anima_ctx* ctx, const ring::Args& a) {
+  using G = ring::Geom<COLS, TIn, LN>;
+  const void* fn = reinterpret_cast<const void*>(&ring::rows_ring_kernel<COLS, TIn, LN>);
+  int st = set_max_dynamic_smem(fn, G::SMEM);
+  if (st) return st;
+  const long long need = (a.rows + G::TEAMS - 1) / G::TEAMS;
+  const int grid = static_cast<int>(need < ctx->num_sms ? need : ctx->num_sms);
+  ring::rows_ring_kernel<COLS, TIn, LN><<<grid, G::THREADS, G::SMEM, ctx->stream>>>(a);
+  return check_launch("rows_ring_kernel");
+}
+
+// The ring kernel takes the int8-output cases of 2048 and 8192 columns (rows read with 1D bulk
+// copies: 16-byte aligned row starts); everything else runs on rows_kernel.
+template <typename TIn, bool LN>
+bool ring_case(int cols, const TIn* x, int ldx, const anima_qact* q) {
+  return q && q->hi && (cols == 2048 || cols == 8192) && (!LN || cols == 2048) &&
+         (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (static_cast<long long>(ldx) * sizeof(TIn)) % 16 == 0;
+}
+
 template <typename TIn, typename TOut, bool LN>
 int launch_rows(anima_ctx* ctx, const TIn* x, int rows, int cols, int ldx, const float* mod, int so, int sco,
                 float eps, int rotate, TOut* y, const anima_qact* q, int act = ANIMA_ACT_NONE) {
+  if (ring_case<TIn, LN>(cols, x, ldx, q)) {
+    const ring::Args a{x, rows, ldx, mod, so, sco, eps, rotate, act, q->hi, q->lo, q->scale, q->ld};
+    if constexpr (LN) {
+      return launch_ring<2048, TIn, true>(ctx, a);
+    } else {
+      return cols == 2048 ? launch_ring<2048, TIn, false>(ctx, a) : launch_ring<8192, TIn, false>(ctx, a);
+    }
+  }
   int8_t* hi = q ? q->hi : nullptr;
   int8_t* lo = q ? q->lo : nullptr;
   float* sc = q ? q->scale : nullptr;

@@ -132,6 +132,15 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// 1D bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned) from global to shared
+// memory, completing on the mbarrier's transaction count.
+__device__ __forceinline__ void bulk_load_1d(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
 // TMA tile store / reduce-add of a shared-memory box (bulk-group completion), and its waits.
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
@@ -389,5 +398,35 @@ __device__ __forceinline__ f2 add2(f2 a, f2 b) { return __fadd2_rn(a, b); }
 __device__ __forceinline__ f2 mul2(f2 a, f2 b) { return __fmul2_rn(a, b); }
 __device__ __forceinline__ f2 fma2(f2 a, f2 b, f2 c) { return __ffma2_rn(a, b, c); }
 __device__ __forceinline__ f2 sub2(f2 a, f2 b) { return __ffma2_rn(b, dup2(-1.0f), a); }
+
+__device__ __forceinline__ float rcp_approx(float x) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+__device__ __forceinline__ float ex2_approx(float x) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
+// GELU(x) = x Phi(x) on a pair, with erfc from Abramowitz & Stegun 7.1.26 (|error of erf| <=
+// 1.5e-7): for z >= 0, erfc(z) = t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) exp(-z^2), t = 1 / (1 + p z).
+// With Q = Phi(-|x|) = erfc(|x| / sqrt 2) / 2, x Phi(x) = x (1 - Q) for x >= 0 and x Q for x < 0,
+// which is x / 2 + |x| (1/2 - Q) in both cases. The 1/2 of erfc is folded into the (negated)
+// coefficients, 1/sqrt 2 into p, and -1/2 log2(e) into the exponent's factor.
+__device__ __forceinline__ f2 gelu2(f2 x) {
+  const f2 ax = make_float2(fabsf(x.x), fabsf(x.y));
+  const f2 d = fma2(ax, dup2(0.3275911f * 0.70710678118654752f), dup2(1.0f));
+  const f2 t = make_float2(rcp_approx(d.x), rcp_approx(d.y));
+  const f2 n = mul2(x, mul2(x, dup2(-0.72134752044448170f)));  // -x^2 / 2 log2(e)
+  const f2 e = make_float2(ex2_approx(n.x), ex2_approx(n.y));
+  f2 q = fma2(dup2(-0.5f * 1.061405429f), t, dup2(-0.5f * -1.453152027f));
+  q = fma2(q, t, dup2(-0.5f * 1.421413741f));
+  q = fma2(q, t, dup2(-0.5f * -0.284496736f));
+  q = fma2(q, t, dup2(-0.5f * 0.254829592f));  // -erfc / (2 t exp(-x^2 / 2))
+  const f2 h = fma2(q, mul2(t, e), dup2(0.5f));  // 1/2 - Q
+  return fma2(ax, h, mul2(x, dup2(0.5f)));
+}
 
 }  // namespace anima

@@ -7,7 +7,7 @@ Per block (x is the fp32 residual stream [B L, 2048], as in the reference):
                   residual in the epilogue
   cross-attention LN+adaLN+ConvRot+quant -> q GEMM with per-head RMSNorm -> attention against the
                   per-prompt K/V cache -> ConvRot+quant -> o GEMM + gated residual
-  MLP             LN+adaLN+ConvRot+quant -> layer1 GEMM (fp16 pre-activation) -> GELU+ConvRot+quant
+  MLP             LN+adaLN+ConvRot+quant -> layer1 GEMM (+GELU epilogue, fp16) -> ConvRot+quant
                   -> layer2 GEMM + gated residual
 Activations entering a ConvRot linear are per-token int8 planes (precision "a16": hi + lo/254,
 two MMAs, ~16-bit; "a8": one plane, plain W8A8). Attention runs on fp16 q/k/v/P by default (same
@@ -311,9 +311,10 @@ class AnimaDiT:
         ops.linear(qa, blk["cross_o"], out=x, resid=True, gate=m_cross, g_off=2 * D, name="dit.cross.out")
         # MLP
         ops.layernorm_mod_quant(x, m_mlp, 0, D, D, out=qa)
-        # layer1 stores its pre-activation (fp16); GELU runs in the memory-bound ConvRot+quant pass
-        h = ops.linear(qa, blk["l1"], out=bufs["h"], name="dit.mlp1")
-        ops.rotate_quant(h, out=qh, act="gelu")
+        # GELU on layer1's fp32 accumulators in the GEMM epilogue (it has issue slots to spare), then
+        # the fp16 hidden layer's ConvRot+quant
+        h = ops.linear(qa, blk["l1"], out=bufs["h"], act="gelu", name="dit.mlp1")
+        ops.rotate_quant(h, out=qh)
         ops.linear(qh, blk["l2"], out=x, resid=True, gate=m_mlp, g_off=2 * D, name="dit.mlp2")
 
     def _gather_kv(self, qkv: torch.Tensor, B: int, L: int, bufs: dict) -> torch.Tensor:

@@ -238,6 +238,7 @@ def kernel_case(args):
     ln    LayerNorm + adaLN + ConvRot + two-plane quantization of [4096, 2048]
     gelu  GELU + ConvRot + quantization of the fp16 MLP hidden [4096, 8192]
     rotq  ConvRot + quantization of the fp16 attention output [4096, 2048]
+    rotq8k  ConvRot + quantization of the fp16 MLP hidden after GELU [4096, 8192]
     xembed / final  the fp32 SIMT GEMMs of the patch embedding (68 -> 2048) and the final layer (2048 -> 64)"""
     import torch
 
@@ -321,8 +322,8 @@ def kernel_case(args):
         ids = torch.randint(0, 4096, (512,)).tolist()
         fn = lambda: ad(te.encode(ids), ids)  # noqa: E731
         work, unit = 1.0, "prompts/s"
-    elif args.kernel in ("gelu", "rotq"):
-        K = 8192 if args.kernel == "gelu" else 2048
+    elif args.kernel in ("gelu", "rotq", "rotq8k"):
+        K = 2048 if args.kernel == "rotq" else 8192
         h = torch.randn(M, K, device="cuda").half()
         q = ops.QuantRows.empty(M, K, planes, "cuda")
         act = "gelu" if args.kernel == "gelu" else None
@@ -333,21 +334,36 @@ def kernel_case(args):
     for _ in range(3):
         fn()
     torch.cuda.synchronize()
-    # each sample times `batch` back-to-back launches, so short kernels are not measured with the
-    # host's launch latency; inputs stay L2-resident between launches when they fit
+    # each sample times `batch` back-to-back launches replayed from a CUDA graph, so short kernels
+    # are not measured with the host's per-call latency (Python, ctypes, launch); the VAE and text
+    # encoder cases, which read sizes back to the host, run eagerly. Inputs stay L2-resident
+    # between launches when they fit.
+    graph = None
+    if not args.no_graph and args.kernel not in ("vae", "te"):
+        graph = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.graph(graph, stream=side):
+            for _ in range(args.batch):
+                fn()
+        torch.cuda.current_stream().wait_stream(side)
     ts = []
     for _ in range(args.reps):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        for _ in range(args.batch):
-            fn()
+        if graph is not None:
+            graph.replay()
+        else:
+            for _ in range(args.batch):
+                fn()
         e1.record()
         e1.synchronize()
         ts.append(e0.elapsed_time(e1) / args.batch)
     dev.Context.get(0).sync()
     ms = statistics.median(ts)
     rate = work / (ms * 1e-3) / {"GB/s": 1e9, "images/s": 1.0, "prompts/s": 1.0}.get(unit, 1e12)
-    print(json.dumps({"kernel": args.kernel, "precision": args.precision, "attn": args.attn, "ms_median": ms,
+    print(json.dumps({"kernel": args.kernel, "precision": args.precision, "attn": args.attn, "graph": graph is not None,
+                      "ms_median": ms,
                       "ms_min": min(ts), "rate": rate, "unit": unit, "reps": args.reps}), flush=True)
 
 
@@ -580,7 +596,7 @@ def main():
     ap.add_argument("--attn", default="f16", choices=["bf16", "f16"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--no-graph", action="store_true", help="launch kernels from Python per step instead of CUDA graphs")
+    ap.add_argument("--no-graph", action="store_true", help="launch kernels from Python per step (kernel cases: per launch) instead of CUDA graphs")
     ap.add_argument("--cfg", type=float, default=None,
                     help="BASELINE configs[4]: guidance scale with a negative context (batch 2 per image), 30 steps")
     ap.add_argument("--res", type=int, default=1024, help="with --cfg: image side (1024 or 1536)")

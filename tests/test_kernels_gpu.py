@@ -102,6 +102,35 @@ def test_gelu_rotate_quant(ops):
     assert rel_l2(q.dequant().cpu().numpy(), ref) < 6e-5
 
 
+# The int8 outputs of 2048- and 8192-column rows run on the persistent ring kernel (rows streamed
+# into shared-memory stages by bulk copies). Row counts: fewer than one CTA's teams, not a multiple
+# of the grid, and more rows per CTA than the ring has stages (stages refilled); rows read at a
+# stride wider than the row. Every row is checked, not only the whole-matrix error.
+@pytest.mark.parametrize("kind,rows,pad", [
+    ("ln", 1, 0), ("ln", 1633, 0), ("ln", 4096, 0),
+    ("rot16", 5, 64), ("rot16", 6000, 0), ("rotbf16", 300, 0), ("rot32", 4000, 0),
+    ("gelu", 3, 0), ("gelu", 4096, 0), ("rot32_8192", 1000, 256)])
+def test_ring_rows(ops, kind, rows, pad):
+    cols = 8192 if kind in ("gelu", "rot32_8192") else 2048
+    dtype = {"rot16": torch.float16, "gelu": torch.float16, "rotbf16": torch.bfloat16}.get(kind, torch.float32)
+    wide = (randn((rows, cols + pad), 61 + rows) * 2 + 0.25).to(dtype)
+    x = wide[:, :cols]
+    xf = x.float().numpy()
+    if kind == "ln":
+        mod = randn((6144,), 62, 0.5)
+        q = ops.layernorm_mod_quant(x.contiguous().to(DEV), mod.to(DEV), 0, 2048, 2048)
+        ref = oracle.rotate(oracle.layer_norm(xf) * (1 + mod[2048:4096].numpy()) + mod[:2048].numpy())
+    else:
+        q = ops.rotate_quant(wide.to(DEV)[:, :cols], act="gelu" if kind == "gelu" else None)
+        ref = oracle.rotate(oracle.gelu(xf) if kind == "gelu" else xf)
+    got = q.dequant().cpu().numpy()
+    row_err = np.sqrt(((got - ref) ** 2).sum(1) / (ref ** 2).sum(1))
+    assert row_err.max() < 1.5e-4, (row_err.argmax(), row_err.max())
+    assert rel_l2(got, ref) < 6e-5
+    np.testing.assert_allclose(q.scale.cpu().numpy(), np.abs(ref).max(1) / 127, rtol=1e-5)
+    assert q.hi.abs().max().item() <= 127 and q.lo.abs().max().item() <= 127
+
+
 @pytest.mark.parametrize("cols", [256, 2048])
 def test_rotate_plain(ops, cols):
     x = randn((67, cols), 6)
