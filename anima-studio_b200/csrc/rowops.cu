@@ -432,8 +432,9 @@ __global__ void __launch_bounds__(256, 4) rows_kernel(const TIn* __restrict__ x,
 // flight hold no registers and overlap the arithmetic of earlier rows. Teams of WPR consumer
 // warps take one row each at a time, every warp PASSES x 512 columns of it (two groups per pass,
 // one per half-warp); the row's sums and maximum go across the team through shared memory. Rows
-// are split this finely so that the 27-28 rows an SM gets spread evenly over many warps: at 2048
-// columns 7 teams of 4 warps take 4 rows each. CTA b takes rows b, b + grid, b + 2 grid, ... and
+// are split so that the 27-28 rows an SM gets divide evenly over the teams (at 2048 columns 7
+// teams of 2 warps take 4 rows each; at 8192, 3 teams of 8 warps 9-10 rows each), with enough
+// columns per warp that the per-row work (waits, reductions, the scale) is spread thin. CTA b takes rows b, b + grid, b + 2 grid, ... and
 // team m of it the CTA's m-th, (m + TEAMS)-th, ... row.
 namespace ring {
 
@@ -442,15 +443,15 @@ constexpr int kMaxStages = 32;
 
 template <int COLS, typename TIn, bool LN>
 struct Geom {
-  static constexpr int PASSES = COLS == 2048 ? 1 : 2;  // passes (512 columns each) per warp
-  static constexpr int WPR = COLS / (512 * PASSES);     // warps per row: 4 at 2048, 8 at 8192
-  static constexpr int CW = WPR == 4 ? 28 : 24;         // consumer warps (+ 1 producer: 29 / 25)
-  static constexpr int TEAMS = CW / WPR;                // rows in work at once: 7 / 3
+  static constexpr int PASSES = 2;                   // passes (512 columns each) per warp
+  static constexpr int WPR = COLS / (512 * PASSES);  // warps per row: 2 at 2048, 8 at 8192
+  static constexpr int CW = COLS == 2048 ? 14 : 24;  // consumer warps (+ 1 producer: 15 / 25)
+  static constexpr int TEAMS = CW / WPR;             // rows in work at once: 7 / 3
   static constexpr int THREADS = 32 * (CW + 1);
   static constexpr int ROWB = COLS * static_cast<int>(sizeof(TIn));
   // shared memory: ring [STAGES][ROWB] | Hadamard tiles [CW] | scale, shift [2][COLS] (LN) |
-  // reduction slots [2][CW] | full, empty mbarriers [STAGES] | abort flag
-  static constexpr int FIXED = CW * kTileWords * 4 + (LN ? 8 * COLS : 0) + 8 * CW + 16;
+  // reduction slots [2][CW] | full, empty mbarriers [STAGES] | modulation mbarrier | abort flag
+  static constexpr int FIXED = CW * kTileWords * 4 + (LN ? 8 * COLS : 0) + 8 * CW + 8 + 16;
   static constexpr int FIT = (kSmemLimit - FIXED) / (ROWB + 16);
   static constexpr int STAGES = FIT < kMaxStages ? FIT : kMaxStages;
   static constexpr int SMEM = STAGES * (ROWB + 16) + FIXED;
@@ -484,7 +485,7 @@ __device__ __forceinline__ bool drain_wait(uint64_t* bar, uint32_t parity) {
   return true;
 }
 
-// Named barrier of team m (ids 2..; 1 is the consumers' barrier, 0 __syncthreads): the WPR warps
+// Named barrier of team m (ids 2..; 0 is __syncthreads): the WPR warps
 // of the team, every thread taking part. bar.red.and also returns whether every thread's pred was
 // true.
 __device__ __forceinline__ void team_bar(int m, int threads) {
@@ -539,13 +540,15 @@ __global__ void __launch_bounds__(Geom<COLS, TIn, LN>::THREADS, 1) rows_ring_ker
   float* red = modv + (LN ? 2 * COLS : 0);
   uint64_t* full = reinterpret_cast<uint64_t*>(red + 2 * G::CW);
   uint64_t* empty = full + S;
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + S);
+  uint64_t* modbar = empty + S;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(modbar + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (warp == G::CW && lane == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], G::WPR);
     }
+    mbar_init(modbar, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -555,6 +558,11 @@ __global__ void __launch_bounds__(Geom<COLS, TIn, LN>::THREADS, 1) rows_ring_ker
   if (warp == G::CW) {  // producer
     if (lane == 0) {
       const TIn* x = static_cast<const TIn*>(a.x);
+      if constexpr (LN) {  // the scale and shift vectors, once per CTA, ahead of the first row
+        mbar_arrive_expect_tx(modbar, 8 * COLS);
+        bulk_load_1d(modv, a.mod + a.scale_off, 4 * COLS, modbar);
+        bulk_load_1d(modv + COLS, a.mod + a.shift_off, 4 * COLS, modbar);
+      }
       long long issued = 0;
       for (long long u = 0;; ++u) {
         const long long row = blockIdx.x + u * grid;
@@ -570,18 +578,11 @@ __global__ void __launch_bounds__(Geom<COLS, TIn, LN>::THREADS, 1) rows_ring_ker
       // CTA's shared memory is released (on the normal path these waits return at once)
       for (long long u = issued > S ? issued - S : 0; u < issued; ++u)
         if (!drain_wait(&full[u % S], static_cast<uint32_t>(u / S) & 1)) break;
+      if constexpr (LN) drain_wait(modbar, 0);
     }
     return;
   }
 
-  // the consumers stage the modulation vectors while the producer's first copies are in flight
-  if constexpr (LN) {
-    for (int c = threadIdx.x; c < COLS; c += 32 * G::CW) {
-      modv[c] = a.mod[a.scale_off + c];
-      modv[COLS + c] = a.mod[a.shift_off + c];
-    }
-    asm volatile("bar.sync 1, %0;" ::"r"(32 * G::CW) : "memory");
-  }
   const int team = warp / G::WPR, wr = warp % G::WPR;
   const int half = lane >> 4, t = lane & 15;
   float* tb = tiles + warp * kTileWords + half * kTileHalf;
@@ -596,7 +597,9 @@ __global__ void __launch_bounds__(Geom<COLS, TIn, LN>::THREADS, 1) rows_ring_ker
     const int s = static_cast<int>(u % S);
     // a wait that gave up (bounded; the abort is raised) ends the whole team together, so no warp
     // is left at a team barrier
-    const bool ok = mbar_wait(&full[s], static_cast<uint32_t>(u / S) & 1, abort_flag, kErrTimeoutFull);
+    bool ok = true;
+    if (LN && u == team) ok = mbar_wait(modbar, 0, abort_flag, kErrTimeoutFull);  // before the first row
+    ok = ok && mbar_wait(&full[s], static_cast<uint32_t>(u / S) & 1, abort_flag, kErrTimeoutFull);
     if constexpr (G::WPR == 1) {
       if (!ok) return;
     } else {
@@ -645,7 +648,7 @@ __global__ void __launch_bounds__(Geom<COLS, TIn, LN>::THREADS, 1) rows_ring_ker
     amax = team_reduce<G::WPR, G::CW, true>(amax, tred, team, phase);
     // quantizing the unscaled Hadamard output with 127 / amax gives the same fp32 values as
     // quantizing y / 16 (the 1/16 is a power of two)
-    const float inv = amax > 0.f ? 127.0f / amax : 0.f;
+    const float inv = amax > 0.f ? __fdividef(127.0f, amax) : 0.f;
     if (wr == 0 && lane == 0) a.qscale[row] = amax > 0.f ? (amax * post) / 127.0f : 1.0f;
     const PairScale ps(inv * lane_sign, a.rotate != 0);
     int8_t* hi = a.qhi + row * a.qld + col0;
