@@ -904,8 +904,10 @@ __global__ void euler_kernel(float* x, const float* __restrict__ v, const float*
 // and the slices' partial tiles are summed through shared memory at the end. The next tile's
 // global loads are issued before the current tile's FMAs.
 // QA: A is given as quantized rows, A[m, k] = qs[m] * (qhi[m, k] + qlo[m, k] / 254).
-template <typename TB, bool QA, int BM>
-__global__ void __launch_bounds__(256) simt_gemm_kernel(int M, int N, int K, float alpha, const float* __restrict__ A,
+// VEC: A (fp32) and B are read as 16-byte vectors (4 fp32 or 8 16-bit values along k; needs K,
+// lda and ldb multiples of 8 and 16-byte aligned rows), else element by element.
+template <typename TB, bool QA, int BM, bool VEC>
+__global__ void __launch_bounds__(256, 2) simt_gemm_kernel(int M, int N, int K, float alpha, const float* __restrict__ A,
                                                         int lda, const TB* __restrict__ B, int ldb,
                                                         const float* __restrict__ bias, int act, float* C, int ldc,
                                                         int accumulate, const float* __restrict__ gate, int gate_off,
@@ -924,27 +926,57 @@ __global__ void __launch_bounds__(256) simt_gemm_kernel(int M, int N, int K, flo
   float* As = smem + sl * SLICE;
   float* Bs = As + BK * AS;
   float ra[AE], rb[BE];
+  // element e of this thread's share of the A (B) tile: row i / BK, column i % BK of the tile, with
+  // i = lt + e * ST element by element, or, for 16-byte vectors of V elements, i = V * (lt + (e / V)
+  // * ST) + e % V (a vector's elements are consecutive along k)
+  auto a_idx = [&](int e) {
+    return VEC && !QA ? 4 * (lt + (e / 4) * ST) + e % 4 : lt + e * ST;
+  };
+  constexpr int VB = 16 / static_cast<int>(sizeof(TB));
+  auto b_idx = [&](int e) { return VEC ? VB * (lt + (e / VB) * ST) + e % VB : lt + e * ST; };
   auto fetch = [&](int k0) {
+    if constexpr (VEC && !QA) {
 #pragma unroll
-    for (int e = 0; e < AE; ++e) {
-      const int i = lt + e * ST, r = i / BK, k = k0 + i % BK, m = m0 + r;
-      float a = 0.f;
-      if (m < M && k < K) {
-        const size_t idx = static_cast<size_t>(m) * lda + k;
-        if constexpr (QA) {
-          a = static_cast<float>(qhi[idx]);
-          if (qlo) a += static_cast<float>(qlo[idx]) * (1.0f / 254.0f);
-          a *= qs[m];
-        } else {
-          a = A[idx];
-        }
+      for (int e = 0; e < AE; e += 4) {
+        const int i = a_idx(e), r = i / BK, k = k0 + i % BK, m = m0 + r;
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (m < M && k < K) a = *reinterpret_cast<const float4*>(A + static_cast<size_t>(m) * lda + k);
+        ra[e] = a.x; ra[e + 1] = a.y; ra[e + 2] = a.z; ra[e + 3] = a.w;
       }
-      ra[e] = a;
-    }
+    } else {
 #pragma unroll
-    for (int e = 0; e < BE; ++e) {
-      const int i = lt + e * ST, r = i / BK, k = k0 + i % BK, n = n0 + r;
-      rb[e] = (n < N && k < K) ? to_f<TB>(B[static_cast<size_t>(n) * ldb + k]) : 0.f;
+      for (int e = 0; e < AE; ++e) {
+        const int i = a_idx(e), r = i / BK, k = k0 + i % BK, m = m0 + r;
+        float a = 0.f;
+        if (m < M && k < K) {
+          const size_t idx = static_cast<size_t>(m) * lda + k;
+          if constexpr (QA) {
+            a = static_cast<float>(qhi[idx]);
+            if (qlo) a += static_cast<float>(qlo[idx]) * (1.0f / 254.0f);
+            a *= qs[m];
+          } else {
+            a = A[idx];
+          }
+        }
+        ra[e] = a;
+      }
+    }
+    if constexpr (VEC) {
+#pragma unroll
+      for (int e = 0; e < BE; e += VB) {
+        const int i = b_idx(e), r = i / BK, k = k0 + i % BK, n = n0 + r;
+        uint4 u = make_uint4(0u, 0u, 0u, 0u);
+        if (n < N && k < K) u = *reinterpret_cast<const uint4*>(B + static_cast<size_t>(n) * ldb + k);
+        const TB* h = reinterpret_cast<const TB*>(&u);
+#pragma unroll
+        for (int j = 0; j < VB; ++j) rb[e + j] = to_f<TB>(h[j]);
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < BE; ++e) {
+        const int i = b_idx(e), r = i / BK, k = k0 + i % BK, n = n0 + r;
+        rb[e] = (n < N && k < K) ? to_f<TB>(B[static_cast<size_t>(n) * ldb + k]) : 0.f;
+      }
     }
   };
   float acc[4][4] = {};
@@ -954,12 +986,12 @@ __global__ void __launch_bounds__(256) simt_gemm_kernel(int M, int N, int K, flo
   for (int t = 0; t < steps; ++t) {
 #pragma unroll
     for (int e = 0; e < AE; ++e) {
-      const int i = lt + e * ST;
+      const int i = a_idx(e);
       As[(i % BK) * AS + i / BK] = ra[e];
     }
 #pragma unroll
     for (int e = 0; e < BE; ++e) {
-      const int i = lt + e * ST;
+      const int i = b_idx(e);
       Bs[(i % BK) * BS + i / BK] = rb[e];
     }
     __syncthreads();
@@ -1037,12 +1069,20 @@ void launch_simt(cudaStream_t st, int sms, int M, int N, int K, float alpha, con
                  int gate_off, const int8_t* qhi = nullptr, const int8_t* qlo = nullptr, const float* qs = nullptr) {
   const int bm = simt_bm(M, N, sms);
   const dim3 grid((N + 63) / 64, (M + bm - 1) / bm);
-#define SIMT(BMV)                                                                                                \
-  simt_gemm_kernel<TB, QA, BMV><<<grid, 256, 0, st>>>(M, N, K, alpha, A, lda, B, ldb, bias, act, C, ldc, accumulate, \
-                                                      gate, gate_off, qhi, qlo, qs)
-  if (bm == 64) SIMT(64);
-  else if (bm == 32) SIMT(32);
-  else SIMT(16);
+  const bool vec = K % 8 == 0 && ldb % 8 == 0 && (reinterpret_cast<uintptr_t>(B) & 15) == 0 &&
+                   (QA || (lda % 8 == 0 && (reinterpret_cast<uintptr_t>(A) & 15) == 0));
+#define SIMT(BMV, V)                                                                                             \
+  simt_gemm_kernel<TB, QA, BMV, V><<<grid, 256, 0, st>>>(M, N, K, alpha, A, lda, B, ldb, bias, act, C, ldc, accumulate, \
+                                                         gate, gate_off, qhi, qlo, qs)
+  if (vec) {
+    if (bm == 64) SIMT(64, true);
+    else if (bm == 32) SIMT(32, true);
+    else SIMT(16, true);
+  } else {
+    if (bm == 64) SIMT(64, false);
+    else if (bm == 32) SIMT(32, false);
+    else SIMT(16, false);
+  }
 #undef SIMT
 }
 
