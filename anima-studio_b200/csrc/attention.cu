@@ -946,6 +946,7 @@ int attention_launch(anima_ctx* ctx, const anima_attention_args* a, bool static_
   ANIMA_REQUIRE(a->batch > 0 && a->heads > 0 && a->Lq > 0 && a->Lk > 0, "anima_attention: empty problem");
   ANIMA_REQUIRE(a->q && a->k && a->v && a->out, "anima_attention: NULL data pointer");
   const int group = a->group > 1 ? a->group : 1;
+  if (attention_planes_ok(a)) return attention_planes(ctx, a);  // the VAE's wide single head
   if (group > 1 || a->causal || a->head_dim != attn::HD || a->dtype == ANIMA_F32) {
     ANIMA_REQUIRE(a->dtype == ANIMA_F32 || a->dtype == ANIMA_BF16 || a->dtype == ANIMA_F16,
                   "anima_attention: q/k/v dtype %d", a->dtype);

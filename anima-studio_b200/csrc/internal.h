@@ -22,6 +22,10 @@ struct anima_ctx {
   void* attn_static_ws = nullptr;   // static workspace of anima_attention_noalloc (flags first)
   int8_t* w4_ws = nullptr;          // int8 grid of the W4 weight anima_linear is running (gemm_i8.cu)
   size_t w4_ws_bytes = 0;
+  void* vae_ws = nullptr;           // bf16 hi/lo planes of the VAE convolution's input (vae.cu)
+  size_t vae_ws_bytes = 0;
+  void* mat_ws = nullptr;           // scores, probability and operand planes of attention_planes (vae.cu)
+  size_t mat_ws_bytes = 0;
 };
 
 namespace anima {
@@ -50,6 +54,11 @@ struct DeviceScope {
 // cudaFuncAttributeMaxDynamicSharedMemorySize = bytes for kernel fn on the current device. The
 // attribute belongs to the device, so it is set once per (kernel, device) pair, under a lock.
 int set_max_dynamic_smem(const void* fn, int bytes);
+
+// Single-head attention with a wide head (the VAE's d = 384 over every latent pixel) on the tensor
+// cores, with the scores materialised (vae.cu); attention_planes_ok says whether it takes `a`.
+bool attention_planes_ok(const anima_attention_args* a);
+int attention_planes(anima_ctx* ctx, const anima_attention_args* a);
 
 // Decode 4-bit weights to their int8 grid values (rowops.cu; the arithmetic of anima_unpack_w4):
 // out int8 [N, K] from packed nibbles [N, K/2] and fp8 group scales [N, K/16].

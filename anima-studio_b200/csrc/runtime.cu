@@ -208,6 +208,8 @@ int anima_ctx_destroy(anima_ctx* ctx) {
   if (ctx->attn_ws) cudaFree(ctx->attn_ws);
   if (ctx->attn_flags) cudaFree(ctx->attn_flags);
   if (ctx->w4_ws) cudaFree(ctx->w4_ws);
+  if (ctx->vae_ws) cudaFree(ctx->vae_ws);
+  if (ctx->mat_ws) cudaFree(ctx->mat_ws);
   delete ctx;
   return ANIMA_OK;
 }

@@ -72,6 +72,22 @@ def test_single_head_attention_d384():
     assert rel_l2(out, text_np.attention(q, k, v)[0]) < 1e-5
 
 
+# At least 2^20 scores the single head runs on the tensor cores: S = Q K^T and O = P V as
+# two-plane bf16 GEMMs (about 16 significant bits per operand, fp32 sums) around a row softmax.
+@pytest.mark.parametrize("Lq,Lk", [(2048, 2048), (1024, 1536)])
+def test_single_head_attention_d384_tensor_cores(Lq, Lk):
+    ops = pkg("ops")
+    D = 384
+    g = torch.Generator().manual_seed(Lq + Lk)
+    q = torch.randn(Lq, 3 * D, generator=g) * 1.5
+    kv = torch.randn(Lk, 3 * D, generator=g)
+    out = ops.attention(q.to(DEV), kv.to(DEV), kv.to(DEV), Lq=Lq, Lk=Lk, H=1, D=D, ldq=3 * D, ldk=3 * D, ldv=3 * D,
+                        q_off=0, k_off=D, v_off=2 * D, out_dtype=torch.float32).cpu().numpy()
+    qn = q[:, :D].numpy()[None]
+    kn, vn = kv[:, D:2 * D].numpy()[None], kv[:, 2 * D:].numpy()[None]
+    assert rel_l2(out, text_np.attention(qn, kn, vn)[0]) < 3e-5
+
+
 def test_vae_decoder_matches_reference():
     syn, vae = pkg("synthetic"), pkg("vae")
     g = dict(np.load(os.path.join(GOLDEN, "vae_64.npz")))
