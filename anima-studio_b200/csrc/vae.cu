@@ -507,6 +507,26 @@ static int split_planes(anima_ctx* ctx, const float* x, int h, int w, int c, lon
 // row softmax between them that writes P as planes. Taken for fp32 q/k/v and output, one head,
 // no mask, batch 1, d a multiple of 64, and at least 2^20 scores (smaller ones stay on the
 // CUDA-core kernel, as the text models' do).
+int matmul_planes(anima_ctx* ctx, int M, int N, int K, const float* A, int lda, const void* B, const float* bias,
+                  float* C, int ldc, int accumulate) {
+  if (M < 256 || K % 8 != 0 || lda % 8 != 0 || ldc != N || (reinterpret_cast<uintptr_t>(A) & 15) != 0 ||
+      (reinterpret_cast<uintptr_t>(B) & 15) != 0 || (reinterpret_cast<uintptr_t>(C) & 15) != 0)
+    return ANIMA_ERR_UNSUPPORTED;
+  const size_t plane = static_cast<size_t>(M) * K;
+  if (ctx->vae_ws_bytes < 2 * plane * sizeof(__nv_bfloat16)) {
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    ANIMA_CUDA(cudaStreamIsCapturing(ctx->stream, &cap));
+    if (cap != cudaStreamCaptureStatusNone) return ANIMA_ERR_UNSUPPORTED;
+  }
+  int st = vae::grow_ws(ctx, &ctx->vae_ws, &ctx->vae_ws_bytes, 2 * plane * sizeof(__nv_bfloat16), "anima_matmul");
+  if (st) return st;
+  auto* hi = static_cast<__nv_bfloat16*>(ctx->vae_ws);
+  auto* lo = hi + plane;
+  st = vae::split_planes(ctx, A, 1, M, K, lda, 0, hi, lo);
+  if (st) return st;
+  return vae::tc_gemm(ctx, hi, lo, 1, M, K, 1, B, N, bias, C, accumulate);
+}
+
 bool attention_planes_ok(const anima_attention_args* a) {
   return a->dtype == ANIMA_F32 && a->out_dtype == ANIMA_F32 && a->heads == 1 && a->batch == 1 && a->group <= 1 &&
          !a->causal && !a->key_len && a->head_dim % 64 == 0 && a->head_dim <= 1024 &&

@@ -204,6 +204,25 @@ def test_matmul_simt(ops, M, N, K, kind):
     assert rel_l2(y, ref) < 2e-6
 
 
+# bf16 weights without scale, activation or gate run on the tensor cores (A split into two bf16
+# planes: ~2^-17 relative per element, fp32 sums); the rest stays on the CUDA-core kernel above
+@pytest.mark.parametrize("M,N,K,resid", [(4096, 64, 2048, False), (512, 1024, 1024, True), (300, 3, 16, False),
+                                         (1000, 384, 96, True)])
+def test_matmul_bf16_tensor_cores(ops, M, N, K, resid):
+    W = pkg("weights")
+    x = randn((M, K), 23)
+    w = (randn((N, K), 24, 0.05)).to(torch.bfloat16)
+    b = randn((N,), 25, 0.1)
+    lin = W.Linear("bf16", N, K, w.to(DEV).contiguous(), None, bias=b.to(DEV))
+    base = randn((M, N), 26)
+    out = base.clone().to(DEV) if resid else None
+    y = ops.matmul(x.to(DEV), lin, out=out, resid=resid).cpu().numpy()
+    ref = x.double().numpy() @ w.double().numpy().T + b.double().numpy()
+    if resid:
+        ref = ref + base.double().numpy()
+    assert rel_l2(y, ref) < 2e-5
+
+
 # ----------------------------------------------------------------------------- tcgen05 int8 GEMM
 
 def make_linear(N, K, seed):
