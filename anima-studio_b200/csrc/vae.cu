@@ -1,98 +1,14 @@
-// Wan-2.1 VAE decoder operators (app/models/vae.js; math of tools/reference.py:254-295):
-// NHWC 3x3 convolution as an implicit GEMM with the nearest 2x upsample of Resample fused into its
-// loads, and the decoder's channel RMS norm with the SiLU that follows it.
-//
-// The VAE runs once per image (after the denoising loop), so these are CUDA-core kernels: fp32
-// activations, bf16 weights (OHWI, as the reference's asset builder stores them), fp32 sums.
+// Wan-2.1 VAE decoder operators (app/models/vae.js; math of tools/reference.py:254-295): the NHWC
+// 3x3 convolution as a tensor-core implicit GEMM (the nearest 2x upsample of Resample applied when
+// the input is split into its bf16 planes), the same GEMM for bf16 matmuls and for the decoder's
+// wide single-head attention, and the channel RMS norm with the SiLU that follows it. Activations
+// stay fp32 between kernels; the weights are bf16 (OHWI, as the reference's asset builder stores
+// them).
 #include "internal.h"
 #include "sm100.cuh"
 
 namespace anima {
 namespace vae {
-
-constexpr int BM = 64;   // output pixels per tile
-constexpr int BN = 64;   // output channels per tile
-constexpr int BK = 32;   // input channels per k-step (one filter tap at a time)
-
-// out[p, o] (+)= bias[o] + sum_{ky, kx, c} in[p + (ky - 1, kx - 1), c] * w[o, ky, kx, c], pad 1;
-// with UP the input is first upsampled 2x (nearest): in_up[y, x] = in[y / 2, x / 2].
-// A 256-thread CTA computes a 64-pixel x 64-channel tile, 4 x 4 per thread, from k-major tiles
-// of the gathered inputs and the weights in shared memory.
-template <bool UP>
-__global__ void __launch_bounds__(256) conv3x3_kernel(const float* __restrict__ x, int h, int w, int cin,
-                                                      const __nv_bfloat16* __restrict__ wt,
-                                                      const float* __restrict__ bias, int cout, float* out,
-                                                      int accumulate) {
-  __shared__ __align__(16) float As[BK][BM];
-  __shared__ __align__(16) float Bs[BK][BN];
-  const int Ho = UP ? 2 * h : h, Wo = UP ? 2 * w : w;
-  const long long M = static_cast<long long>(Ho) * Wo;
-  const long long p0 = static_cast<long long>(blockIdx.x) * BM;
-  const int o0 = blockIdx.y * BN;
-  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
-  // the pixel this thread gathers for the A tile, and its output coordinates
-  const int ap = tid & 63;
-  const long long gp = p0 + ap;
-  const int oy = gp < M ? static_cast<int>(gp / Wo) : 0, ox = gp < M ? static_cast<int>(gp % Wo) : 0;
-  const int K = 9 * cin;
-  float acc[4][4] = {};
-  for (int tap = 0; tap < 9; ++tap) {
-    const int iy = oy + tap / 3 - 1, ix = ox + tap % 3 - 1;  // in the (upsampled) input
-    const bool inside = gp < M && iy >= 0 && iy < Ho && ix >= 0 && ix < Wo;
-    const float* src = inside ? x + (static_cast<long long>(UP ? iy / 2 : iy) * w + (UP ? ix / 2 : ix)) * cin : x;
-    for (int c0 = 0; c0 < cin; c0 += BK) {
-      __syncthreads();
-      // A: 64 pixels x 32 channels, 4 channels per load, two loads per thread
-#pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        const int cc = ((tid >> 6) + 4 * r) * 4;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (inside && c0 + cc < cin) v = *reinterpret_cast<const float4*>(src + c0 + cc);
-        As[cc][ap] = v.x;
-        As[cc + 1][ap] = v.y;
-        As[cc + 2][ap] = v.z;
-        As[cc + 3][ap] = v.w;
-      }
-      // B: 64 output channels x 32 inputs of this tap, 8 bf16 per load
-      {
-        const int o = tid >> 2, j = (tid & 3) * 8;
-        float bv[8] = {};
-        if (o0 + o < cout && c0 + j < cin) {
-          const uint4 u = *reinterpret_cast<const uint4*>(wt + static_cast<long long>(o0 + o) * K + tap * cin + c0 + j);
-          const __nv_bfloat16* hv = reinterpret_cast<const __nv_bfloat16*>(&u);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) bv[i] = __bfloat162float(hv[i]);
-        }
-#pragma unroll
-        for (int i = 0; i < 8; ++i) Bs[j + i][o] = bv[i];
-      }
-      __syncthreads();
-#pragma unroll 8
-      for (int k = 0; k < BK; ++k) {
-        const float4 a = *reinterpret_cast<const float4*>(&As[k][ty * 4]);
-        const float4 b = *reinterpret_cast<const float4*>(&Bs[k][tx * 4]);
-        const float av[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-          for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bw[j], acc[i][j]);
-      }
-    }
-  }
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const long long p = p0 + ty * 4 + i;
-    if (p >= M) continue;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int o = o0 + tx * 4 + j;
-      if (o >= cout) continue;
-      const float v = acc[i][j] + (bias ? bias[o] : 0.f);
-      float* d = out + p * cout + o;
-      *d = accumulate ? *d + v : v;
-    }
-  }
-}
 
 // ------------------------------------------------------------------ tcgen05 implicit GEMM
 // out[p, o] (+)= bias[o] + sum_{tap, c} in[p + tap offset, c] * w[o, tap, c] with the input given
