@@ -179,7 +179,11 @@ int anima_linear(anima_ctx* ctx, const anima_qact* x, const anima_weight* W, con
 
 /* runMatmul for "bf16"/"f32" weights (ops.js:14-33, gemm.js:81-127): C = epi(alpha A B^T),
  * A fp32 [M, lda], B bf16/f32 [N, ldb]; epilogue (+bias[n]) act, then store or C += gate*y.
- * Used for x_embedder, final layer, time conditioning and the LoRA down/up products. */
+ * Used for x_embedder, final layer, time conditioning and the LoRA down/up products. bf16 weights
+ * with alpha 1, no activation and no gate, M >= 256, K and lda multiples of 8, ldc == N and 16-byte
+ * aligned A, B and C run on the tensor cores with A split into two bf16 planes (as anima_conv3x3,
+ * sharing its buffer; inside stream capture only when that buffer is already large enough); the
+ * rest, and all fp32 weights, on a CUDA-core kernel with fp32 products. */
 int anima_matmul(anima_ctx* ctx, int M, int N, int K, float alpha, const float* A, int lda, const anima_weight* B,
                  int act, float* C, int ldc, int accumulate, const float* gate, int gate_off);
 
@@ -247,7 +251,10 @@ int anima_zero(anima_ctx* ctx, void* p, size_t bytes);
 /* ops.conv3x3 / conv3x3Into (ops.js:97-109, the conv3 tiles of gemm.js): NHWC 3x3 convolution,
  * pad 1, of x fp32 [h * w, cin] with W bf16 OHWI [N, 9 cin] (+ W.bias); with up != 0 the input is
  * first upsampled 2x (nearest, the Resample of the Wan decoder). out fp32 [H * Wd, N] (H, Wd the
- * output size) = the result, or += it when accumulate != 0 (a residual). cin a multiple of 8. */
+ * output size) = the result, or += it when accumulate != 0 (a residual). cin a multiple of 8.
+ * Runs on the tensor cores with x split into two bf16 planes (hi + lo, about 16 significant bits;
+ * fp32 accumulation), held in a buffer the context allocates on first use and grows, outside
+ * stream capture only, to 4 bytes per input element (after the upsample). */
 int anima_conv3x3(anima_ctx* ctx, const float* x, int h, int w, int cin, const anima_weight* W, int up, float* out,
                   int accumulate);
 /* ops.channelNorm (ops.js:120-126, the Wan decoder's RMS_norm): y = x / max(||x||_2, 1e-12) *
