@@ -1,6 +1,8 @@
-// Non-causal multi-head attention on tcgen05 (kind::f16), head_dim 128: the DiT's self-attention
-// (Lq = Lk = 4096 at 1024^2) and cross-attention against cached text keys (Lk = 256..512). The
-// reference's counterpart is the fp32 WGSL flash kernel of app/gpu/kernels.js:147-299.
+// Multi-head attention on tcgen05 (kind::f16), head_dim 128: the DiT's self-attention (Lq = Lk =
+// 4096 at 1024^2), cross-attention against cached text keys (Lk = 256..512), and the Qwen3 text
+// encoder's causal attention with 16 q heads over 8 k/v heads (k/v head = h / group; a causal unit
+// stops at the key block of its last query and masks each row's later keys). The reference's
+// counterpart is the fp32 WGSL flash kernel of app/gpu/kernels.js:147-299.
 //
 // A unit = one (batch, head) and two 128-query tiles A and B. A CTA runs one unit; with more than
 // one wave of units, every grid-th unit (one CTA per SM); or, under stream-K (below), an equal
@@ -60,6 +62,8 @@ struct Params {
   // stream-K: the units' key blocks split evenly over the CTAs (no key mask; every unit has ublk)
   int stream_k, units, ublk;
   int persist;       // whole units, CTA c taking units c, c + grid, ... (grid = SM count)
+  int group;         // q heads per k/v head (k/v head = h / group)
+  int causal;        // key j visible to query i only when j <= i
   float* ws;         // [units][PART_FLOATS] partial softmax states of split units
   unsigned* flags;   // [units] tail part written (cleared by the head part)
 };
@@ -159,7 +163,9 @@ __device__ __forceinline__ int build_segments(const Params& p, int4* out) {
     for (int unit = blockIdx.x; unit < p.units && n < MAX_SEGS; unit += step) {
       const int b = unit / p.q_pairs / p.heads;
       const int kv_len = p.key_len ? min(p.Lk, p.key_len[p.kv_bcast ? 0 : b]) : p.Lk;
-      out[n++] = make_int4(unit, 0, kv_len > 0 ? (kv_len + TILE - 1) / TILE : 0, kWhole);
+      int nblk = kv_len > 0 ? (kv_len + TILE - 1) / TILE : 0;
+      if (p.causal) nblk = min(nblk, 2 * (unit % p.q_pairs) + 2);  // keys up to the pair's last query
+      out[n++] = make_int4(unit, 0, nblk, kWhole);
     }
     return n;
   }
@@ -260,7 +266,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int nb = sg.z - sg.y;
         if (nb <= 0) continue;
         const int q0 = qp * 2 * TILE;
-        const int qc = p.q_col + h * HD, kc = p.k_col + h * HD, vc = p.v_col + h * HD;
+        const int qc = p.q_col + h * HD, kc = p.k_col + (h / p.group) * HD, vc = p.v_col + (h / p.group) * HD;
         if (qn > 0 && !mbar_wait(q_empty, (qn - 1) & 1, abort_flag, kErrTimeoutEmpty)) break;
         mbar_arrive_expect_tx(q_full, 2 * TILE_BYTES);
         tma_load_3d(smem + OFF_Q, &tm_q, q_full, qc, q0, b);
@@ -409,6 +415,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       // keys past kv_len get probability 0; only the last block of a unit can hold such keys
       int kv_len = p.Lk;
       if (p.key_len) kv_len = min(kv_len, p.key_len[p.kv_bcast ? 0 : segs[si].x / p.q_pairs / p.heads]);
+      // causal: this thread's row sees keys up to its own index
+      if (p.causal) kv_len = min(kv_len, (segs[si].x % p.q_pairs) * 2 * TILE + x * TILE + row + 1);
       // where this warp's output rows go (read again from shared memory after the key loop)
       auto out_base = [&](int& qrow) {
         const int unit = segs[si].x;
@@ -654,7 +662,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 
 // Stream-K pays when whole units leave the last wave of CTAs far from full. Legal without a key
-// mask (every unit has the same key blocks) and with at least one unit per SM (a unit is then cut
+// mask or causality (every unit has the same key blocks) and with at least one unit per SM (a unit is then cut
 // into two parts at most); chosen (mode -1) when the last wave would leave more than 5% of the
 // SMs idle and units are long enough (>= 16 key blocks) to hide the cost of a cut: each segment
 // reloads Q and refills the pipeline, and a cut unit writes and reads back a 130 KB partial.
@@ -663,7 +671,8 @@ bool use_stream_k(const anima_ctx* ctx, const anima_attention_args* a, long long
   const int mode = ctx->attn_split;
   const int sms = ctx->num_sms;
   // a CTA then runs at most units / sms + 3 segments
-  if (mode == 0 || a->key_len || units < sms || units > static_cast<long long>(MAX_SEGS - 4) * sms || ublk < 1)
+  if (mode == 0 || a->key_len || a->causal || units < sms || units > static_cast<long long>(MAX_SEGS - 4) * sms ||
+      ublk < 1)
     return false;
   if (mode == 1) return true;
   const long long waves = (units + sms - 1) / sms;
@@ -947,15 +956,15 @@ int attention_launch(anima_ctx* ctx, const anima_attention_args* a, bool static_
   ANIMA_REQUIRE(a->q && a->k && a->v && a->out, "anima_attention: NULL data pointer");
   const int group = a->group > 1 ? a->group : 1;
   if (attention_planes_ok(a)) return attention_planes(ctx, a);  // the VAE's wide single head
-  if (group > 1 || a->causal || a->head_dim != attn::HD || a->dtype == ANIMA_F32) {
+  if (a->head_dim != attn::HD || a->dtype == ANIMA_F32 || a->heads % group != 0) {
     ANIMA_REQUIRE(a->dtype == ANIMA_F32 || a->dtype == ANIMA_BF16 || a->dtype == ANIMA_F16,
                   "anima_attention: q/k/v dtype %d", a->dtype);
     return text_attention(ctx, a, group);  // no workspace either way
   }
   ANIMA_REQUIRE(a->dtype == ANIMA_BF16 || a->dtype == ANIMA_F16, "anima_attention: q/k/v dtype must be bf16 or f16");
   const long long cols_q = a->q_off + static_cast<long long>(a->heads) * a->head_dim;
-  const long long cols_k = a->k_off + static_cast<long long>(a->heads) * a->head_dim;
-  const long long cols_v = a->v_off + static_cast<long long>(a->heads) * a->head_dim;
+  const long long cols_k = a->k_off + static_cast<long long>(a->heads / group) * a->head_dim;
+  const long long cols_v = a->v_off + static_cast<long long>(a->heads / group) * a->head_dim;
   ANIMA_REQUIRE(a->ldq >= cols_q && a->ldk >= cols_k && a->ldv >= cols_v, "anima_attention: row stride too small");
   ANIMA_REQUIRE(a->q_off % 8 == 0 && a->k_off % 8 == 0 && a->v_off % 8 == 0 && a->ldq % 8 == 0 && a->ldk % 8 == 0 &&
                     a->ldv % 8 == 0,
@@ -1009,6 +1018,8 @@ int attention_launch(anima_ctx* ctx, const anima_attention_args* a, bool static_
   p.out_dtype = a->out_dtype;
   p.key_len = a->key_len;
   p.kv_bcast = kv_bcast ? 1 : 0;
+  p.group = group;
+  p.causal = a->causal ? 1 : 0;
   const float scale = a->scale > 0.f ? a->scale : 1.0f / sqrtf(static_cast<float>(a->head_dim));
   p.scale_log2 = scale * 1.4426950408889634f;
 

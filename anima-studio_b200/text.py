@@ -64,9 +64,12 @@ class Qwen3:
         for ly in self.layers:
             h = ops.rmsnorm(x, ly["ln1"], D)
             hq = ops.rotate_quant(h, self.planes)               # one rotation + quantization for q, k, v
-            q = ops.rmsnorm(ops.linear(hq, ly["q"]), ly["qn"], HD)
-            k = ops.rmsnorm(ops.linear(hq, ly["k"]), ly["kn"], HD)
-            v = ops.linear(hq, ly["v"])
+            # q, k, v leave their norms / projections as fp16 for the tcgen05 attention (causal, 16 q
+            # heads over 8 k/v heads); its softmax and output stay fp32
+            f16 = torch.float16
+            q = ops.rmsnorm(ops.linear(hq, ly["q"]), ly["qn"], HD, out_dtype=f16)
+            k = ops.rmsnorm(ops.linear(hq, ly["k"]), ly["kn"], HD, out_dtype=f16)
+            v = ops.linear(hq, ly["v"], out_dtype=f16)
             ops.rope(q, cs, L, H, HD)
             ops.rope(k, cs, L, KH, HD)
             a = ops.attention(q, k, v, Lq=L, Lk=L, H=H, D=HD, group=H // KH, causal=True, out_dtype=torch.float32)

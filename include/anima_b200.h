@@ -219,10 +219,12 @@ int anima_qk_norm_rope(anima_ctx* ctx, void* qkv, int dtype, int L, int H, int D
 int anima_rope(anima_ctx* ctx, void* x, int dtype, int L, int H, int D, int row_stride, int col_off,
                const float* rope, int rope_rows);
 /* ops.attention (ops.js:166-208, kernels.js:147-299): multi-head attention with fp32 softmax.
- * Non-causal, head_dim 128, one k/v head per q head (the DiT's attentions): the tcgen05 flash
- * kernel. Causal, grouped k/v heads or head_dim 64 or 384 (the Qwen3 text encoder, the LLM adapter
- * and the VAE's single-head attention, once per prompt or image): a CUDA-core kernel over 32-key
- * tiles in shared memory, which also takes fp32 q/k/v.
+ * head_dim 128 with bf16/fp16 q/k/v (the DiT's attentions; the Qwen3 text encoder's, causal with
+ * grouped k/v heads): the tcgen05 flash kernel. fp32 q/k/v with one wide head (head_dim a multiple
+ * of 64, at least 2^20 scores: the VAE's d = 384 attention): tensor-core GEMMs around a row
+ * softmax, with the fp32 scores materialised in a context buffer (Lq Lk 8 bytes plus the operand
+ * planes, grown outside stream capture only). Everything else (head_dim 64, fp32 q/k/v, small
+ * problems): a CUDA-core kernel over 32-key tiles in shared memory.
  * The stream-K schedule (see anima_ctx_set_attention_split) launches one CTA per SM and lets a CTA
  * wait, bounded at 2 s, for a partial result written by a lower-numbered CTA; it therefore needs
  * all of the device's SMs to be available to this kernel at once. Where other work can hold SMs
