@@ -60,12 +60,12 @@ int set_max_dynamic_smem(const void* fn, int bytes);
 bool attention_planes_ok(const anima_attention_args* a);
 int attention_planes(anima_ctx* ctx, const anima_attention_args* a);
 
-// C (+)= A B^T + bias for fp32 A [M, K] (rows lda apart) and bf16 B [N, K] on the tensor cores (A as
-// two bf16 planes), C [M, N] dense (vae.cu). Returns ANIMA_ERR_UNSUPPORTED, with nothing launched,
+// C (+)= A B^T + bias for fp32 A [M, K] (rows lda apart) and bf16 (f16: fp16) B [N, K] on the tensor
+// cores (A as two planes of B's type), C [M, N] dense (vae.cu). Returns ANIMA_ERR_UNSUPPORTED, with nothing launched,
 // when the shape or alignment does not suit it or its plane buffer would have to grow inside
 // stream capture; the caller then takes the CUDA-core GEMM.
 int matmul_planes(anima_ctx* ctx, int M, int N, int K, const float* A, int lda, const void* B, const float* bias,
-                  float* C, int ldc, int accumulate);
+                  float* C, int ldc, int accumulate, bool f16);
 
 // Decode 4-bit weights to their int8 grid values (rowops.cu; the arithmetic of anima_unpack_w4):
 // out int8 [N, K] from packed nibbles [N, K/2] and fp8 group scales [N, K/16].

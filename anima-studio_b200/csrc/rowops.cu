@@ -1342,16 +1342,19 @@ int anima_matmul(anima_ctx* ctx, int M, int N, int K, float alpha, const float* 
   ANIMA_REQUIRE(ctx && A && B && B->data && C, "anima_matmul: NULL argument");
   ANIMA_ON_DEVICE(ctx);
   ANIMA_REQUIRE(M > 0 && N > 0 && K > 0 && lda >= K && ldc >= N, "anima_matmul: bad shape");
-  ANIMA_REQUIRE(B->kind == ANIMA_W_BF16 || B->kind == ANIMA_W_F32, "anima_matmul: weight kind %d (bf16 or f32 only)",
-                B->kind);
-  ProfScope prof(ctx, B->kind == ANIMA_W_BF16 ? "gemm.bf16" : "gemm.f32", 2.0 * M * N * K, 0);
-  // bf16 weights, no scale, activation or gate: the tensor-core GEMM on two bf16 planes of A when
-  // the shape suits it, else the CUDA-core kernel below
-  if (B->kind == ANIMA_W_BF16 && alpha == 1.0f && act == ANIMA_ACT_NONE && !gate) {
-    const int st = matmul_planes(ctx, M, N, K, A, lda, B->data, B->bias, C, ldc, accumulate);
+  ANIMA_REQUIRE(B->kind == ANIMA_W_BF16 || B->kind == ANIMA_W_F32 || B->kind == ANIMA_W_F16,
+                "anima_matmul: weight kind %d (bf16, f32 or f16 only)", B->kind);
+  ProfScope prof(ctx, B->kind == ANIMA_W_F32 ? "gemm.f32" : "gemm.16bit", 2.0 * M * N * K, 0);
+  // 16-bit weights, no scale, activation or gate: the tensor-core GEMM on two planes of A when the
+  // shape suits it, else the CUDA-core kernel below
+  if (B->kind != ANIMA_W_F32 && alpha == 1.0f && act == ANIMA_ACT_NONE && !gate) {
+    const int st = matmul_planes(ctx, M, N, K, A, lda, B->data, B->bias, C, ldc, accumulate, B->kind == ANIMA_W_F16);
     if (st != ANIMA_ERR_UNSUPPORTED) return st;
   }
-  if (B->kind == ANIMA_W_BF16)
+  if (B->kind == ANIMA_W_F16)
+    launch_simt<__half, false>(ctx->stream, ctx->num_sms, M, N, K, alpha, A, lda, (const __half*)B->data, K, B->bias,
+                               act, C, ldc, accumulate, gate, gate_off);
+  else if (B->kind == ANIMA_W_BF16)
     launch_simt<__nv_bfloat16, false>(ctx->stream, ctx->num_sms, M, N, K, alpha, A, lda, (const __nv_bfloat16*)B->data, K,
                                       B->bias, act, C, ldc, accumulate, gate, gate_off);
   else

@@ -36,6 +36,7 @@ constexpr int SMEM = STAGES * STAGE_BYTES + 256 + 1024;
 
 struct Params {
   int H, W, cin, cout, taps;       // taps: 9 (3x3, pad 1) or 1
+  int f16;                         // operands fp16 instead of bf16
   int tile_w, tile_h, tiles_x, n_tiles, num_tiles, BN, nchunks;
   const float* bias;
   float* out;
@@ -121,7 +122,7 @@ __global__ void __launch_bounds__(THREADS, 1) conv_tc_kernel(const __grid_consta
     }
   } else if (warp == 5) {  // MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = idesc_f16(BM, p.BN, true, false);
+      const uint32_t idesc = idesc_f16(BM, p.BN, !p.f16, false);
       int stage = 0;
       uint32_t phase = 0;
       int i = 0;
@@ -219,11 +220,13 @@ __global__ void __launch_bounds__(THREADS, 1) conv_tc_kernel(const __grid_consta
   }
 }
 
-// Input planes for the tensor-core convolution: hi = bf16(x), lo = bf16(x - hi) per element, with
+// Input planes for the tensor-core convolution: hi = T(x), lo = T(x - hi) per element (T bf16, or
+// fp16 for the LoRA up-projection's small-range operands), with
 // the nearest 2x upsample applied on the way when up != 0; x rows (pixels) ldx floats apart. One
 // thread per 8 channels of a pixel.
+template <typename T>
 __global__ void split_planes_kernel(const float* __restrict__ x, int h, int w, int c, long long ldx, int up,
-                                    __nv_bfloat16* __restrict__ hi, __nv_bfloat16* __restrict__ lo, long long n8) {
+                                    T* __restrict__ hi, T* __restrict__ lo, long long n8) {
   const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= n8) return;
   const int c8 = c / 8;
@@ -237,11 +240,19 @@ __global__ void split_planes_kernel(const float* __restrict__ x, int h, int w, i
   uint32_t hw[4], lw[4];
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
-    const __nv_bfloat162 h2 = __floats2bfloat162_rn(v[2 * k], v[2 * k + 1]);
-    const float2 hf = __bfloat1622float2(h2);
-    const __nv_bfloat162 l2 = __floats2bfloat162_rn(v[2 * k] - hf.x, v[2 * k + 1] - hf.y);
-    hw[k] = *reinterpret_cast<const uint32_t*>(&h2);
-    lw[k] = *reinterpret_cast<const uint32_t*>(&l2);
+    if constexpr (std::is_same<T, __half>::value) {
+      const __half2 h2 = __floats2half2_rn(v[2 * k], v[2 * k + 1]);
+      const float2 hf = __half22float2(h2);
+      const __half2 l2 = __floats2half2_rn(v[2 * k] - hf.x, v[2 * k + 1] - hf.y);
+      hw[k] = *reinterpret_cast<const uint32_t*>(&h2);
+      lw[k] = *reinterpret_cast<const uint32_t*>(&l2);
+    } else {
+      const __nv_bfloat162 h2 = __floats2bfloat162_rn(v[2 * k], v[2 * k + 1]);
+      const float2 hf = __bfloat1622float2(h2);
+      const __nv_bfloat162 l2 = __floats2bfloat162_rn(v[2 * k] - hf.x, v[2 * k + 1] - hf.y);
+      hw[k] = *reinterpret_cast<const uint32_t*>(&h2);
+      lw[k] = *reinterpret_cast<const uint32_t*>(&l2);
+    }
   }
   reinterpret_cast<uint4*>(hi)[i] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
   reinterpret_cast<uint4*>(lo)[i] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
@@ -367,9 +378,11 @@ static int grow_ws(anima_ctx* ctx, void** buf, size_t* have, size_t want, const 
 
 // out[p, n] (+)= bias[n] + sum_{tap, c} (hi + lo)[p + tap offset, c] * w[n, tap, c] on the tensor
 // cores: planes [H, W, cin] bf16, w bf16 [N, taps * cin] K-major, out fp32 [H W, N].
-static int tc_gemm(anima_ctx* ctx, const __nv_bfloat16* hi, const __nv_bfloat16* lo, int H, int W, int cin, int taps,
-                   const void* wdata, int N, const float* bias, float* out, int accumulate) {
+static int tc_gemm(anima_ctx* ctx, const void* hi, const void* lo, int H, int W, int cin, int taps,
+                   const void* wdata, int N, const float* bias, float* out, int accumulate, bool f16 = false) {
   tc::Params p{};
+  p.f16 = f16 ? 1 : 0;
+  const CUtensorMapDataType dt = f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   p.H = H;
   p.W = W;
   p.cin = cin;
@@ -394,12 +407,12 @@ static int tc_gemm(anima_ctx* ctx, const __nv_bfloat16* hi, const __nv_bfloat16*
   const uint64_t adims[3] = {static_cast<uint64_t>(cin), static_cast<uint64_t>(W), static_cast<uint64_t>(H)};
   const uint64_t astr[2] = {static_cast<uint64_t>(cin) * 2, static_cast<uint64_t>(W) * cin * 2};
   const uint32_t abox[3] = {static_cast<uint32_t>(tc::CK), static_cast<uint32_t>(p.tile_w), static_cast<uint32_t>(p.tile_h)};
-  int st = make_tmap(&tm_hi, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, hi, adims, astr, abox, CU_TENSOR_MAP_SWIZZLE_128B);
-  if (!st) st = make_tmap(&tm_lo, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, lo, adims, astr, abox, CU_TENSOR_MAP_SWIZZLE_128B);
+  int st = make_tmap(&tm_hi, dt, 3, hi, adims, astr, abox, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!st) st = make_tmap(&tm_lo, dt, 3, lo, adims, astr, abox, CU_TENSOR_MAP_SWIZZLE_128B);
   const uint64_t wdims[2] = {static_cast<uint64_t>(taps) * cin, static_cast<uint64_t>(N)};
   const uint64_t wstr[1] = {static_cast<uint64_t>(taps) * cin * 2};
   const uint32_t wbox[2] = {static_cast<uint32_t>(tc::CK), static_cast<uint32_t>(p.BN)};
-  if (!st) st = make_tmap(&tm_w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, wdata, wdims, wstr, wbox, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!st) st = make_tmap(&tm_w, dt, 2, wdata, wdims, wstr, wbox, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st) return st;
   st = set_max_dynamic_smem(reinterpret_cast<const void*>(&tc::conv_tc_kernel<false>), tc::SMEM);
   if (st) return st;
@@ -408,10 +421,11 @@ static int tc_gemm(anima_ctx* ctx, const __nv_bfloat16* hi, const __nv_bfloat16*
   return check_launch("conv_tc_kernel");
 }
 
-static int split_planes(anima_ctx* ctx, const float* x, int h, int w, int c, long long ldx, int up,
-                        __nv_bfloat16* hi, __nv_bfloat16* lo) {
+template <typename T>
+static int split_planes(anima_ctx* ctx, const float* x, int h, int w, int c, long long ldx, int up, T* hi, T* lo) {
   const long long n8 = static_cast<long long>(up ? 4 : 1) * h * w * (c / 8);
-  tc::split_planes_kernel<<<static_cast<unsigned>((n8 + 255) / 256), 256, 0, ctx->stream>>>(x, h, w, c, ldx, up, hi, lo, n8);
+  tc::split_planes_kernel<T><<<static_cast<unsigned>((n8 + 255) / 256), 256, 0, ctx->stream>>>(x, h, w, c, ldx, up, hi,
+                                                                                            lo, n8);
   return check_launch("split_planes_kernel");
 }
 
@@ -424,7 +438,7 @@ static int split_planes(anima_ctx* ctx, const float* x, int h, int w, int c, lon
 // no mask, batch 1, d a multiple of 64, and at least 2^20 scores (smaller ones stay on the
 // CUDA-core kernel, as the text models' do).
 int matmul_planes(anima_ctx* ctx, int M, int N, int K, const float* A, int lda, const void* B, const float* bias,
-                  float* C, int ldc, int accumulate) {
+                  float* C, int ldc, int accumulate, bool f16) {
   if (M < 256 || K % 8 != 0 || lda % 8 != 0 || ldc != N || (reinterpret_cast<uintptr_t>(A) & 15) != 0 ||
       (reinterpret_cast<uintptr_t>(B) & 15) != 0 || (reinterpret_cast<uintptr_t>(C) & 15) != 0)
     return ANIMA_ERR_UNSUPPORTED;
@@ -436,11 +450,16 @@ int matmul_planes(anima_ctx* ctx, int M, int N, int K, const float* A, int lda, 
   }
   int st = vae::grow_ws(ctx, &ctx->vae_ws, &ctx->vae_ws_bytes, 2 * plane * sizeof(__nv_bfloat16), "anima_matmul");
   if (st) return st;
-  auto* hi = static_cast<__nv_bfloat16*>(ctx->vae_ws);
-  auto* lo = hi + plane;
-  st = vae::split_planes(ctx, A, 1, M, K, lda, 0, hi, lo);
+  if (f16) {
+    auto* hi = static_cast<__half*>(ctx->vae_ws);
+    st = vae::split_planes(ctx, A, 1, M, K, lda, 0, hi, hi + plane);
+  } else {
+    auto* hi = static_cast<__nv_bfloat16*>(ctx->vae_ws);
+    st = vae::split_planes(ctx, A, 1, M, K, lda, 0, hi, hi + plane);
+  }
   if (st) return st;
-  return vae::tc_gemm(ctx, hi, lo, 1, M, K, 1, B, N, bias, C, accumulate);
+  auto* hi = static_cast<uint16_t*>(ctx->vae_ws);
+  return vae::tc_gemm(ctx, hi, hi + plane, 1, M, K, 1, B, N, bias, C, accumulate, f16);
 }
 
 bool attention_planes_ok(const anima_attention_args* a) {

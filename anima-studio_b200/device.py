@@ -19,7 +19,7 @@ LIB_PATH = os.environ.get("ANIMA_LIB", os.path.join(HERE, "libanima_b200.so"))
 
 ANIMA_F32, ANIMA_BF16, ANIMA_F16, ANIMA_I8, ANIMA_U8 = range(5)
 ACT = {None: 0, "none": 0, "gelu": 1, "silu": 2}
-W_I8, W_W4, W_BF16, W_F32 = range(4)
+W_I8, W_W4, W_BF16, W_F32, W_F16 = range(5)
 OUT_STORE, OUT_RESID, OUT_QKV_NORM_ROPE, OUT_HEAD_NORM = range(4)
 
 DTYPE_CODE = {torch.float32: ANIMA_F32, torch.bfloat16: ANIMA_BF16, torch.float16: ANIMA_F16,

@@ -163,6 +163,7 @@ def attach_loras(registries, active):
                 W._lora_cat = None
                 W._lora_bt = None
                 W._lora_down = None
+                W._lora_up = None
 
 
 def _cat_A(W):
@@ -245,6 +246,45 @@ def _down_linear(W):
         lin = Linear("i8", n2, K, q.contiguous(), sc.contiguous(), name=W.name + ".lora_down")
         W._lora_down = lin
     return lin
+
+
+# How ops.linear applies the side paths: "delta" (default) computes the [M, N] update on the tensor
+# cores (the down GEMM below, then T B^T as a two-plane fp16 GEMM) and hands it to the int8 GEMM's
+# epilogue as its ADD input, the reference's own structure (ops.js:70-87); "fused" multiplies
+# T B^T inside the int8 GEMM's epilogue on CUDA cores (anima_linear_opts.lora_*).
+PATH = "delta"
+
+
+def _up_linear(W):
+    """scale_e * B_e of every entry as one fp16 [N, n2] weight over the down GEMM's n2 output
+    columns: the entry's rank columns in both the hi half [0, R) and the lo half [R, 2R) of T (whose
+    sum is x_r A^T), zero elsewhere (cached per attach)."""
+    from .weights import Linear
+
+    lin = getattr(W, "_lora_up", None)
+    if lin is None:
+        down = _down_linear(W)
+        R = sum(e["r"] for e in W.lora)
+        b2 = torch.zeros(W.N, down.N, dtype=torch.float32, device=W.lora[0]["B"].device)
+        r0 = 0
+        for e in W.lora:
+            blk = e["B"].float() * e["scale"]
+            b2[e["off"]:e["off"] + e["n"], r0:r0 + e["r"]] = blk
+            b2[e["off"]:e["off"] + e["n"], R + r0:R + r0 + e["r"]] = blk
+            r0 += e["r"]
+        lin = Linear("f16", W.N, down.N, b2.half().contiguous(), None, name=W.name + ".lora_up")
+        W._lora_up = lin
+    return lin
+
+
+def lora_delta_tc(x, W) -> torch.Tensor:
+    """[M, N] fp32 low-rank update on the tensor cores: T = x_r A^T (hi and lo halves) by the int8
+    GEMM, then T B2^T by the two-plane fp16 GEMM of anima_matmul (T to ~22 bits, scale * B in fp16:
+    ~2^-11 of the update, as the fused epilogue)."""
+    from .ops import linear, matmul
+
+    T = linear(x, _down_linear(W))
+    return matmul(T, _up_linear(W))
 
 
 def lora_epilogue(x, W, opts) -> list:

@@ -193,7 +193,7 @@ def linear(x, W, *, out: torch.Tensor | None = None, resid: bool = False, gate: 
           "item_rows"}: the k|v columns go to those buffers over NVLink instead of to `out`
           (sharding.KVExchange; anima_linear_opts.peer_*).
     """
-    from .lora import lora_delta, lora_epilogue
+    from . import lora as lora_mod
 
     if W.kind in ("bf16", "f32"):
         return matmul(x, W, act=act, out=out, resid=resid, gate=gate, g_off=g_off)
@@ -203,9 +203,10 @@ def linear(x, W, *, out: torch.Tensor | None = None, resid: bool = False, gate: 
     o = dev.LinearOpts()
     keep = None
     if W.lora:
-        keep = lora_epilogue(x, W, o)   # fused into the GEMM epilogue
-        if keep is None:                 # entries the fused form does not take: an added delta
-            delta = lora_delta(x, W)
+        if lora_mod.PATH == "fused":
+            keep = lora_mod.lora_epilogue(x, W, o)   # T B^T inside the GEMM epilogue (None: entries it
+        if keep is None:                             # cannot take, which get an added delta)
+            delta = lora_mod.lora_delta_tc(x, W) if lora_mod.PATH == "delta" else lora_mod.lora_delta(x, W)
             add = delta if add is None else add + delta
     if out is None:
         if resid:

@@ -42,7 +42,7 @@ class Linear:
 
     def c(self) -> dev.Weight:
         w = dev.Weight()
-        w.kind = {"i8": dev.W_I8, "w4": dev.W_W4, "bf16": dev.W_BF16, "f32": dev.W_F32}[self.kind]
+        w.kind = {"i8": dev.W_I8, "w4": dev.W_W4, "bf16": dev.W_BF16, "f32": dev.W_F32, "f16": dev.W_F16}[self.kind]
         w.N, w.K = self.N, self.K
         w.data = self.data.data_ptr()
         w.scale = self.scale.data_ptr() if self.scale is not None else 0

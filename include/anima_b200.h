@@ -39,7 +39,7 @@ typedef enum { ANIMA_F32 = 0, ANIMA_BF16 = 1, ANIMA_F16 = 2, ANIMA_I8 = 3, ANIMA
 typedef enum { ANIMA_ACT_NONE = 0, ANIMA_ACT_GELU = 1, ANIMA_ACT_SILU = 2 } anima_act;
 
 /* Weight kinds of app/weights.js:118-146 ({kind: "i8" | "w4" | "bf16"}) plus fp32 (LoRA A/B). */
-typedef enum { ANIMA_W_I8 = 0, ANIMA_W_W4 = 1, ANIMA_W_BF16 = 2, ANIMA_W_F32 = 3 } anima_weight_kind;
+typedef enum { ANIMA_W_I8 = 0, ANIMA_W_W4 = 1, ANIMA_W_BF16 = 2, ANIMA_W_F32 = 3, ANIMA_W_F16 = 4 } anima_weight_kind;
 
 /* Rotated, per-token quantized activation rows (the "xr" input of ops.linear, ops.js:48-54):
  *   x[m, k] ~= scale[m] * (hi[m, k] + lo[m, k] / 254)
@@ -55,7 +55,8 @@ typedef struct {
  *   I8  : data = int8 codes [N, K], scale = weight_scale [N]
  *   W4  : data = packed nibbles [N, K/2] (low nibble = even k), s_rel = fp8-e4m3 [N, K/16],
  *         codebook = [16], scale = weight_s_channel [N]
- *   BF16: data = bf16 [N, K];  F32: data = fp32 [N, K]
+ *   BF16: data = bf16 [N, K];  F32: data = fp32 [N, K];  F16: data = fp16 [N, K] (anima_matmul
+ *         only: the LoRA up-projection)
  * ConvRot layers (I8, W4) take rotated inputs, as in the reference (ops.js:35). */
 typedef struct {
   int kind, N, K;

@@ -328,14 +328,17 @@ def _lora_ref(qa, entries, N):
                                        ([(128, 1024, 8, 1.5)], "resid"),
                                        ([(0, 2048, 32, 1.0), (2048, 2048, 32, 1.0)], "qkv"),
                                        ([(0, 6144, 6, 1.0)], "store")])
-def test_linear_lora_epilogue(ops, spec, mode):
-    """The fused side path multiplies fp16 copies of x_r A^T and scale * B^T (fp32 sums), so the
-    output carries ~2^-11 of the LoRA delta (a few % of y here) on top of the base GEMM's fp32
-    rounding: 3e-5 of the output where the base path alone is held to 2e-6. The [M, N] delta
-    fallback (rank 6) stays fp32."""
+@pytest.mark.parametrize("path", ["delta", "fused"])
+def test_linear_lora_epilogue(ops, spec, mode, path, monkeypatch):
+    """Both side-path forms carry fp16 copies of scale * B^T and fp32 sums (the fused epilogue also
+    an fp16 copy of x_r A^T; the tensor-core delta two fp16 planes of it), so the output carries
+    ~2^-11 of the LoRA delta (a few % of y here) on top of the base GEMM's fp32 rounding: 3e-5 of
+    the output where the base path alone is held to 2e-6. With the fused form, entries it cannot
+    take (rank 6) go through the fp32 CUDA-core delta."""
+    monkeypatch.setattr(pkg("lora"), "PATH", path)
     M, K = 260, 2048
     fused = all(r % 4 == 0 for (_, _, r, _) in spec)
-    tol = 3e-5 if fused else 2e-6
+    tol = 3e-5 if (fused or path == "delta") else 2e-6
     N = 6144 if mode in ("store", "qkv") else 2048
     lin, wq, ws = make_linear(N, K, 8)
     lin.lora = [{k: v for k, v in e.items() if not k.endswith("_np")} for e in _lora_entries(K, spec, 50)]
