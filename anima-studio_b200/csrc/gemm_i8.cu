@@ -95,7 +95,10 @@ struct Cfg {
   // LoRA: one [LORA_R, BN] fp16 slice of scale * B^T per epilogue warpgroup (fp16 keeps three
   // pipeline stages within the 227 KB a CTA may hold)
   static constexpr int LORA_BYTES = LORA ? 2 * LORA_R * BN * 2 : 0;
-  static constexpr int STAGES = ((LORA ? 224 : 216) * 1024 - STAGING_BYTES - LORA_BYTES) / STAGE_BYTES;
+  // the tile's per-column vectors (weight scale, bias, gate) per epilogue warpgroup, loaded before
+  // the accumulator wait (the LoRA build reads them from global memory: no room for a third stage)
+  static constexpr int VEC_BYTES = LORA ? 0 : 2 * 3 * BN * 4;
+  static constexpr int STAGES = ((LORA ? 224 : 216) * 1024 - STAGING_BYTES - LORA_BYTES - VEC_BYTES) / STAGE_BYTES;
   static constexpr int ACC_COLS = NPLANES * BN;
   // one accumulator buffer per epilogue warpgroup when two fit in TMEM, else one (the second
   // epilogue warpgroup then idles and the epilogue of a tile delays the next tile's MMAs)
@@ -103,8 +106,9 @@ struct Cfg {
   static_assert(ACC_BUFS * ACC_COLS <= 512, "accumulators exceed TMEM");
   static constexpr int TMEM_COLS = 512;
   static constexpr int BAR_BYTES = 256;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + STAGING_BYTES + LORA_BYTES + BAR_BYTES + 1024;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + STAGING_BYTES + LORA_BYTES + VEC_BYTES + BAR_BYTES + 1024;
   static_assert(STAGES >= 2, "need at least two pipeline stages");
+  static_assert(SMEM_BYTES <= 232448, "shared memory exceeds the 227 KB a CTA may hold");
 };
 
 // ------------------------------------------------------------------ epilogue helpers
@@ -129,6 +133,30 @@ __device__ __forceinline__ void ldv(const float* p, float (&v)[CH]) {
   }
 }
 __device__ __forceinline__ void ld32(const float* p, float (&v)[32]) { ldv<32>(p, v); }
+
+// CH consecutive fp32 values from shared or global memory (generic 16-byte loads).
+template <int CH>
+__device__ __forceinline__ void ldg_any(const float* p, float (&v)[CH]) {
+  const float4* q = reinterpret_cast<const float4*>(p);
+#pragma unroll
+  for (int j = 0; j < CH / 4; ++j) {
+    const float4 t = q[j];
+    v[4 * j] = t.x;
+    v[4 * j + 1] = t.y;
+    v[4 * j + 2] = t.z;
+    v[4 * j + 3] = t.w;
+  }
+}
+
+// A tile's row and column constants for the epilogue: this row's activation scale, and the
+// weight scale, bias and gate of the tile's columns (indexed by the column within the tile; in
+// shared memory, or in global memory for the LoRA build).
+struct EpiVec {
+  float as;
+  const float* ws;
+  const float* bias;
+  const float* gate;  // residual mode: the gate; per-head norm modes: the norm weight of the column's head
+};
 
 template <int CH>
 __device__ __forceinline__ void tmem_ldc(uint32_t taddr, uint32_t (&r)[CH]) {
@@ -188,13 +216,14 @@ __device__ __forceinline__ void lora_cols(const LoraTile& lt, int col, float (&v
 }
 
 // After the loads landed: y = a_scale[m] w_scale[n] (hi + lo / 254) (+ bias) (+ add) (+ LoRA) (act).
+// av: this piece's ADD values when already loaded (else nullptr: loaded here).
 template <int BN, int NPLANES, int CH, bool LORA>
-__device__ __forceinline__ void finish_cols(const Params& p, int m, int n, bool row_ok, const uint32_t (&rh)[CH],
-                                            const uint32_t (&rl)[CH], float (&v)[CH], bool apply_act,
-                                            const LoraTile& lt, int col) {
-  const float as = row_ok ? __ldg(p.a_scale + m) : 0.0f;
+__device__ __forceinline__ void finish_cols(const Params& p, const EpiVec& ev, int m, int n, bool row_ok,
+                                            const uint32_t (&rh)[CH], const uint32_t (&rl)[CH], float (&v)[CH],
+                                            bool apply_act, const LoraTile& lt, int col, const float* av = nullptr) {
+  const float as = ev.as;
   float ws[CH];
-  ldv<CH>(p.w_scale + n, ws);
+  ldg_any<CH>(ev.ws + col, ws);
   if constexpr (NPLANES == 2) {
     const float as_lo = as * (1.0f / 254.0f);
 #pragma unroll
@@ -207,15 +236,20 @@ __device__ __forceinline__ void finish_cols(const Params& p, int m, int n, bool 
   }
   if (p.bias) {
     float bv[CH];
-    ldv<CH>(p.bias + n, bv);
+    ldg_any<CH>(ev.bias + col, bv);
 #pragma unroll
     for (int j = 0; j < CH; ++j) v[j] += bv[j];
   }
   if (p.add && row_ok) {
-    float av[CH];
-    ldv<CH>(p.add + static_cast<size_t>(m) * p.ld_add + n, av);
+    if (av) {
 #pragma unroll
-    for (int j = 0; j < CH; ++j) v[j] += av[j];
+      for (int j = 0; j < CH; ++j) v[j] += av[j];
+    } else {
+      float ad[CH];
+      ldv<CH>(p.add + static_cast<size_t>(m) * p.ld_add + n, ad);
+#pragma unroll
+      for (int j = 0; j < CH; ++j) v[j] += ad[j];
+    }
   }
   if constexpr (LORA) {
     if (lt.bt_s && row_ok) lora_cols<BN, CH>(lt, col, v);
@@ -235,13 +269,13 @@ __device__ __forceinline__ void finish_cols(const Params& p, int m, int n, bool 
 
 // Load CH accumulator columns and finish them (no overlap; used by the per-head epilogues).
 template <int BN, int NPLANES, bool LORA, int CH = 16>
-__device__ __forceinline__ void load_cols(const Params& p, uint32_t taddr, int col, int m, int n, bool row_ok,
-                                          float (&v)[CH], bool apply_act, const LoraTile& lt) {
+__device__ __forceinline__ void load_cols(const Params& p, const EpiVec& ev, uint32_t taddr, int col, int m, int n,
+                                          bool row_ok, float (&v)[CH], bool apply_act, const LoraTile& lt) {
   uint32_t rh[CH], rl[CH];
   issue_cols<BN, NPLANES, CH>(taddr, col, rh, rl);
   tmem_ld_wait(rh);
   if constexpr (NPLANES == 2) tmem_ld_wait(rl);
-  finish_cols<BN, NPLANES, CH, LORA>(p, m, n, row_ok, rh, rl, v, apply_act, lt, col);
+  finish_cols<BN, NPLANES, CH, LORA>(p, ev, m, n, row_ok, rh, rl, v, apply_act, lt, col);
 }
 
 // ------------------------------------------------------------------ staged stores
@@ -323,9 +357,9 @@ __device__ __forceinline__ void stage_acquire() {
 // One tile's epilogue for this warp's 32 rows (m = row of this lane) over BN columns from n0.
 // stage: this warp's two staging buffers; y0: first row of the warp's quadrant.
 template <int BN, int NPLANES, bool LORA>
-__device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap* tm_out, const PeerMaps* pm,
-                                              uint8_t* stage, uint32_t taddr, int m, int y0, int n0,
-                                              const LoraTile& lt) {
+__device__ __forceinline__ void epilogue_tile(const Params& p, const EpiVec& ev, const CUtensorMap* tm_out,
+                                              const PeerMaps* pm, uint8_t* stage, uint32_t taddr, int m, int y0,
+                                              int n0, const LoraTile& lt) {
   const bool row_ok = m < p.M;
   const int lane = threadIdx.x & 31;
   const int esz = p.out_dtype == ANIMA_F32 ? 4 : 2;
@@ -333,29 +367,36 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap
   const int ppc = chc / 16;       // 16-column pieces per chunk
   constexpr int CH = 16;
   if (p.out_mode == ANIMA_OUT_STORE || p.out_mode == ANIMA_OUT_RESID) {
-    // software pipeline over 16-column pieces: the TMEM loads of piece c+1 are in flight while
-    // piece c is finished and staged
+    // software pipeline over 16-column pieces: the TMEM loads (and this row's ADD values) of piece
+    // c+1 are in flight while piece c is finished and staged
     const bool resid = p.out_mode == ANIMA_OUT_RESID;
+    const bool add = !LORA && p.add && row_ok;  // (the LoRA build has no registers to spare for it)
+    const float* arow = add ? p.add + static_cast<size_t>(m) * p.ld_add + n0 : nullptr;
     constexpr int PIPE = 2;
     uint32_t rh[PIPE][CH], rl[PIPE][CH];
+    float av[PIPE][CH];
     issue_cols<BN, NPLANES, CH>(taddr, 0, rh[0], rl[0]);
+    if (add) ldv<CH>(arow, av[0]);
     tmem_ld_wait(rh[0]);
     if constexpr (NPLANES == 2) tmem_ld_wait(rl[0]);
 #pragma unroll
     for (int c = 0; c < BN / CH; ++c) {
       const int cur = PIPE == 2 ? (c & 1) : 0;
-      if (PIPE == 2 && c + 1 < BN / CH)
+      if (PIPE == 2 && c + 1 < BN / CH) {
         issue_cols<BN, NPLANES, CH>(taddr, CH * (c + 1), rh[(cur + 1) % PIPE], rl[(cur + 1) % PIPE]);
+        if (add) ldv<CH>(arow + CH * (c + 1), av[(cur + 1) % PIPE]);
+      }
       const int col = CH * c;
       const int chunk = col / chc, q = (col % chc) / CH;
       uint8_t* buf = stage + (chunk & 1) * STAGE_BUF;
       if (q == 0) stage_acquire<1>();
       float v[CH];
-      finish_cols<BN, NPLANES, CH, LORA>(p, m, n0 + col, row_ok, rh[cur], rl[cur], v, true, lt, col);
+      finish_cols<BN, NPLANES, CH, LORA>(p, ev, m, n0 + col, row_ok, rh[cur], rl[cur], v, true, lt, col,
+                                         add ? av[cur] : nullptr);
       if (resid) {
         float g[CH];
         if (p.gate) {
-          ldv<CH>(p.gate + p.gate_off + n0 + col, g);
+          ldg_any<CH>(ev.gate + col, g);
 #pragma unroll
           for (int j = 0; j < CH; ++j) v[j] *= g[j];
         }
@@ -385,7 +426,7 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap
         uint8_t* buf = stage + (chunk & 1) * STAGE_BUF;
         if (q == 0) stage_acquire<1>();
         float v[CH];
-        load_cols<BN, NPLANES, LORA, CH>(p, taddr, h0 + col, m, nh + col, row_ok, v, true, lt);
+        load_cols<BN, NPLANES, LORA, CH>(p, ev, taddr, h0 + col, m, nh + col, row_ok, v, true, lt);
         stage_piece(buf, lane, p.out_dtype, q, v);
         if (q == ppc - 1) {
           if (p.peer_count)
@@ -396,31 +437,33 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap
       }
       continue;
     }
+    const int tok = (qkv && row_ok) ? (m % p.rope_rows) : 0;
+    const float* cs = qkv ? p.rope + static_cast<size_t>(tok) * 64 : nullptr;
+    const float* sn = qkv ? p.rope + static_cast<size_t>(p.rope_rows) * 64 + static_cast<size_t>(tok) * 64 : nullptr;
     float ss = 0.f;
 #pragma unroll 1
     for (int c = 0; c < 128; c += CH) {
       float v[CH];
-      load_cols<BN, NPLANES, LORA, CH>(p, taddr, h0 + c, m, nh + c, row_ok, v, true, lt);
+      load_cols<BN, NPLANES, LORA, CH>(p, ev, taddr, h0 + c, m, nh + c, row_ok, v, true, lt);
 #pragma unroll
       for (int j = 0; j < CH; ++j) ss += v[j] * v[j];
     }
     const float rs = 1.0f / sqrtf(ss * (1.0f / 128.0f) + p.eps);
-    const float* w = is_k ? p.norm_k : p.norm_q;
+    // the head's norm weights: in shared memory with the tile's other column constants (global
+    // memory in the LoRA build)
+    const float* w = LORA ? (is_k ? p.norm_k : p.norm_q) : ev.gate + h0;
     if (qkv) {
       // pieces arrive in pairs (c, 64 + c): the two halves of the head fill buffers 0 and 1
-      const int tok = row_ok ? (m % p.rope_rows) : 0;
-      const float* cs = p.rope + static_cast<size_t>(tok) * 64;
-      const float* sn = p.rope + static_cast<size_t>(p.rope_rows) * 64 + static_cast<size_t>(tok) * 64;
 #pragma unroll 1
       for (int c = 0; c < 64; c += CH) {
         const int q = (c % chc) / CH;
         if (q == 0) stage_acquire<0>();
         float v1[CH], v2[CH];
-        load_cols<BN, NPLANES, LORA, CH>(p, taddr, h0 + c, m, nh + c, row_ok, v1, true, lt);
-        load_cols<BN, NPLANES, LORA, CH>(p, taddr, h0 + 64 + c, m, nh + 64 + c, row_ok, v2, true, lt);
+        load_cols<BN, NPLANES, LORA, CH>(p, ev, taddr, h0 + c, m, nh + c, row_ok, v1, true, lt);
+        load_cols<BN, NPLANES, LORA, CH>(p, ev, taddr, h0 + 64 + c, m, nh + 64 + c, row_ok, v2, true, lt);
         float a[CH], b[CH];
-        ldv<CH>(w + c, a);
-        ldv<CH>(w + 64 + c, b);
+        ldg_any<CH>(w + c, a);
+        ldg_any<CH>(w + 64 + c, b);
 #pragma unroll
         for (int j = 0; j < CH; ++j) {
           v1[j] *= rs * a[j];
@@ -454,9 +497,9 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const CUtensorMap
         uint8_t* buf = stage + (chunk & 1) * STAGE_BUF;
         if (q == 0) stage_acquire<1>();
         float v[CH];
-        load_cols<BN, NPLANES, LORA, CH>(p, taddr, h0 + col, m, nh + col, row_ok, v, true, lt);
+        load_cols<BN, NPLANES, LORA, CH>(p, ev, taddr, h0 + col, m, nh + col, row_ok, v, true, lt);
         float wv[CH];
-        ldv<CH>(w + col, wv);
+        ldg_any<CH>(w + col, wv);
 #pragma unroll
         for (int j = 0; j < CH; ++j) v[j] = v[j] * rs * wv[j];
         stage_piece(buf, lane, p.out_dtype, q, v);
@@ -501,7 +544,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* staging = smem + C::STAGES * C::STAGE_BYTES;  // 1024-aligned (stage sizes are)
   __half* lora_smem = reinterpret_cast<__half*>(staging + C::STAGING_BYTES);
-  uint64_t* full = reinterpret_cast<uint64_t*>(staging + C::STAGING_BYTES + C::LORA_BYTES);
+  float* epi_vec = reinterpret_cast<float*>(staging + C::STAGING_BYTES + C::LORA_BYTES);  // [2][3][BN]
+  uint64_t* full = reinterpret_cast<uint64_t*>(staging + C::STAGING_BYTES + C::LORA_BYTES + C::VEC_BYTES);
   uint64_t* empty = full + C::STAGES;
   uint64_t* acc_full = empty + C::STAGES;
   uint64_t* acc_empty = acc_full + 2;
@@ -635,16 +679,52 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int g = warp >> 2;
     const int row = quad * 32 + lane;
     int t = g;
+    float* vec = epi_vec + g * 3 * BN;
     for (int tile = blockIdx.x + g * gridDim.x; tile < p.num_tiles;
          tile += C::ACC_BUFS * gridDim.x, t += C::ACC_BUFS) {
       const int buf = g;
       const uint32_t acc_phase = (t / C::ACC_BUFS) & 1;
-      bool ok = warp_wait(&acc_full[buf], acc_phase, abort_flag, kErrTimeoutAcc);
-      if constexpr (LORA) ok = wg_sync_and(g, ok);  // also: the previous tile's LoRA slice is read
-      if (!ok) break;
-      tc_fence_after();
       int mb, nb;
       tile_coords(p, tile, mb, nb);
+      // The tile's constants, loaded while its MMAs run (a piece of the epilogue would otherwise
+      // wait for them): this row's activation scale, and into shared memory, once per warpgroup
+      // (after all four warps are done with the previous tile's), the columns' weight scale, bias
+      // and gate.
+      EpiVec ev;
+      ev.as = (mb * BM + row < p.M) ? __ldg(p.a_scale + mb * BM + row) : 0.0f;
+      if constexpr (LORA) {
+        ev.ws = p.w_scale + nb * BN;
+        ev.bias = p.bias ? p.bias + nb * BN : nullptr;
+        ev.gate = p.gate ? p.gate + p.gate_off + nb * BN : nullptr;
+      } else {
+        wg_sync_and(g, true);
+        const int tid = threadIdx.x - g * 128;
+#pragma unroll
+        for (int i = tid; i < BN; i += 128) {
+          const int n = nb * BN + i;
+          vec[i] = __ldg(p.w_scale + n);
+          if (p.bias) vec[BN + i] = __ldg(p.bias + n);
+          if (p.out_mode == ANIMA_OUT_RESID) {
+            if (p.gate) vec[2 * BN + i] = __ldg(p.gate + p.gate_off + n);
+          } else if (p.out_mode != ANIMA_OUT_STORE) {
+            // the per-head norms: the third vector holds the norm weight of each column's head
+            const int nh = n & ~127;
+            const bool qkv = p.out_mode == ANIMA_OUT_QKV_NORM_ROPE;
+            const bool is_q = !qkv || nh < p.n_q;
+            const bool is_k = qkv && !is_q && nh < 2 * p.n_q;
+            vec[2 * BN + i] = (is_q || is_k) ? __ldg((is_k ? p.norm_k : p.norm_q) + (n & 127)) : 0.0f;
+          }
+        }
+        ev.ws = vec;
+        ev.bias = vec + BN;
+        ev.gate = vec + 2 * BN;
+      }
+      bool ok = warp_wait(&acc_full[buf], acc_phase, abort_flag, kErrTimeoutAcc);
+      // the same branch for the four warps after a failed wait; also publishes the vectors (and,
+      // in the LoRA build, orders the previous tile's reads of its LoRA slice before the next)
+      ok = wg_sync_and(g, ok);
+      if (!ok) break;
+      tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + buf * C::ACC_COLS;
       LoraTile lt;
       lt.bt_s = nullptr;
@@ -694,7 +774,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           lt.r = r;
         }
       }
-      epilogue_tile<BN, NPLANES, LORA>(p, &tm_out, &pm, staging + warp * 2 * STAGE_BUF, taddr, mb * BM + row,
+      epilogue_tile<BN, NPLANES, LORA>(p, ev, &tm_out, &pm, staging + warp * 2 * STAGE_BUF, taddr, mb * BM + row,
                                        mb * BM + quad * 32, nb * BN, lt);
       tc_fence_before();
       __syncwarp();

@@ -163,6 +163,7 @@ def attach_loras(registries, active):
                 W._lora_cat = None
                 W._lora_bt = None
                 W._lora_down = None
+                W._lora_down_slices = None
                 W._lora_up = None
 
 
@@ -277,14 +278,82 @@ def _up_linear(W):
     return lin
 
 
+# The down GEMM has few output tiles (ceil(M / 128) x n2 / 128: 32-64 at 1024^2) for the SMs. Where
+# its K range is long (MLP layer 2: 8192) it is cut into up to four slices of at least 2048 that run
+# as concurrent GEMMs on side streams; shorter slices would not pay for a launch's fixed cost
+# (~7 us) and the extra sum. Each slice's partial T is its exact int32 sums times the same scales;
+# the partials are added in a fixed order (deterministic), which changes T by fp32 rounding only.
+_SIDE_STREAMS: dict = {}
+_NUM_SMS: dict = {}
+
+
+def _side_streams(device, n: int) -> list:
+    ss = _SIDE_STREAMS.setdefault(device, [])
+    while len(ss) < n:
+        ss.append(torch.cuda.Stream(device))
+    return ss[:n]
+
+
+def _k_slices(M: int, down, device) -> int:
+    if device not in _NUM_SMS:
+        _NUM_SMS[device] = torch.cuda.get_device_properties(device).multi_processor_count
+    tiles = ((M + 127) // 128) * (down.N // 128)
+    S = 1
+    while S < 4 and tiles * 2 * S <= _NUM_SMS[device] and down.K % (2 * S * 128) == 0 and down.K // (2 * S) >= 2048:
+        S *= 2
+    return S
+
+
+def _down_slices(W, S: int) -> list:
+    """The down weight cut into S contiguous K slices (cached per attach)."""
+    from .weights import Linear
+
+    cache = getattr(W, "_lora_down_slices", None)
+    if cache is None or len(cache) != S:
+        down = _down_linear(W)
+        k = down.K // S
+        cache = [Linear("i8", down.N, k, down.data[:, i * k:(i + 1) * k].contiguous(), down.scale,
+                        name=f"{down.name}.k{i}") for i in range(S)]
+        W._lora_down_slices = cache
+    return cache
+
+
+def down_product(x, W) -> torch.Tensor:
+    """T = x_r A^T for all of W's entries: fp32 [M, n2], hi-plane products in columns [0, R) and
+    lo-plane products in [R, 2R) (see _down_linear)."""
+    from .ops import QuantRows, lincomb, linear
+
+    down = _down_linear(W)
+    M = x.rows
+    S = _k_slices(M, down, x.hi.device)
+    if S == 1:
+        return linear(x, down)
+    k = down.K // S
+    parts = _down_slices(W, S)
+    outs = [torch.empty(M, down.N, dtype=torch.float32, device=x.hi.device) for _ in range(S)]
+    cur = torch.cuda.current_stream(x.hi.device)
+    side = _side_streams(x.hi.device, S - 1)
+    for st in side:
+        st.wait_stream(cur)
+    for i in range(S):
+        xs = QuantRows(x.hi[:, i * k:(i + 1) * k], x.lo[:, i * k:(i + 1) * k] if x.lo is not None else None, x.scale)
+        if i == 0:
+            linear(xs, parts[0], out=outs[0])
+        else:
+            with torch.cuda.stream(side[i - 1]):
+                linear(xs, parts[i], out=outs[i])
+    for st in side:
+        cur.wait_stream(st)
+    return lincomb(outs[0], *[(1.0, o) for o in outs])
+
+
 def lora_delta_tc(x, W) -> torch.Tensor:
     """[M, N] fp32 low-rank update on the tensor cores: T = x_r A^T (hi and lo halves) by the int8
     GEMM, then T B2^T by the two-plane fp16 GEMM of anima_matmul (T to ~22 bits, scale * B in fp16:
     ~2^-11 of the update, as the fused epilogue)."""
-    from .ops import linear, matmul
+    from .ops import matmul
 
-    T = linear(x, _down_linear(W))
-    return matmul(T, _up_linear(W))
+    return matmul(down_product(x, W), _up_linear(W))
 
 
 def lora_epilogue(x, W, opts) -> list:
@@ -292,14 +361,12 @@ def lora_epilogue(x, W, opts) -> list:
     (one int8 tensor-core GEMM, `_down_linear`), then the GEMM adds T B^T per entry before its
     activation. Returns the tensors that must stay alive until the GEMM is enqueued, or None when
     W's entries do not fit the fused form."""
-    from .ops import linear
-
     if not _fusable(W) or W.K % 128:
         return None
     A = _cat_A(W)
     R = A.shape[0]
     down = _down_linear(W)
-    T = linear(x, down)                      # [M, 2R (+ padding)]: hi and lo partial products
+    T = down_product(x, W)                   # [M, 2R (+ padding)]: hi and lo partial products
     bt = _cat_Bt(W)
     opts.lora_t, opts.ld_t, opts.lora_t_lo = T.data_ptr(), down.N, R
     opts.lora_bt, opts.ld_bt = bt.data_ptr(), W.N

@@ -323,6 +323,21 @@ def _lora_ref(qa, entries, N):
     return d
 
 
+def test_lora_down_product_k_slices(ops):
+    """A long-K down-projection (MLP layer 2, K = 8192) runs as K slices on side streams whose fp32
+    partials are summed in a fixed order: the same T as one GEMM, to fp32 rounding."""
+    lora = pkg("lora")
+    M, N, K = 300, 2048, 8192
+    lin, _, _ = make_linear(N, K, 8)
+    lin.lora = [{k: v for k, v in e.items() if not k.endswith("_np")}
+                for e in _lora_entries(K, [(0, 2048, 32, 1.0)], 51)]
+    qa = ops.rotate_quant(randn((M, K), 52).to(DEV))
+    assert lora._k_slices(M, lora._down_linear(lin), qa.hi.device) == 4
+    T = lora.down_product(qa, lin).cpu().numpy()
+    T1 = ops.linear(qa, lora._down_linear(lin)).cpu().numpy()
+    assert rel_l2(T, T1) < 1e-6
+
+
 # fused (ranks multiple of 4, 16-aligned ranges) and the [M, N] delta fallback (rank 6)
 @pytest.mark.parametrize("spec,mode", [([(0, 2048, 32, 1.0), (2048, 2048, 32, 0.5), (4096, 2048, 16, 2.0)], "store"),
                                        ([(128, 1024, 8, 1.5)], "resid"),
