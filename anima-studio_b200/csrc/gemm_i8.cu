@@ -354,6 +354,62 @@ __device__ __forceinline__ void stage_acquire() {
   __syncwarp();
 }
 
+// The store / residual epilogue of NCOL columns [cb, cb + NCOL) of a tile for this warp's 32 rows.
+// t: this warp's running tile count; the two staging buffers alternate over the warp's chunks in
+// order, across tiles too, so a buffer is rewritten only after the store before the last has read it.
+template <int BN, int NPLANES, bool LORA, int NCOL>
+__device__ __forceinline__ void store_cols(const Params& p, const EpiVec& ev, const CUtensorMap* tm_out, uint8_t* stage,
+                                           uint32_t taddr, int m, int y0, int n0, const LoraTile& lt, int cb, int t) {
+  const bool row_ok = m < p.M;
+  const int lane = threadIdx.x & 31;
+  const int esz = p.out_dtype == ANIMA_F32 ? 4 : 2;
+  const int chc = 128 / esz;      // columns per staging chunk
+  const int ppc = chc / 16;       // 16-column pieces per chunk
+  constexpr int CH = 16;
+  static_assert(NCOL % 64 == 0, "whole staging chunks");
+  // software pipeline over 16-column pieces: the TMEM loads (and this row's ADD values) of piece
+  // c+1 are in flight while piece c is finished and staged
+  const bool resid = p.out_mode == ANIMA_OUT_RESID;
+  const bool add = !LORA && p.add && row_ok;  // (the LoRA build has no registers to spare for it)
+  const float* arow = add ? p.add + static_cast<size_t>(m) * p.ld_add + n0 : nullptr;
+  constexpr int PIPE = 2;
+  uint32_t rh[PIPE][CH], rl[PIPE][CH];
+  float av[PIPE][CH];
+  issue_cols<BN, NPLANES, CH>(taddr, cb, rh[0], rl[0]);
+  if (add) ldv<CH>(arow + cb, av[0]);
+  tmem_ld_wait(rh[0]);
+  if constexpr (NPLANES == 2) tmem_ld_wait(rl[0]);
+#pragma unroll
+  for (int c = 0; c < NCOL / CH; ++c) {
+    const int cur = PIPE == 2 ? (c & 1) : 0;
+    if (PIPE == 2 && c + 1 < NCOL / CH) {
+      issue_cols<BN, NPLANES, CH>(taddr, cb + CH * (c + 1), rh[(cur + 1) % PIPE], rl[(cur + 1) % PIPE]);
+      if (add) ldv<CH>(arow + cb + CH * (c + 1), av[(cur + 1) % PIPE]);
+    }
+    const int col = cb + CH * c;
+    const int chunk = col / chc, q = (col % chc) / CH;
+    uint8_t* buf = stage + ((t * (NCOL / chc) + (col - cb) / chc) & 1) * STAGE_BUF;
+    if (q == 0) stage_acquire<1>();
+    float v[CH];
+    finish_cols<BN, NPLANES, CH, LORA>(p, ev, m, n0 + col, row_ok, rh[cur], rl[cur], v, true, lt, col,
+                                       add ? av[cur] : nullptr);
+    if (resid) {
+      float g[CH];
+      if (p.gate) {
+        ldg_any<CH>(ev.gate + col, g);
+#pragma unroll
+        for (int j = 0; j < CH; ++j) v[j] *= g[j];
+      }
+    }
+    stage_piece(buf, lane, p.out_dtype, q, v);
+    if (q == ppc - 1) stage_flush(tm_out, buf, n0 + chunk * chc, y0, resid);
+    if (PIPE == 2 && c + 1 < NCOL / CH) {
+      tmem_ld_wait(rh[(cur + 1) % PIPE]);
+      if constexpr (NPLANES == 2) tmem_ld_wait(rl[(cur + 1) % PIPE]);
+    }
+  }
+}
+
 // One tile's epilogue for this warp's 32 rows (m = row of this lane) over BN columns from n0.
 // stage: this warp's two staging buffers; y0: first row of the warp's quadrant.
 template <int BN, int NPLANES, bool LORA>
@@ -367,47 +423,7 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const EpiVec& ev,
   const int ppc = chc / 16;       // 16-column pieces per chunk
   constexpr int CH = 16;
   if (p.out_mode == ANIMA_OUT_STORE || p.out_mode == ANIMA_OUT_RESID) {
-    // software pipeline over 16-column pieces: the TMEM loads (and this row's ADD values) of piece
-    // c+1 are in flight while piece c is finished and staged
-    const bool resid = p.out_mode == ANIMA_OUT_RESID;
-    const bool add = !LORA && p.add && row_ok;  // (the LoRA build has no registers to spare for it)
-    const float* arow = add ? p.add + static_cast<size_t>(m) * p.ld_add + n0 : nullptr;
-    constexpr int PIPE = 2;
-    uint32_t rh[PIPE][CH], rl[PIPE][CH];
-    float av[PIPE][CH];
-    issue_cols<BN, NPLANES, CH>(taddr, 0, rh[0], rl[0]);
-    if (add) ldv<CH>(arow, av[0]);
-    tmem_ld_wait(rh[0]);
-    if constexpr (NPLANES == 2) tmem_ld_wait(rl[0]);
-#pragma unroll
-    for (int c = 0; c < BN / CH; ++c) {
-      const int cur = PIPE == 2 ? (c & 1) : 0;
-      if (PIPE == 2 && c + 1 < BN / CH) {
-        issue_cols<BN, NPLANES, CH>(taddr, CH * (c + 1), rh[(cur + 1) % PIPE], rl[(cur + 1) % PIPE]);
-        if (add) ldv<CH>(arow + CH * (c + 1), av[(cur + 1) % PIPE]);
-      }
-      const int col = CH * c;
-      const int chunk = col / chc, q = (col % chc) / CH;
-      uint8_t* buf = stage + (chunk & 1) * STAGE_BUF;
-      if (q == 0) stage_acquire<1>();
-      float v[CH];
-      finish_cols<BN, NPLANES, CH, LORA>(p, ev, m, n0 + col, row_ok, rh[cur], rl[cur], v, true, lt, col,
-                                         add ? av[cur] : nullptr);
-      if (resid) {
-        float g[CH];
-        if (p.gate) {
-          ldg_any<CH>(ev.gate + col, g);
-#pragma unroll
-          for (int j = 0; j < CH; ++j) v[j] *= g[j];
-        }
-      }
-      stage_piece(buf, lane, p.out_dtype, q, v);
-      if (q == ppc - 1) stage_flush(tm_out, buf, n0 + chunk * chc, y0, resid);
-      if (PIPE == 2 && c + 1 < BN / CH) {
-        tmem_ld_wait(rh[(cur + 1) % PIPE]);
-        if constexpr (NPLANES == 2) tmem_ld_wait(rl[(cur + 1) % PIPE]);
-      }
-    }
+    store_cols<BN, NPLANES, LORA, BN>(p, ev, tm_out, stage, taddr, m, y0, n0, lt, 0, 0);
     return;
   }
   // Per-head RMSNorm (+ split-half RoPE for q/k heads of a fused qkv projection): a head is 128
@@ -555,6 +571,11 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  // Store and residual epilogues split every tile's columns between the two epilogue warpgroups
+  // (each takes BN / 2 columns of every tile): a tile's epilogue is latency-bound per warp, so this
+  // halves it, and with it the last tile's epilogue that no MMA overlaps. The per-head norms need
+  // a head's 128 columns in one thread and keep one warpgroup per tile, alternating.
+  const bool split = !LORA && C::ACC_BUFS == 2 && (p.out_mode == ANIMA_OUT_STORE || p.out_mode == ANIMA_OUT_RESID);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -563,7 +584,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], NPLANES);
-      mbar_init(&acc_empty[b], 4);  // one arrival per epilogue warp
+      mbar_init(&acc_empty[b], split ? 8 : 4);  // one arrival per epilogue warp that reads it
     }
     mbar_init(&drain[0], 1);
     mbar_init(&drain[1], 1);
@@ -674,15 +695,16 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
     }
   } else if (warp < 4 * C::ACC_BUFS) {
-    // epilogue warpgroup g = warp / 4 handles the CTA's local tiles t with t % ACC_BUFS == g
+    // epilogue warpgroup g = warp / 4
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
     const int g = warp >> 2;
     const int row = quad * 32 + lane;
-    int t = g;
+    // the CTA's local tiles t this warpgroup serves: all of them (split), else t % ACC_BUFS == g
+    const int step = split ? 1 : C::ACC_BUFS;
+    int t = split ? 0 : g;
     float* vec = epi_vec + g * 3 * BN;
-    for (int tile = blockIdx.x + g * gridDim.x; tile < p.num_tiles;
-         tile += C::ACC_BUFS * gridDim.x, t += C::ACC_BUFS) {
-      const int buf = g;
+    for (int tile = blockIdx.x + t * gridDim.x; tile < p.num_tiles; tile += step * gridDim.x, t += step) {
+      const int buf = t % C::ACC_BUFS;
       const uint32_t acc_phase = (t / C::ACC_BUFS) & 1;
       int mb, nb;
       tile_coords(p, tile, mb, nb);
@@ -774,8 +796,12 @@ __global__ void __launch_bounds__(THREADS, 1)
           lt.r = r;
         }
       }
-      epilogue_tile<BN, NPLANES, LORA>(p, ev, &tm_out, &pm, staging + warp * 2 * STAGE_BUF, taddr, mb * BM + row,
-                                       mb * BM + quad * 32, nb * BN, lt);
+      if (split)
+        store_cols<BN, NPLANES, LORA, BN / 2>(p, ev, &tm_out, staging + warp * 2 * STAGE_BUF, taddr, mb * BM + row,
+                                              mb * BM + quad * 32, nb * BN, lt, g * (BN / 2), t);
+      else
+        epilogue_tile<BN, NPLANES, LORA>(p, ev, &tm_out, &pm, staging + warp * 2 * STAGE_BUF, taddr, mb * BM + row,
+                                         mb * BM + quad * 32, nb * BN, lt);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
