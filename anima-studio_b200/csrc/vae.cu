@@ -20,9 +20,11 @@ namespace vae {
 // tap-shifted pixel origin, so the zero padding of the border and the channels past cin come from
 // the TMA's out-of-bounds fill (a chunk's weights past its tap multiply zeros); the B tile is the
 // weights' [BN rows x 64] box at K offset tap * cin + chunk * 64 (rows past cout are zeros too).
-// Persistent CTAs, 192 threads: warps 0-3 epilogue (thread = pixel row of the accumulator), warp 4
-// TMA producer, warp 5 TMEM allocator and single-thread MMA issuer; three pipeline stages and two
-// accumulator buffers in tensor memory, so a tile's epilogue overlaps the next tile's MMAs.
+// Persistent CTAs, 320 threads: warps 0-3 and 6-9 two epilogue warpgroups (thread = pixel row of the
+// accumulator; with BN >= 128 each takes half of every tile's channels, which halves the
+// latency-bound epilogue of short-K GEMMs), warp 4 TMA producer, warp 5 TMEM allocator and
+// single-thread MMA issuer; three pipeline stages and two accumulator buffers in tensor memory, so
+// a tile's epilogue overlaps the next tile's MMAs.
 namespace tc {
 
 constexpr int BM = 128;
@@ -31,7 +33,7 @@ constexpr int A_BYTES = BM * CK * 2;        // one plane's tile
 constexpr int MAX_BN = 256;
 constexpr int STAGES = 3;
 constexpr int STAGE_BYTES = 2 * A_BYTES + MAX_BN * CK * 2;
-constexpr int THREADS = 192;
+constexpr int THREADS = 320;
 constexpr int SMEM = STAGES * STAGE_BYTES + 256 + 1024;
 
 struct Params {
@@ -64,7 +66,7 @@ __global__ void __launch_bounds__(THREADS, 1) conv_tc_kernel(const __grid_consta
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 4);  // one arrival per epilogue warp
+      mbar_init(&acc_empty[b], 8);  // one arrival per epilogue warp
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -169,9 +171,15 @@ __global__ void __launch_bounds__(THREADS, 1) conv_tc_kernel(const __grid_consta
         }
       }
     }
-  } else {  // epilogue: warp w reads TMEM lanes 32 w .. 32 w + 31 (pixel rows of the tile)
-    const int row = warp * 32 + lane;
+  } else {  // epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31 (pixel rows of the tile)
+    const int quad = warp & 3;
+    const int g = warp >= 6 ? 1 : 0;
+    const int row = quad * 32 + lane;
     const bool vec = (p.cout & 3) == 0;
+    // this warpgroup's channels of a tile: halves when BN >= 128 (multiples of 32 columns)
+    const bool halves = p.BN >= 128;
+    const int cb = halves ? g * (p.BN / 2) : 0;
+    const int ce = halves ? cb + p.BN / 2 : (g == 0 ? p.BN : 0);
     int i = 0;
     for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++i) {
       const int buf = i & 1;
@@ -183,19 +191,26 @@ __global__ void __launch_bounds__(THREADS, 1) conv_tc_kernel(const __grid_consta
       const bool in = x < p.W && y < p.H;
       const int n0 = nt * p.BN;
       float* o = p.out + (static_cast<long long>(in ? y : 0) * p.W + (in ? x : 0)) * p.cout;
-      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(warp * 32) << 16) + buf * MAX_BN;
-      for (int c0 = 0; c0 < p.BN; c0 += 32) {
-        uint32_t r[32];
-        tmem_ld32(taddr + c0, r);
-        tmem_ld_wait(r);
-        if (!in) continue;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + buf * MAX_BN;
+      // 32 columns at a time, the next group's TMEM load in flight while this one is stored
+      auto store32 = [&](const uint32_t (&r)[32], int c0) {
+        if (!in) return;
 #pragma unroll
         for (int j = 0; j < 32; j += 4) {
           const int n = n0 + c0 + j;
           if (n >= p.cout) break;
           float v[4];
+          if (vec && p.bias) {
+            const float4 b4 = __ldg(reinterpret_cast<const float4*>(p.bias + n));
+            v[0] = __uint_as_float(r[j]) + b4.x;
+            v[1] = __uint_as_float(r[j + 1]) + b4.y;
+            v[2] = __uint_as_float(r[j + 2]) + b4.z;
+            v[3] = __uint_as_float(r[j + 3]) + b4.w;
+          } else {
 #pragma unroll
-          for (int q = 0; q < 4; ++q) v[q] = __uint_as_float(r[j + q]) + (p.bias && n + q < p.cout ? p.bias[n + q] : 0.f);
+            for (int q = 0; q < 4; ++q)
+              v[q] = __uint_as_float(r[j + q]) + (p.bias && n + q < p.cout ? p.bias[n + q] : 0.f);
+          }
           if (vec) {
             float4* d4 = reinterpret_cast<float4*>(o + n);
             float4 cur = p.accumulate ? *d4 : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -206,6 +221,21 @@ __global__ void __launch_bounds__(THREADS, 1) conv_tc_kernel(const __grid_consta
               if (n + q < p.cout) o[n + q] = (p.accumulate ? o[n + q] : 0.f) + v[q];
           }
         }
+      };
+      uint32_t r0[32], r1[32];
+      if (cb < ce) {
+        tmem_ld32(taddr + cb, r0);
+        tmem_ld_wait(r0);
+      }
+      for (int c0 = cb; c0 < ce; c0 += 64) {  // r0 holds columns c0 .. c0 + 31
+        const bool more1 = c0 + 32 < ce, more2 = c0 + 64 < ce;
+        if (more1) tmem_ld32(taddr + c0 + 32, r1);
+        store32(r0, c0);
+        if (!more1) break;
+        tmem_ld_wait(r1);
+        if (more2) tmem_ld32(taddr + c0 + 64, r0);
+        store32(r1, c0 + 32);
+        if (more2) tmem_ld_wait(r0);
       }
       tc_fence_before();
       __syncwarp();
