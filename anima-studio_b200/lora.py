@@ -165,6 +165,13 @@ def attach_loras(registries, active):
                 W._lora_down = None
                 W._lora_down_slices = None
                 W._lora_up = None
+    # the side streams of the K-sliced down-projection, created here (outside any CUDA graph
+    # capture) rather than on their first use, which may be inside one
+    for lora, strength in active:
+        for m in lora.modules if strength else []:
+            if m.A.is_cuda:
+                _side_streams(m.A.device, 3)
+                break
 
 
 def _cat_A(W):
