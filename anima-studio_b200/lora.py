@@ -301,14 +301,20 @@ def _side_streams(device, n: int) -> list:
     return ss[:n]
 
 
+def k_slice_count(M: int, n_down: int, K: int, num_sms: int) -> int:
+    """How many K slices the down GEMM ([M, K] x [n_down, K]^T) runs as: doubled while the slices'
+    tiles still fit the SMs at once and each slice keeps at least 2048 of K (in 128-wide blocks)."""
+    tiles = ((M + 127) // 128) * (n_down // 128)
+    S = 1
+    while S < 4 and tiles * 2 * S <= num_sms and K % (2 * S * 128) == 0 and K // (2 * S) >= 2048:
+        S *= 2
+    return S
+
+
 def _k_slices(M: int, down, device) -> int:
     if device not in _NUM_SMS:
         _NUM_SMS[device] = torch.cuda.get_device_properties(device).multi_processor_count
-    tiles = ((M + 127) // 128) * (down.N // 128)
-    S = 1
-    while S < 4 and tiles * 2 * S <= _NUM_SMS[device] and down.K % (2 * S * 128) == 0 and down.K // (2 * S) >= 2048:
-        S *= 2
-    return S
+    return k_slice_count(M, down.N, down.K, _NUM_SMS[device])
 
 
 def _down_slices(W, S: int) -> list:

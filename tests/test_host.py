@@ -119,6 +119,19 @@ def test_lora_key_matching():
     assert W.lora[0]["off"] == 2048 and W.lora[0]["n"] == 2048
 
 
+def test_lora_down_k_slice_count():
+    """The down-projection is cut along K only where K is long (MLP layer 2, 8192) and the slices'
+    tiles fit the SMs together; K = 2048 linears and large batches stay one GEMM."""
+    k = pkg("lora").k_slice_count
+    assert k(4096, 128, 8192, 148) == 4      # MLP layer 2, 1024^2: 32 tiles -> 128 in 4 slices of 2048
+    assert k(300, 128, 8192, 148) == 4
+    assert k(4096, 256, 8192, 148) == 2      # 64 tiles: two slices fill 128 SMs
+    assert k(4096, 128, 2048, 148) == 1      # K = 2048: slices would not pay for a launch
+    assert k(4096, 256, 2048, 148) == 1
+    assert k(8192, 256, 8192, 148) == 1      # CFG batch: 128 tiles already
+    assert k(4096, 128, 4096, 148) == 2
+
+
 def test_synthetic_checkpoint_is_deterministic():
     syn = pkg("synthetic")
     a = syn.block_tensors(3, 1, "mixed", 28, direct=True)
