@@ -42,6 +42,38 @@ def test_library_has_no_multicast_loads():
                 assert qualifier not in line, f"{f}: {line.strip()}"
 
 
+def test_ctypes_structs_match_the_c_header(tmp_path):
+    """The ctypes mirrors of the C-ABI structs (device.py) have the header's field names, offsets
+    and sizes, as a C compiler lays them out (gcc on include/anima_b200.h)."""
+    import ctypes as C
+    import shutil
+    import subprocess
+
+    dev = pkg("device")
+    structs = {"anima_qact": dev.QAct, "anima_weight": dev.Weight, "anima_linear_opts": dev.LinearOpts,
+               "anima_peer_group": dev.PeerGroup, "anima_attention_args": dev.AttentionArgs}
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    lines = ["#include <stdio.h>", "#include <stddef.h>", '#include "anima_b200.h"', "int main(void) {"]
+    for cname, cls in structs.items():
+        lines.append(f'  printf("{cname} sizeof %zu\\n", sizeof({cname}));')
+        for fname, *_ in cls._fields_:
+            lines.append(f'  printf("{cname} {fname} %zu\\n", offsetof({cname}, {fname}));')
+    lines += ["  return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "layout"
+    inc = os.path.join(ROOT, "include")
+    subprocess.run([cc, "-std=c11", "-I", inc, str(src), "-o", str(exe)], check=True, capture_output=True)
+    out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split("\n")
+    got = {(a, b): int(c) for a, b, c in (ln.split() for ln in out if ln)}
+    for cname, cls in structs.items():
+        assert got[(cname, "sizeof")] == C.sizeof(cls), cname
+        for fname, *_ in cls._fields_:
+            assert got[(cname, fname)] == getattr(cls, fname).offset, (cname, fname)
+
+
 def test_int8_quantizer_bit_exact():
     g = load("quant_int8.npz")
     q = pkg("quant").quantize_int8_convrot(torch.from_numpy(g["w"]))
