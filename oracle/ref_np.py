@@ -12,6 +12,8 @@ from __future__ import annotations
 
 import json
 import math
+import os
+from concurrent.futures import ThreadPoolExecutor
 
 import numpy as np
 
@@ -34,6 +36,32 @@ FIXED_LUT = np.array([
 ], dtype=np.float32)
 
 f32 = np.float32
+
+# Row-wise elementwise work (the softmax of a score matrix, the GELU of the MLP hidden) runs over
+# row chunks on a thread pool: numpy and scipy release the GIL inside these loops, and every row's
+# result is computed by the same operations whatever the chunking, so the values do not depend on
+# the thread count. Threads only: no process is forked.
+_POOL = None
+
+
+def _threads() -> int:
+    try:
+        return max(1, len(os.sched_getaffinity(0)))
+    except AttributeError:  # pragma: no cover - not Linux
+        return max(1, os.cpu_count() or 1)
+
+
+def _by_rows(fn, n_rows: int, min_rows: int = 64) -> None:
+    """fn(r0, r1) for row chunks [r0, r1) covering [0, n_rows), on the pool when it pays."""
+    global _POOL
+    nt = _threads()
+    if nt == 1 or n_rows < 2 * min_rows:
+        fn(0, n_rows)
+        return
+    if _POOL is None:
+        _POOL = ThreadPoolExecutor(max_workers=nt)
+    step = max(min_rows, -(-n_rows // nt))
+    list(_POOL.map(lambda r0: fn(r0, min(n_rows, r0 + step)), range(0, n_rows, step)))
 
 
 # ----------------------------------------------------------------------------- weight formats
@@ -145,9 +173,20 @@ def rotate_half(x):
 
 
 def gelu(x):
-    """Exact erf GELU, as F.gelu (tools/reference.py:242)."""
-    x64 = x.astype(np.float64)
-    return (0.5 * x64 * (1.0 + _erf(x64 / math.sqrt(2.0)))).astype(f32)
+    """Exact erf GELU, as F.gelu (tools/reference.py:242), evaluated in float64."""
+    x = np.asarray(x)
+    if x.ndim == 0:
+        x64 = np.float64(x)
+        return f32(0.5 * x64 * (1.0 + _erf(x64 / math.sqrt(2.0))))
+    x2 = x.reshape(-1, x.shape[-1]) if x.ndim > 1 else x.reshape(1, -1)
+    out = np.empty(x2.shape, dtype=f32)
+
+    def rows(r0, r1):
+        x64 = x2[r0:r1].astype(np.float64)
+        out[r0:r1] = 0.5 * x64 * (1.0 + _erf(x64 / math.sqrt(2.0)))
+
+    _by_rows(rows, x2.shape[0])
+    return out.reshape(x.shape)
 
 
 def silu(x):
@@ -167,12 +206,17 @@ def attention(q, k, v, key_len=None):
     scale = f32(1.0 / math.sqrt(D))
     for h in range(H):  # fp32 with max subtraction, like the reference's fp32 SDPA on the CPU
         s = (q[h].astype(f32) @ k[h].astype(f32).T) * scale
-        if key_len is not None:
-            s[:, key_len:] = -np.inf
-        s -= s.max(axis=-1, keepdims=True)
-        p = np.exp(s)
-        p /= p.sum(axis=-1, keepdims=True, dtype=f32)
-        out[h] = p @ v[h].astype(f32)
+
+        def softmax_rows(r0, r1, s=s):
+            b = s[r0:r1]
+            if key_len is not None:
+                b[:, key_len:] = -np.inf
+            b -= b.max(axis=-1, keepdims=True)
+            np.exp(b, out=b)
+            b /= b.sum(axis=-1, keepdims=True, dtype=f32)
+
+        _by_rows(softmax_rows, Lq)
+        out[h] = s @ v[h].astype(f32)
     return out
 
 
